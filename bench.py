@@ -1,0 +1,376 @@
+#!/usr/bin/env python
+"""Decode throughput of the Llama-3-8B-shaped model (BASELINE metric:
+"decode tok/s (Llama-8B shape, bs1) at 1/2/4/8 B200; GEMV % of HBM peak").
+
+A step is one decode step of the whole batch (32 layers + lm_head + greedy
+argmax) replayed from the captured CUDA graph.  Workload:
+random-init fp16 weights ~N(0, 0.02) (seeded), a 512-token uniform random
+prompt (prefilled untimed), then W warm-up and K timed decode steps at batch B,
+context 512+W .. 512+W+K.  Each step streams ~15 GB of weights, far more than
+the 126 MB L2, so no flush is needed.
+
+  value    device-resident greedy loop (b2_model_generate_greedy), CUDA events
+           on the model's stream, max over ranks
+  e2e      the public step API b2_model_decode_step: host token/position in
+           (H2D from pinned memory), fp32 logits [B, V] and next ids out (D2H),
+           every step
+  roofline the dominant kernel (gate/up GEMV with SwiGLU epilogue) timed on its
+           launch stream, algorithmic bytes / avg launch time vs measured HBM peak
+  cpu_baseline  the reference's own src/cpu forward (oracle/_ref) on the host
+
+N > 1 runs Megatron tensor parallelism over NCCL (one process per GPU under
+torchrun); `--impl reference` times the reference's CPU path instead.
+"""
+import argparse
+import datetime as dt
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import threading
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, os.path.join(ROOT, "serving-engine_b200"))
+sys.path.insert(0, os.path.join(ROOT, "oracle"))
+
+METRIC = "decode tok/s (Llama-8B shape, bs1) at 1/2/4/8 B200; GEMV % of HBM peak"
+LLAMA8B = dict(vocab=128256, hidden=4096, inter=14336, layers=32, nq=32, nkv=8, head_dim=128, eps=1e-5,
+               theta=500000.0)
+PROMPT = 512
+SEED_W, SEED_P = 1234, 42
+FALLBACK_HBM = 6650.0
+
+
+def log(*a):
+    print(*a, file=sys.stderr, flush=True)
+
+
+def measured_peak():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        with open(p) as f:
+            return float(json.load(f)["hbm_gbs"]), "measured (MEASURED_PEAKS.json hbm_gbs, copy burst)"
+    except Exception:
+        return FALLBACK_HBM, "fallback (6.65 TB/s, earlier measurement on this pool)"
+
+
+def ncu_traffic(kernel_tag):
+    """Per-launch DRAM bytes recorded from an ncu capture in profiles/ (or None)."""
+    d = os.path.join(ROOT, "profiles")
+    if not os.path.isdir(d):
+        return None
+    for fn in sorted(os.listdir(d)):
+        if not fn.endswith(".md"):
+            continue
+        try:
+            with open(os.path.join(d, fn)) as f:
+                for line in f:
+                    if line.startswith(f"traffic_bytes_per_launch[{kernel_tag}]:"):
+                        return float(line.split(":", 1)[1].strip())
+        except OSError:
+            pass
+    return None
+
+
+class ClockSampler:
+    """nvidia-smi clocks / throttle reasons sampled every 100 ms in the background."""
+
+    FIELDS = ("timestamp,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_id: str):
+        self.f = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
+        try:
+            self.p = subprocess.Popen(["nvidia-smi", "-i", gpu_id, f"--query-gpu={self.FIELDS}",
+                                       "--format=csv,noheader,nounits", "-lms", "100"], stdout=self.f,
+                                      stderr=subprocess.DEVNULL)
+        except Exception:
+            self.p = None
+        self.windows = []
+
+    def mark(self, t0, t1):
+        self.windows.append((t0, t1))
+
+    def stop(self):
+        if self.p:
+            self.p.terminate()
+            try:
+                self.p.wait(5)
+            except Exception:
+                self.p.kill()
+        self.f.flush()
+        self.f.seek(0)
+        rows = [r.split(", ") for r in self.f.read().strip().splitlines() if r.count(",") >= 8]
+        os.unlink(self.f.name)
+        samples = []
+        for r in rows:
+            try:
+                ts = dt.datetime.strptime(r[0].strip(), "%Y/%m/%d %H:%M:%S.%f").timestamp()
+                samples.append((ts, float(r[1]), float(r[2]), r[3], r[5:9]))
+            except Exception:
+                continue
+        inside = [s for s in samples if any(a - 0.15 <= s[0] <= b + 0.15 for a, b in self.windows)] or samples
+        if not inside:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no nvidia-smi samples"], "samples": 0}
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for s in inside for i, v in enumerate(s[4]) if v.strip() == "Active"})
+        return {"sm_mhz": statistics.median(s[1] for s in inside), "sm_max_mhz": max(s[2] for s in inside),
+                "reasons": reasons, "samples": len(inside)}
+
+
+# ---------------------------------------------------------------------------
+# CPU: the reference's src/cpu path
+# ---------------------------------------------------------------------------
+
+def _cpu_models():
+    """A 1-layer Llama-3-8B-width model on the reference's forward_cpu (tied
+    lm_head: the reference always ties it) and the reference's lm_head matmul
+    alone (the 0-layer part), or the oracle port when oracle/_ref is absent."""
+    import numpy as np
+    import oracle as O
+    cfg1 = O.Config(**{**LLAMA8B, "layers": 1}, tied=True)
+    W = O.seeded_weights(cfg1, SEED_W)
+    x = np.ones((1, cfg1.hidden), np.float32)
+    if O.ref_lib() is not None:
+        m1 = O.RefModel(cfg1, W)
+        run1 = lambda ids: m1.forward(ids)  # noqa: E731
+        run0 = lambda ids: O.matmul_transB(x, W["embed"], ref=True)  # noqa: E731
+        kind = "reference"
+    else:
+        O.set_threads(1)
+        run1 = lambda ids: O.forward(cfg1, W, ids, logit_row0=len(ids))  # noqa: E731
+        run0 = lambda ids: O.matmul_transB(x, W["embed"])  # noqa: E731
+        kind = "port"
+    return run1, run0, kind, np.array([7], np.int64), W
+
+
+CPU_SAMPLE = ("one decode step at Llama-3-8B widths through the reference forward_cpu on a 1-token sequence: "
+              "t1 = 1-layer forward (embedding, 1 decoder layer, final norm, 128256x4096 lm_head), "
+              "t0 = the reference lm_head matmul alone, step time = t0 + 32*(t1 - t0); the reference CPU path "
+              "has no KV cache and recomputes all c+1 positions at context c, so this is an upper bound on "
+              "its decode rate")
+
+
+def cpu_baseline_single():
+    run1, run0, kind, ids, keep = _cpu_models()
+    t1s, t0s = [], []
+    for _ in range(3):
+        a = time.perf_counter(); run1(ids); t1s.append(time.perf_counter() - a)
+        a = time.perf_counter(); run0(ids); t0s.append(time.perf_counter() - a)
+    t1, t0 = statistics.median(t1s), statistics.median(t0s)
+    step = t0 + LLAMA8B["layers"] * max(t1 - t0, 0.0)
+    return {"value": 1.0 / step, "unit": "tok/s", "cores": 1, "kind": kind, "sample": CPU_SAMPLE,
+            "step_s": step, "layer_s": t1 - t0, "head_s": t0}
+
+
+def run_reference(args, rank, world):
+    """--impl reference: the reference's CPU implementation on all host threads
+    (independent sequences, one per thread, sharing the read-only weights)."""
+    if rank != 0:
+        return
+    threads = os.cpu_count() or 1
+    run1, run0, kind, ids, keep = _cpu_models()
+
+    def parallel(fn):
+        ts = [threading.Thread(target=fn, args=(ids,)) for _ in range(threads)]
+        a = time.perf_counter()
+        for t in ts:
+            t.start()
+        for t in ts:
+            t.join()
+        return time.perf_counter() - a
+
+    t0 = statistics.median([parallel(run0) for _ in range(2)])  # head part, measured once
+    layer_times = []
+    for i in range(args.warmup + args.steps):
+        t1 = parallel(run1)
+        if i >= args.warmup:
+            layer_times.append(max(t1 - t0, 1e-9))
+    layer = statistics.median(layer_times)
+    step = t0 + LLAMA8B["layers"] * layer
+    value = threads / step
+    sample = (CPU_SAMPLE + f"; {threads} host threads each decode an independent sequence concurrently; "
+              f"each timed step runs the 1-layer sample on every thread")
+    out = {"impl": "reference", "metric": METRIC, "value": value, "unit": "tok/s", "n_gpus": world,
+           "steps": args.steps, "warmup": args.warmup, "ms_per_step": step * 1e3, "higher_is_better": True,
+           "scaling": "strong", "vs_baseline": None, "dtype": "f32",
+           "data": "synthetic: seeded random-init weights ~N(0,0.02) rounded to fp16, 1-token prompt",
+           "config": config_dict(args, world),
+           "cpu_baseline": {"value": value, "unit": "tok/s", "cores": threads, "kind": kind, "sample": sample},
+           "e2e": {"value": value, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(out), flush=True)
+
+
+def config_dict(args, world):
+    return {"workload": f"Llama-3-8B-shaped decode, batch {args.batch}, {args.prompt}-token prompt then "
+                        f"{args.warmup}+{args.steps} decode steps",
+            "model": f"llama3-8b-shape random-init (H4096 L{args.layers} 32/8 heads D128 FFN14336 V128256, "
+                     "theta 5e5)",
+            "global_batch": args.batch, "prompt_len": args.prompt,
+            "ctx_range": [args.prompt + args.warmup, args.prompt + args.warmup + args.steps],
+            "parallelism": f"tp{world}",
+            "l2": "inputs larger than L2: every step streams ~15 GB of weights (L2 126 MB)"}
+
+
+# ---------------------------------------------------------------------------
+# GPU arm
+# ---------------------------------------------------------------------------
+
+def run_b2(args, rank, world, local):
+    import numpy as np
+    import torch
+    import torch.distributed as dist
+
+    import b2engine as b2
+
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    nccl_id = None
+    if world > 1:
+        obj = [b2.nccl_unique_id() if rank == 0 else None]
+        dist.broadcast_object_list(obj, src=0)
+        nccl_id = obj[0]
+    B, K, W = args.batch, args.steps, args.warmup
+    max_seq = max(4096, args.prompt + 2 * (W + K) + 8)
+    c = dict(LLAMA8B, layers=args.layers)
+    m = b2.Model(c["vocab"], c["hidden"], c["inter"], c["layers"], c["nq"], c["nkv"], c["head_dim"], eps=c["eps"],
+                 theta=c["theta"], tied=False, max_batch=B, max_seq=max_seq, tp_rank=rank, tp_size=world,
+                 nccl_id=nccl_id)
+    m.init_random(SEED_W, 0.02)
+    prompt = np.random.default_rng(SEED_P).integers(0, c["vocab"], (B, args.prompt))
+    t = time.time()
+    m.prefill(prompt, want_logits=False)
+    log(f"[rank {rank}] prefill {args.prompt} tokens in {time.time() - t:.2f} s")
+    stream = torch.cuda.ExternalStream(m.stream, device=dev)
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    def max_over_ranks(x):
+        if world == 1:
+            return x
+        t = torch.tensor([x], dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    uuid = "GPU-" + str(torch.cuda.get_device_properties(dev).uuid)
+    clocks = ClockSampler(uuid)
+    time.sleep(0.3)
+
+    # warm-up: W device-resident steps
+    m.generate_greedy(W, fetch=False)
+    m.sync()
+    pos0 = args.prompt + W
+
+    # value: K device-resident steps, CUDA events on the model's stream
+    barrier()
+    torch.cuda.synchronize()
+    m.sync()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    w0 = time.time()
+    e0.record(stream)
+    m.generate_greedy(K, fetch=False)
+    e1.record(stream)
+    e1.synchronize()
+    w1 = time.time()
+    torch.cuda.synchronize()
+    barrier()
+    clocks.mark(w0, w1)
+    ms = max_over_ranks(e0.elapsed_time(e1))
+    next_tok = m.read("tokens", np.int64, B)
+
+    # per-kernel launch durations (dominant kernel for the roofline)
+    ctx_mid = pos0 + K // 2
+    ktimes = {k: m.time_kernel(k, B, reps=2) for k in b2.Model.KERNELS}
+    kbytes = {k: m.kernel_bytes(k, B, ctx_mid) for k in b2.Model.KERNELS}
+
+    # e2e: public step API with host buffers, same contexts as the timed loop
+    barrier()
+    torch.cuda.synchronize()
+    tok = next_tok.copy()
+    e2, e3 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    w2 = time.time()
+    e2.record(stream)
+    for i in range(K):
+        _, tok = m.decode_step(tok, [pos0 + i] * B, want_logits=True, want_next=True)
+    e3.record(stream)
+    e3.synchronize()
+    w3 = time.time()
+    barrier()
+    clocks.mark(w2, w3)
+    ms_e2e = max_over_ranks(e2.elapsed_time(e3))
+    ck = clocks.stop()
+
+    if rank == 0:
+        peak, peak_src = measured_peak()
+        dom = max(ktimes, key=lambda k: ktimes[k] * (c["layers"] if k != "lm_head" else 1))
+        dom = "gate_up" if "gate_up" in ktimes else dom
+        achieved = kbytes[dom] / (ktimes[dom] * 1e-3) / 1e9
+        step_ms = ms / K
+        step_bytes = m.step_bytes(B, ctx_mid)
+        step_gbs = step_bytes / (step_ms * 1e-3) / 1e9
+        launches = m.step_launches(B)
+        out = {
+            "metric": METRIC, "value": B * K / (ms * 1e-3), "unit": "tok/s", "n_gpus": world, "steps": K,
+            "warmup": W, "ms_per_step": step_ms, "higher_is_better": True, "scaling": "strong",
+            "vs_baseline": None, "dtype": "f16",
+            "data": "synthetic: seeded random-init fp16 weights ~N(0,0.02), uniform random prompt ids",
+            "config": config_dict(args, world),
+            "e2e": {"value": B * K / (ms_e2e * 1e-3), "unit": "tok/s", "h2d_bytes_per_step": 12 * B,
+                    "d2h_bytes_per_step": 4 * B * c["vocab"] + 8 * B, "ms_per_step": ms_e2e / K,
+                    "api": "b2_model_decode_step (host token + position in, fp32 logits + next id out)"},
+            "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
+                         "frac": achieved / peak, "traffic": ncu_traffic(dom), "kernel": f"gemv {dom}",
+                         "bytes_per_launch": kbytes[dom], "launch_ms": ktimes[dom], "peak_source": peak_src},
+            "step_roofline": {"bytes_per_step": step_bytes, "achieved": step_gbs, "peak": peak, "unit": "GB/s",
+                              "frac": step_gbs / peak},
+            "kernels_ms_per_launch": {k: round(v, 5) for k, v in ktimes.items()},
+            "gpu_launches": launches * K,
+            "clocks": ck,
+        }
+        if world == 1 and not args.no_cpu_baseline:
+            try:
+                out["cpu_baseline"] = cpu_baseline_single()
+            except Exception as ex:  # reported, never fatal
+                out["cpu_baseline"] = {"value": None, "error": str(ex)[:200]}
+        print(json.dumps(out), flush=True)
+    m.close()
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=256)
+    ap.add_argument("--warmup", type=int, default=8)
+    ap.add_argument("--batch", type=int, default=1)
+    ap.add_argument("--impl", default="b2", choices=["b2", "reference"])
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--prompt", type=int, default=PROMPT, help="prompt length (512 for the metric)")
+    ap.add_argument("--layers", type=int, default=LLAMA8B["layers"],
+                    help="decoder depth (reduced only for small profiler captures; the metric uses 32)")
+    args = ap.parse_args()
+    args.warmup = max(args.warmup, 3)
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if args.impl == "reference":
+        run_reference(args, rank, world)
+        return
+    if world > 1:
+        import torch.distributed as dist
+        dist.init_process_group("gloo", timeout=dt.timedelta(seconds=300))
+    try:
+        run_b2(args, rank, world, local)
+    finally:
+        if world > 1:
+            import torch.distributed as dist
+            dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,287 @@
+/*
+ * b2engine.h -- C-ABI boundary of the B200-native (sm_100a) per-token forward
+ * path.  Every entry point takes plain device pointers, sizes and a CUDA
+ * stream (as void*), never allocates or synchronises unless its comment says
+ * so, and returns a status: 0 on success, a cudaError_t value (> 0) when CUDA
+ * reported an error, or one of the negative B2_ERR_* codes below.
+ *
+ * Each entry point names the reference interface it replaces
+ * (XVX-016/serving-engine, paths relative to that project).  The reference's
+ * C++ signatures (namespace engine::cuda, void returns, exceptions on error)
+ * are kept as inline wrappers over this layer in
+ * serving-engine_b200/compat/src/... so that its callers build unchanged.
+ *
+ * Element types: "half" is IEEE fp16, "bf16" is bfloat16, "float" is fp32.
+ */
+#ifndef B2ENGINE_H
+#define B2ENGINE_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+enum {
+    B2_OK = 0,
+    B2_ERR_INVALID = -1,     /* bad argument (null pointer, non-positive size, ...) */
+    B2_ERR_UNSUPPORTED = -2, /* shape or alignment this build does not handle */
+    B2_ERR_WORKSPACE = -3,   /* caller-provided scratch too small */
+    B2_ERR_NCCL = -4,        /* NCCL call failed */
+    B2_ERR_STATE = -5,       /* object used in the wrong state */
+    B2_ERR_TIMEOUT = -6      /* a bounded device-side wait gave up */
+};
+
+/* Human-readable text for a status value (static storage). */
+const char* b2_status_string(int status);
+/* Build identification, e.g. "b2engine 0.1 sm_100a". */
+const char* b2_version(void);
+
+/* Strided view over a K or V cache: element (b, h, s, d) lives at
+ * data + b*stride_b + h*stride_h + s*stride_s + d*stride_d (elements of half).
+ * Replaces engine::cuda::KVView (src/cuda/kv_view.h:17-31). stride_d must be 1. */
+typedef struct b2_kv_view {
+    const void* data;
+    int64_t stride_b;
+    int64_t stride_h;
+    int64_t stride_s;
+    int64_t stride_d;
+} b2_kv_view;
+
+/* ---------------------------------------------------------------------------
+ * Operator API (one entry per engine::cuda function, src/cuda/kernels.h)
+ * ------------------------------------------------------------------------- */
+
+/* out[i,:] = table[ids[i],:]; ids int64 [seq_len], table/out half.
+ * Replaces engine::cuda::embedding_lookup (src/cuda/kernels.h:14-21). */
+int b2_embedding_lookup(const int64_t* token_ids, const void* table, void* out,
+                        int64_t seq_len, int64_t hidden_size, void* stream);
+
+/* out = x * rsqrt(mean(x^2) + eps) * weight, fp32 accumulation; half [rows,dim].
+ * Replaces engine::cuda::rmsnorm (src/cuda/kernels.h:26-34). */
+int b2_rmsnorm(const void* x, const void* weight, void* out, int64_t rows, int64_t dim,
+               float eps, void* stream);
+
+/* out[i,j] = x[i,j] + bias[j]; half. Replaces engine::cuda::bias_add (src/cuda/kernels.h:38-45). */
+int b2_bias_add(const void* x, const void* bias, void* out, int64_t M, int64_t N, void* stream);
+
+/* out = a + b; half. Replaces engine::cuda::residual_add (src/cuda/kernels.h:48-54). */
+int b2_residual_add(const void* a, const void* b, void* out, int64_t count, void* stream);
+
+/* Rotate-half RoPE in place on q [S,nq,D] and k [S,nkv,D] at positions
+ * start_pos + s.  Replaces engine::cuda::apply_rope (src/cuda/kernels.h:59-69). */
+int b2_apply_rope(void* q, void* k, int64_t seq_len, int64_t num_q_heads, int64_t num_kv_heads,
+                  int64_t head_dim, int64_t start_pos, float rope_theta, void* stream);
+
+/* Causal GQA attention, q/out [S,nq,D], k/v [S,nkv,D], half, scale 1/sqrt(D).
+ * Replaces engine::cuda::causal_gqa (src/cuda/kernels.h:77-87). */
+int b2_causal_gqa(const void* q, const void* k, const void* v, void* out, int64_t seq_len,
+                  int64_t num_q_heads, int64_t num_kv_heads, int64_t head_dim, void* stream);
+
+/* Row softmax over the last dimension, half in/out, fp32 math.
+ * Replaces engine::cuda::softmax (src/cuda/kernels.h:91-97). */
+int b2_softmax(const void* x, void* out, int64_t rows, int64_t cols, void* stream);
+
+/* Single-token attention over a head-major cache [nkv, max_seq, D] for one
+ * sequence of total_seq_len tokens. q/out [nq, D].
+ * Replaces engine::cuda::decode_gqa (src/cuda/kernels.h:104-115). */
+int b2_decode_gqa(const void* q, const void* k_cache, const void* v_cache, void* out,
+                  int total_seq_len, int num_q_heads, int num_kv_heads, int max_seq, int head_dim,
+                  void* stream);
+
+/* Split-KV GQA decode attention: one query token per sequence, q/out
+ * [B, nq, D] half, seq_lens int32 [B] on the device (read by the kernel, so
+ * the call is graph-capturable across steps), K/V through strided views.
+ * The positions of each (sequence, kv head) are cut into splits of at least
+ * 64 positions, as many as split_buffer holds (about
+ * split_buffer_floats / (B*nq*(D+2)); a few floats hold per-(sequence,
+ * kv head) counters).  Each split writes a partial output and its (max, sum)
+ * pair into split_buffer and the last split to finish merges them, in the
+ * same kernel.  split_buffer may be NULL (one split per (sequence, kv head),
+ * no scratch).  max_seq_len bounds seq_lens and sizes the split count.
+ * Replaces engine::cuda::decode_gqa_split (src/cuda/kernels.h:120-133,
+ * src/cuda/decode_attention_split.cu:183-214). */
+int b2_decode_gqa_split(const void* q, b2_kv_view k_view, b2_kv_view v_view, const int* seq_lens,
+                        void* out, int batch_size, int num_q_heads, int num_kv_heads, int head_dim,
+                        int max_seq_len, float* split_buffer, size_t split_buffer_floats,
+                        void* stream);
+
+/* Causal GQA prefill attention, q/out [B,S,nq,D], k/v [B,S,nkv,D], half.
+ * Replaces engine::cuda::flash_prefill_gqa (src/cuda/kernels.h:136-147). */
+int b2_flash_prefill_gqa(const void* q, const void* k, const void* v, void* out, int64_t seq_len,
+                         int num_q_heads, int num_kv_heads, int head_dim, int batch_size, void* stream);
+
+/* out = silu(gate) * up, half. Replaces engine::cuda::swiglu (src/cuda/kernels.h:151-157). */
+int b2_swiglu(const void* gate, const void* up, void* out, int64_t count, void* stream);
+
+/* C[M,N] = A[M,K] * B[N,K]^T, half in, fp32 accumulate, half out.
+ * Replaces engine::cuda::matmul_transB (src/cuda/kernels.h:164-172). */
+int b2_matmul_transB(const void* A, const void* B, void* C, int M, int K, int N, void* stream);
+
+/* As b2_matmul_transB with fp32 output.
+ * Replaces engine::cuda::matmul_transB_f32 (src/cuda/kernels.h:177-185). */
+int b2_matmul_transB_f32(const void* A, const void* B, float* C, int M, int K, int N, void* stream);
+
+/* y[n] = dot(W[n,:], x), W [N,K] half row-major, fp32 accumulate, half out.
+ * Replaces engine::cuda::gemv (src/cuda/kernels.h:189-196). */
+int b2_gemv(const void* W, const void* x, void* y, int N, int K, void* stream);
+
+/* y[n] = dot(W[n,:], x) + b[n]. Replaces engine::cuda::gemv_bias (src/cuda/kernels.h:199-207). */
+int b2_gemv_bias(const void* W, const void* x, const void* b, void* y, int N, int K, void* stream);
+
+/* y[n] = dot(W[n,:], x) + r[n]. Replaces engine::cuda::gemv_residual (src/cuda/kernels.h:211-219). */
+int b2_gemv_residual(const void* W, const void* x, const void* r, void* y, int N, int K, void* stream);
+
+/* Batched decode GEMV (new API; the reference GEMV is M=1 only):
+ * y[b,n] = dot(W[n,:], x[b,:]) (+ extra), x [B,K] half, y [B,N].
+ * epilogue: 0 none, 1 bias extra[n] (half), 2 residual extra[b,n] (half).
+ * out_f32 != 0 writes fp32 y instead of half (the lm_head form). */
+int b2_gemv_batched(const void* W, const void* x, const void* extra, void* y, int B, int N, int K,
+                    int epilogue, int out_f32, void* stream);
+
+/* Copy K/V rows [num_tokens, nkv, D] into head-major caches [nkv, max_seq, D]
+ * at positions start_pos..start_pos+num_tokens-1 (positions >= max_seq are
+ * skipped).  Replaces engine::cuda::append_kv_cache (src/runtime/kv_cache.h:80-91). */
+int b2_append_kv_cache(const void* src_k, const void* src_v, void* dst_k, void* dst_v,
+                       int num_tokens, int start_pos, int num_kv_heads, int max_seq, int head_dim,
+                       void* stream);
+
+/* ---------------------------------------------------------------------------
+ * Sampler  (replaces engine::SamplerGPU, src/runtime/sampler.h:10-65)
+ * ------------------------------------------------------------------------- */
+
+typedef struct b2_sampler_config {
+    float temperature;        /* <= 1e-6: greedy argmax */
+    int top_k;                /* <= 0 or > max_top_k: min(max_top_k, 64) */
+    float top_p;              /* >= 1: disabled */
+    float repetition_penalty; /* 1: disabled */
+    uint64_t seed;            /* reseed iff seed != 0 and seed != current state */
+} b2_sampler_config;
+
+typedef struct b2_sampler b2_sampler;
+
+/* Allocates the sampler's device workspace (this call allocates). */
+int b2_sampler_create(int vocab_size, int max_top_k, b2_sampler** out);
+int b2_sampler_destroy(b2_sampler* s);
+/* Penalty, argmax or top-k/top-p selection and the seeded draw run on the
+ * device; the chosen id is copied back (this call synchronises `stream`).
+ * d_logits: float [vocab] on the device, left unmodified.  history: host ids.
+ * Replaces SamplerGPU::sample (src/runtime/sampler.h:28-33, sampler.cu:202-340). */
+int b2_sampler_sample(b2_sampler* s, const float* d_logits, const int64_t* history, int history_len,
+                      const b2_sampler_config* cfg, void* stream, int* token_out);
+/* Current LCG state (for tests) and explicit set. */
+uint64_t b2_sampler_rng_state(const b2_sampler* s);
+int b2_sampler_set_rng_state(b2_sampler* s, uint64_t state);
+
+/* ---------------------------------------------------------------------------
+ * Model runtime  (replaces ModelWeightsGPU / ActivationBuffersGPU /
+ * prefill_gpu / decode_step_gpu, src/model/forward_gpu.h:15-113, and the
+ * KVCache layout of src/runtime/kv_cache.h:12-73)
+ * ------------------------------------------------------------------------- */
+
+typedef struct b2_model_config {
+    int vocab_size;
+    int hidden_size;
+    int intermediate_size;
+    int num_layers;
+    int num_q_heads;
+    int num_kv_heads;
+    int head_dim;
+    float rms_norm_eps;
+    float rope_theta;
+    int tie_word_embeddings; /* 1: lm_head is the embedding table */
+    int has_qkv_bias;        /* 1: q/k/v biases (Qwen2); 0: Llama */
+    int max_batch;           /* sequences decoded together */
+    int max_seq;             /* KV capacity per sequence */
+} b2_model_config;
+
+typedef struct b2_model b2_model;
+
+/* Creates a model shard on the current CUDA device (allocates all weights,
+ * the KV cache and activations).  tp_size > 1 shards heads / FFN rows /
+ * vocabulary Megatron-style across ranks; nccl_id is the 128-byte
+ * ncclUniqueId shared by all ranks (NULL when tp_size == 1). */
+int b2_model_create(const b2_model_config* cfg, int tp_rank, int tp_size, const void* nccl_id,
+                    b2_model** out);
+int b2_model_destroy(b2_model* m);
+
+/* Fills every weight from the seeded generator (identical global tensors at
+ * any tp_size; norm weights 1.0).  Synchronises. */
+int b2_model_init_random(b2_model* m, uint64_t seed, float stddev);
+
+/* Uploads one global tensor given in host fp16 [rows, cols] (the rank keeps
+ * its shard).  Names: "embed", "lm_head", "final_norm", and per layer l
+ * "l.ln1", "l.ln2", "l.wq", "l.wk", "l.wv", "l.bq", "l.bk", "l.bv", "l.wo",
+ * "l.wg", "l.wu", "l.wd".  Synchronises. */
+int b2_model_set_tensor(b2_model* m, const char* name, const uint16_t* host_f16, int64_t rows,
+                        int64_t cols);
+
+/* Clears the KV cache positions of all sequences (sets lengths to 0). */
+int b2_model_reset(b2_model* m);
+
+/* Processes `seq_len` prompt tokens of each of `batch` sequences
+ * (host ids [batch, seq_len]) starting at position 0, filling the KV cache.
+ * If host_logits != NULL the fp32 logits of the last position are copied to
+ * it ([batch, vocab]).  Synchronises. */
+int b2_model_prefill(b2_model* m, const int64_t* host_ids, int batch, int seq_len, float* host_logits);
+
+/* One decode step for `batch` sequences: host tokens [batch] at host
+ * positions [batch]; appends K/V and produces logits.  host_logits
+ * ([batch, vocab] fp32) and/or host_next (greedy ids [batch]) may be NULL.
+ * Synchronises.  The step runs as a captured CUDA graph after its first call. */
+int b2_model_decode_step(b2_model* m, const int64_t* host_tokens, const int* host_positions, int batch,
+                         float* host_logits, int64_t* host_next);
+
+/* Device-resident greedy generation: `steps` decode steps replayed back to
+ * back without host round trips, each consuming the argmax of the previous
+ * one.  It continues from the last prefill / decode step: the first step
+ * consumes that step's argmax.  host_tokens_out ([steps, batch]) receives the
+ * token each step consumed (so row 0 is the argmax of the last processed
+ * position); when it is NULL the call only enqueues the steps on the model's
+ * stream (see b2_model_sync), otherwise it synchronises. */
+int b2_model_generate_greedy(b2_model* m, int steps, int64_t* host_tokens_out);
+int b2_model_sync(b2_model* m);
+
+/* The model's CUDA stream (cudaStream_t). */
+void* b2_model_stream(b2_model* m);
+
+/* Device pointers for tests and tools: "logits" (float [max_batch, vocab]),
+ * "hidden" (float [max_batch, hidden]), "kv" (half, the whole cache),
+ * "tokens" (int64 [max_batch]), "positions" (int32 [max_batch]). */
+void* b2_model_buffer(b2_model* m, const char* name);
+
+/* Synchronous copy of `bytes` bytes at byte `offset` of a named buffer (see
+ * b2_model_buffer) into host memory. */
+int b2_model_read(b2_model* m, const char* name, void* host_dst, size_t offset, size_t bytes);
+
+/* Layout of the KV cache: [layer][batch][K=0,V=1][kv_head][max_seq][head_dim]
+ * half, kv heads of this rank only.  Writes the element strides. */
+int b2_model_kv_layout(const b2_model* m, int64_t* stride_layer, int64_t* stride_batch,
+                       int64_t* stride_kv, int64_t* stride_head, int64_t* stride_pos);
+
+/* Algorithmic HBM bytes of one decode step at `batch` sequences whose context
+ * (before the step) is `ctx` tokens, for this rank. */
+double b2_model_step_bytes(const b2_model* m, int batch, int ctx);
+
+/* Times one kernel of the decode step in isolation for roofline reporting:
+ * kind 0 qkv, 1 attention (+combine), 2 o-proj, 3 gate/up, 4 down, 5 lm_head.
+ * Launches it once per layer (different weights each launch, as in a step),
+ * `reps` times over all layers, back to back on the model's stream with the
+ * same launch attributes as the step, and writes the average milliseconds
+ * per launch.  Overwrites activation buffers (not the KV cache contents of
+ * earlier positions).  Synchronises. */
+int b2_model_time_kernel(b2_model* m, int kind, int batch, int reps, float* avg_ms);
+
+/* Algorithmic HBM bytes of one launch of `kind` (as above) at `batch`
+ * sequences with `ctx` context tokens. */
+double b2_model_kernel_bytes(const b2_model* m, int kind, int batch, int ctx);
+
+/* Number of kernel launches one decode step issues (for reporting). */
+int b2_model_step_launches(const b2_model* m, int batch);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* B2ENGINE_H */

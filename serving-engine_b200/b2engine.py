@@ -1,0 +1,313 @@
+"""ctypes binding of the b2engine C-ABI (include/b2engine.h).
+
+Python here is plumbing for tests and the benchmark: device memory comes from
+torch tensors, every computation is a call into lib/libb2engine.so.  There is
+no fallback: if the library is missing or a call fails, an exception is raised.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import os
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(HERE, "lib", "libb2engine.so")
+_LIB = None
+
+vp = C.c_void_p
+i32 = C.c_int
+i64 = C.c_int64
+f32 = C.c_float
+u64 = C.c_uint64
+
+
+class B2Error(RuntimeError):
+    def __init__(self, fn: str, status: int):
+        self.status = status
+        super().__init__(f"{fn} failed: status {status} ({status_string(status)})")
+
+
+class KVView(C.Structure):
+    _fields_ = [("data", vp), ("stride_b", i64), ("stride_h", i64), ("stride_s", i64), ("stride_d", i64)]
+
+
+class SamplerConfig(C.Structure):
+    _fields_ = [("temperature", f32), ("top_k", i32), ("top_p", f32), ("repetition_penalty", f32), ("seed", u64)]
+
+
+class ModelConfig(C.Structure):
+    _fields_ = [("vocab_size", i32), ("hidden_size", i32), ("intermediate_size", i32), ("num_layers", i32),
+                ("num_q_heads", i32), ("num_kv_heads", i32), ("head_dim", i32), ("rms_norm_eps", f32),
+                ("rope_theta", f32), ("tie_word_embeddings", i32), ("has_qkv_bias", i32), ("max_batch", i32),
+                ("max_seq", i32)]
+
+
+# name -> (restype, argtypes)
+_SIGS = {
+    "b2_version": (C.c_char_p, []),
+    "b2_status_string": (C.c_char_p, [i32]),
+    "b2_embedding_lookup": (i32, [vp, vp, vp, i64, i64, vp]),
+    "b2_rmsnorm": (i32, [vp, vp, vp, i64, i64, f32, vp]),
+    "b2_bias_add": (i32, [vp, vp, vp, i64, i64, vp]),
+    "b2_residual_add": (i32, [vp, vp, vp, i64, vp]),
+    "b2_apply_rope": (i32, [vp, vp, i64, i64, i64, i64, i64, f32, vp]),
+    "b2_causal_gqa": (i32, [vp, vp, vp, vp, i64, i64, i64, i64, vp]),
+    "b2_softmax": (i32, [vp, vp, i64, i64, vp]),
+    "b2_decode_gqa": (i32, [vp, vp, vp, vp, i32, i32, i32, i32, i32, vp]),
+    "b2_decode_gqa_split": (i32, [vp, KVView, KVView, vp, vp, i32, i32, i32, i32, i32, vp, C.c_size_t, vp]),
+    "b2_flash_prefill_gqa": (i32, [vp, vp, vp, vp, i64, i32, i32, i32, i32, vp]),
+    "b2_swiglu": (i32, [vp, vp, vp, i64, vp]),
+    "b2_matmul_transB": (i32, [vp, vp, vp, i32, i32, i32, vp]),
+    "b2_matmul_transB_f32": (i32, [vp, vp, vp, i32, i32, i32, vp]),
+    "b2_gemv": (i32, [vp, vp, vp, i32, i32, vp]),
+    "b2_gemv_bias": (i32, [vp, vp, vp, vp, i32, i32, vp]),
+    "b2_gemv_residual": (i32, [vp, vp, vp, vp, i32, i32, vp]),
+    "b2_gemv_batched": (i32, [vp, vp, vp, vp, i32, i32, i32, i32, i32, vp]),
+    "b2_append_kv_cache": (i32, [vp, vp, vp, vp, i32, i32, i32, i32, i32, vp]),
+    "b2_sampler_create": (i32, [i32, i32, C.POINTER(vp)]),
+    "b2_sampler_destroy": (i32, [vp]),
+    "b2_sampler_sample": (i32, [vp, vp, vp, i32, C.POINTER(SamplerConfig), vp, C.POINTER(i32)]),
+    "b2_sampler_rng_state": (u64, [vp]),
+    "b2_sampler_set_rng_state": (i32, [vp, u64]),
+    "b2_nccl_unique_id": (i32, [vp]),
+    "b2_model_create": (i32, [C.POINTER(ModelConfig), i32, i32, vp, C.POINTER(vp)]),
+    "b2_model_destroy": (i32, [vp]),
+    "b2_model_init_random": (i32, [vp, u64, f32]),
+    "b2_model_set_tensor": (i32, [vp, C.c_char_p, vp, i64, i64]),
+    "b2_model_reset": (i32, [vp]),
+    "b2_model_prefill": (i32, [vp, vp, i32, i32, vp]),
+    "b2_model_decode_step": (i32, [vp, vp, vp, i32, vp, vp]),
+    "b2_model_generate_greedy": (i32, [vp, i32, vp]),
+    "b2_model_sync": (i32, [vp]),
+    "b2_model_stream": (vp, [vp]),
+    "b2_model_buffer": (vp, [vp, C.c_char_p]),
+    "b2_model_read": (i32, [vp, C.c_char_p, vp, C.c_size_t, C.c_size_t]),
+    "b2_model_kv_layout": (i32, [vp, C.POINTER(i64), C.POINTER(i64), C.POINTER(i64), C.POINTER(i64), C.POINTER(i64)]),
+    "b2_model_step_bytes": (C.c_double, [vp, i32, i32]),
+    "b2_model_step_launches": (i32, [vp, i32]),
+    "b2_model_time_kernel": (i32, [vp, i32, i32, i32, C.POINTER(f32)]),
+    "b2_model_kernel_bytes": (C.c_double, [vp, i32, i32, i32]),
+}
+
+
+def exported_symbols():
+    return list(_SIGS)
+
+
+def lib():
+    """Load the library (raises if it was not built)."""
+    global _LIB
+    if _LIB is None:
+        if not os.path.exists(LIB_PATH):
+            raise ImportError(f"{LIB_PATH} is missing: run `make -C serving-engine_b200` (or __graft_entry__.build())")
+        if "B2_NCCL_LIB" not in os.environ:
+            # prefer the NCCL that torch ships, so both bind the same libnccl.so.2
+            try:
+                import importlib.util
+                spec = importlib.util.find_spec("nvidia.nccl")
+                for base in (spec.submodule_search_locations or []) if spec else []:
+                    cand = os.path.join(base, "lib", "libnccl.so.2")
+                    if os.path.exists(cand):
+                        os.environ["B2_NCCL_LIB"] = cand
+                        break
+            except Exception:
+                pass
+        L = C.CDLL(LIB_PATH)
+        for name, (res, args) in _SIGS.items():
+            fn = getattr(L, name)
+            fn.restype = res
+            fn.argtypes = args
+        _LIB = L
+    return _LIB
+
+
+def status_string(s: int) -> str:
+    return lib().b2_status_string(s).decode()
+
+
+def call(name: str, *args) -> None:
+    rc = getattr(lib(), name)(*args)
+    if rc != 0:
+        raise B2Error(name, rc)
+
+
+def ptr(t) -> int | None:
+    """Device pointer of a torch tensor (or None)."""
+    return None if t is None else t.data_ptr()
+
+
+def stream_ptr(stream=None) -> int | None:
+    if stream is None:
+        import torch
+        return torch.cuda.current_stream().cuda_stream
+    return stream
+
+
+# ---------------------------------------------------------------------------
+# operator API (torch tensors in, torch tensors out; all compute in the library)
+# ---------------------------------------------------------------------------
+
+def gemv(W, x, y, epi=None, extra=None, stream=None):
+    N, K = W.shape
+    if epi is None:
+        call("b2_gemv", ptr(W), ptr(x), ptr(y), N, K, stream_ptr(stream))
+    elif epi == "bias":
+        call("b2_gemv_bias", ptr(W), ptr(x), ptr(extra), ptr(y), N, K, stream_ptr(stream))
+    elif epi == "residual":
+        call("b2_gemv_residual", ptr(W), ptr(x), ptr(extra), ptr(y), N, K, stream_ptr(stream))
+    else:
+        raise ValueError(epi)
+
+
+def gemv_batched(W, x, y, epilogue=0, extra=None, out_f32=False, stream=None):
+    N, K = W.shape
+    B = x.shape[0]
+    call("b2_gemv_batched", ptr(W), ptr(x), ptr(extra), ptr(y), B, N, K, epilogue, int(out_f32), stream_ptr(stream))
+
+
+def decode_gqa_split(q, kview: KVView, vview: KVView, seq_lens, out, B, nq, nkv, D, max_seq_len,
+                     split_buffer=None, stream=None):
+    cap = 0 if split_buffer is None else split_buffer.numel()
+    call("b2_decode_gqa_split", ptr(q), kview, vview, ptr(seq_lens), ptr(out), B, nq, nkv, D, max_seq_len,
+         ptr(split_buffer), cap, stream_ptr(stream))
+
+
+class Sampler:
+    """engine::SamplerGPU through the C-ABI."""
+
+    def __init__(self, vocab: int, max_top_k: int = 1024):
+        h = vp()
+        call("b2_sampler_create", vocab, max_top_k, C.byref(h))
+        self.h = h
+
+    def sample(self, d_logits, history=(), temperature=0.0, top_k=0, top_p=1.0, repetition_penalty=1.0, seed=42,
+               stream=None) -> int:
+        import numpy as np
+        hist = np.ascontiguousarray(np.asarray(history, dtype=np.int64))
+        cfg = SamplerConfig(temperature, top_k, top_p, repetition_penalty, seed)
+        tok = i32()
+        call("b2_sampler_sample", self.h, ptr(d_logits), hist.ctypes.data if hist.size else None, hist.size,
+             C.byref(cfg), stream_ptr(stream), C.byref(tok))
+        return tok.value
+
+    @property
+    def rng_state(self) -> int:
+        return int(lib().b2_sampler_rng_state(self.h))
+
+    def close(self):
+        if self.h:
+            lib().b2_sampler_destroy(self.h)
+            self.h = None
+
+    __del__ = close
+
+
+def nccl_unique_id() -> bytes:
+    buf = (C.c_char * 128)()
+    call("b2_nccl_unique_id", C.cast(buf, vp))
+    return bytes(buf)
+
+
+class Model:
+    """A decode-path model shard (b2_model_*)."""
+
+    def __init__(self, vocab, hidden, inter, layers, nq, nkv, head_dim, eps=1e-5, theta=10000.0, tied=False,
+                 bias=False, max_batch=1, max_seq=4096, tp_rank=0, tp_size=1, nccl_id: bytes | None = None):
+        self.cfg = ModelConfig(vocab, hidden, inter, layers, nq, nkv, head_dim, eps, theta, int(tied), int(bias),
+                               max_batch, max_seq)
+        h = vp()
+        idbuf = None
+        if nccl_id is not None:
+            idbuf = (C.c_char * 128).from_buffer_copy(nccl_id)
+        call("b2_model_create", C.byref(self.cfg), tp_rank, tp_size, C.cast(idbuf, vp) if idbuf else None, C.byref(h))
+        self.h = h
+        self.vocab = vocab
+        self._B = max_batch
+
+    def init_random(self, seed: int, std: float = 0.02):
+        call("b2_model_init_random", self.h, seed, std)
+
+    def set_tensor(self, name: str, arr16):
+        import numpy as np
+        a = np.ascontiguousarray(arr16, dtype=np.float16)
+        rows, cols = (a.shape[0], a.shape[1]) if a.ndim == 2 else (1, a.size)
+        call("b2_model_set_tensor", self.h, name.encode(), a.ctypes.data, rows, cols)
+
+    def reset(self):
+        call("b2_model_reset", self.h)
+
+    def prefill(self, ids, want_logits=True):
+        import numpy as np
+        a = np.ascontiguousarray(np.atleast_2d(np.asarray(ids, dtype=np.int64)))
+        B, S = a.shape
+        self._B = B
+        out = np.empty((B, self.vocab), np.float32) if want_logits else None
+        call("b2_model_prefill", self.h, a.ctypes.data, B, S, out.ctypes.data if out is not None else None)
+        return out
+
+    def decode_step(self, tokens, positions, want_logits=True, want_next=False):
+        import numpy as np
+        t = np.ascontiguousarray(np.asarray(tokens, dtype=np.int64).reshape(-1))
+        p = np.ascontiguousarray(np.asarray(positions, dtype=np.int32).reshape(-1))
+        B = t.size
+        self._B = B
+        lg = np.empty((B, self.vocab), np.float32) if want_logits else None
+        nx = np.empty(B, np.int64) if want_next else None
+        call("b2_model_decode_step", self.h, t.ctypes.data, p.ctypes.data, B,
+             lg.ctypes.data if lg is not None else None, nx.ctypes.data if nx is not None else None)
+        return lg, nx
+
+    def generate_greedy(self, steps: int, fetch=True):
+        """Device-resident greedy loop continuing from the last prefill / step.
+        fetch=True returns the ids [steps, batch] (synchronises); fetch=False
+        only enqueues the steps on the model's stream."""
+        import numpy as np
+        if fetch:
+            out = np.empty((steps, self._B), np.int64)
+            call("b2_model_generate_greedy", self.h, steps, out.ctypes.data)
+            return out
+        call("b2_model_generate_greedy", self.h, steps, None)
+        return None
+
+    def sync(self):
+        call("b2_model_sync", self.h)
+
+    @property
+    def stream(self) -> int:
+        return lib().b2_model_stream(self.h)
+
+    def buffer(self, name: str) -> int:
+        return lib().b2_model_buffer(self.h, name.encode())
+
+    def read(self, name: str, dtype, count: int, offset_elems: int = 0):
+        import numpy as np
+        out = np.empty(count, dtype)
+        call("b2_model_read", self.h, name.encode(), out.ctypes.data, offset_elems * out.itemsize, out.nbytes)
+        return out
+
+    def kv_layout(self):
+        v = [i64() for _ in range(5)]
+        call("b2_model_kv_layout", self.h, *[C.byref(x) for x in v])
+        return tuple(x.value for x in v)
+
+    def step_bytes(self, batch: int, ctx: int) -> float:
+        return float(lib().b2_model_step_bytes(self.h, batch, ctx))
+
+    KERNELS = ("qkv", "attention", "o_proj", "gate_up", "down", "lm_head")
+
+    def time_kernel(self, kind: str, batch: int, reps: int = 3) -> float:
+        ms = f32()
+        call("b2_model_time_kernel", self.h, self.KERNELS.index(kind), batch, reps, C.byref(ms))
+        return float(ms.value)
+
+    def kernel_bytes(self, kind: str, batch: int, ctx: int) -> float:
+        return float(lib().b2_model_kernel_bytes(self.h, self.KERNELS.index(kind), batch, ctx))
+
+    def step_launches(self, batch: int) -> int:
+        return int(lib().b2_model_step_launches(self.h, batch))
+
+    def close(self):
+        if getattr(self, "h", None):
+            lib().b2_model_destroy(self.h)
+            self.h = None
+
+    __del__ = close

@@ -1,0 +1,417 @@
+// gemv.cu -- decode GEMV family for sm_100a.
+//
+// Decode at small batch is a pure weight stream: every weight byte is read
+// once per step and each is used for B multiply-adds, so the kernel's job is
+// to keep enough 16-byte loads in flight to saturate HBM3e and to hide the
+// kernel boundary.  Design:
+//   * one warp per task (a row, or a pair of rows that its epilogue needs
+//     together: the two rotate-half partners of a q/k head, or the gate and up
+//     rows of one FFN unit), full K per warp, so no cross-warp reduction;
+//   * 128-bit L1-bypassing loads (ld.global.nc.L1::no_allocate.v4), U chunks of
+//     16 bytes per lane per row per batch, software pipelined: the next batch
+//     of loads is issued before the current one is multiplied, so every lane
+//     keeps 2*R*U*16 bytes in flight;
+//   * the activation vector is staged once per CTA in shared memory (for the
+//     X_NORM forms the RMSNorm of the fp32 residual stream is computed there,
+//     fusing the norm kernel away);
+//   * grid sized from the SM count and measured occupancy so that every warp
+//     gets the same number of tasks (no half-empty last wave);
+//   * programmatic dependent launch: the first batch of weight loads is issued
+//     before griddepcontrol.wait, overlapping the previous kernel's tail.
+// Reference kernel replaced: src/cuda/gemv.cu:28-116 (one warp per row,
+// scalar 2-byte loads, separate norm / RoPE / SwiGLU / residual kernels).
+#include <cmath>
+#include <mutex>
+
+#include "gemv.cuh"
+
+namespace b2 {
+
+static int g_sm_count[64];
+static std::once_flag g_sm_once[64];
+
+int sm_count() {
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (dev < 0 || dev >= 64) dev = 0;
+    std::call_once(g_sm_once[dev], [dev]() {
+        int n = 0;
+        cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+        g_sm_count[dev] = n > 0 ? n : 1;
+    });
+    return g_sm_count[dev];
+}
+
+bool pdl_enabled() {
+    static int on = -1;
+    if (on < 0) {
+        const char* e = getenv("B2_PDL");
+        on = (e && e[0] == '0') ? 0 : 1;
+    }
+    return on == 1;
+}
+
+constexpr int kGemvThreads = 256;
+constexpr int kGemvWarps = kGemvThreads / 32;
+
+template <int R, int U>
+__device__ __forceinline__ void load_rows(uint4 (&w)[R][U], const uint4* const (&rp)[R], int cbase, int K8,
+                                          int lane) {
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+        const int c = cbase + u * 32 + lane;
+#pragma unroll
+        for (int r = 0; r < R; ++r) w[r][u] = c < K8 ? ldg_stream(rp[r] + c) : make_uint4(0, 0, 0, 0);
+    }
+}
+
+template <int R, int OM>
+__device__ __forceinline__ void task_rows(const GemvParams& p, int t, const uint4* (&rp)[R]) {
+    if constexpr (OM == OUT_QKV) {
+        const int half = p.D >> 1;
+        const int h = t / half, i = t - h * half;
+        const int r0 = h * p.D + i;
+        rp[0] = reinterpret_cast<const uint4*>(p.W + (size_t)r0 * p.K);
+        rp[1] = reinterpret_cast<const uint4*>(p.W + (size_t)(r0 + half) * p.K);
+    } else if constexpr (OM == OUT_SWIGLU) {
+        rp[0] = reinterpret_cast<const uint4*>(p.W + (size_t)t * p.K);
+        rp[1] = reinterpret_cast<const uint4*>(p.W2 + (size_t)t * p.K);
+    } else {
+        rp[0] = reinterpret_cast<const uint4*>(p.W + (size_t)t * p.K);
+    }
+}
+
+template <int R, int BT, int XM, int OM, int U>
+__global__ void __launch_bounds__(kGemvThreads, 2) gemv_vec_kernel(const GemvParams p) {
+    extern __shared__ __align__(16) uint4 xs[];  // [BT][K8] packed half
+    __shared__ float s_rs[BT];
+    __shared__ unsigned long long s_best[kGemvWarps][BT];
+
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int K8 = p.K >> 3;
+    const int NB = (K8 + 32 * U - 1) / (32 * U);
+    const int total_warps = gridDim.x * kGemvWarps;
+    int t = blockIdx.x * kGemvWarps + warp;
+
+    // Weights do not depend on the previous kernel: start streaming them now.
+    uint4 wn[R][U];
+    if (t < p.tasks) {
+        const uint4* rp[R];
+        task_rows<R, OM>(p, t, rp);
+        load_rows<R, U>(wn, rp, 0, K8, lane);
+    }
+
+    griddep_wait();
+    griddep_launch_dependents();
+
+    // ---- stage x in shared memory --------------------------------------
+    if constexpr (XM == X_NORM) {
+        const float* h = static_cast<const float*>(p.x);
+        for (int b = warp; b < BT; b += kGemvWarps) {
+            float ss = 0.f;
+            if (b < p.B) {
+                const float4* hr = reinterpret_cast<const float4*>(h + (size_t)b * p.ldx);
+                for (int i = lane; i < (p.K >> 2); i += 32) {
+                    const float4 v = hr[i];
+                    ss = fmaf(v.x, v.x, ss); ss = fmaf(v.y, v.y, ss);
+                    ss = fmaf(v.z, v.z, ss); ss = fmaf(v.w, v.w, ss);
+                }
+            }
+            ss = warp_sum(ss);
+            if (lane == 0) s_rs[b] = rsqrtf(ss / (float)p.K + p.eps);
+        }
+        __syncthreads();
+        for (int i = threadIdx.x; i < BT * K8; i += kGemvThreads) {
+            const int b = i / K8, c = i - b * K8;
+            uint4 o = make_uint4(0, 0, 0, 0);
+            if (b < p.B) {
+                const float4* hr = reinterpret_cast<const float4*>(h + (size_t)b * p.ldx) + 2 * c;
+                const float4 a0 = hr[0], a1 = hr[1];
+                float wv[8];
+                unpack8(ldg16(reinterpret_cast<const uint4*>(p.norm_w) + c), wv);
+                const float r = s_rs[b];
+                float f[8] = {a0.x * r * wv[0], a0.y * r * wv[1], a0.z * r * wv[2], a0.w * r * wv[3],
+                              a1.x * r * wv[4], a1.y * r * wv[5], a1.z * r * wv[6], a1.w * r * wv[7]};
+                o = pack8(f);
+            }
+            xs[i] = o;
+        }
+    } else {
+        const __half* xh = static_cast<const __half*>(p.x);
+        for (int i = threadIdx.x; i < BT * K8; i += kGemvThreads) {
+            const int b = i / K8, c = i - b * K8;
+            xs[i] = b < p.B ? ldg16(reinterpret_cast<const uint4*>(xh + (size_t)b * p.ldx) + c)
+                            : make_uint4(0, 0, 0, 0);
+        }
+    }
+    __syncthreads();
+
+    unsigned long long best[BT];
+#pragma unroll
+    for (int b = 0; b < BT; ++b) best[b] = 0ull;
+
+    // ---- stream the warp's tasks ---------------------------------------
+    for (; t < p.tasks; t += total_warps) {
+        float acc[R][BT];
+#pragma unroll
+        for (int r = 0; r < R; ++r)
+#pragma unroll
+            for (int b = 0; b < BT; ++b) acc[r][b] = 0.f;
+
+        for (int cb = 0; cb < NB; ++cb) {
+            uint4 wc[R][U];
+#pragma unroll
+            for (int u = 0; u < U; ++u)
+#pragma unroll
+                for (int r = 0; r < R; ++r) wc[r][u] = wn[r][u];
+            // issue the next batch (this task's next chunk batch, or the next task's first)
+            {
+                int nt = t, ncb = cb + 1;
+                if (ncb == NB) { nt = t + total_warps; ncb = 0; }
+                if (nt < p.tasks) {
+                    const uint4* rp[R];
+                    task_rows<R, OM>(p, nt, rp);
+                    load_rows<R, U>(wn, rp, ncb * 32 * U, K8, lane);
+                }
+            }
+#pragma unroll
+            for (int u = 0; u < U; ++u) {
+                const int c = cb * 32 * U + u * 32 + lane;
+                if (c < K8) {
+#pragma unroll
+                    for (int b = 0; b < BT; ++b) {
+                        const uint4 xv = xs[b * K8 + c];
+#pragma unroll
+                        for (int r = 0; r < R; ++r) acc[r][b] = dot8(wc[r][u], xv, acc[r][b]);
+                    }
+                }
+            }
+        }
+#pragma unroll
+        for (int r = 0; r < R; ++r)
+#pragma unroll
+            for (int b = 0; b < BT; ++b) acc[r][b] = warp_sum(acc[r][b]);
+
+        // ---- epilogue: lane b handles sequence b -------------------------
+        if constexpr (OM == OUT_LOGITS) {
+#pragma unroll
+            for (int b = 0; b < BT; ++b) {
+                if (b < p.B) {
+                    const int gid = p.row_offset + t;
+                    if (gid < p.argmax_limit) {
+                        const unsigned long long k = argmax_key(acc[0][b], (uint32_t)gid);
+                        best[b] = k > best[b] ? k : best[b];
+                    }
+                }
+            }
+        }
+#pragma unroll
+        for (int b = 0; b < BT; ++b) {
+            if (lane != b || b >= p.B) continue;
+            if constexpr (OM == OUT_HALF || OM == OUT_F32) {
+                float v = acc[0][b];
+                if (p.bias) v += __half2float(p.bias[t]);
+                if (p.resid) v += __half2float(p.resid[(size_t)b * p.ld_resid + t]);
+                if constexpr (OM == OUT_HALF)
+                    static_cast<__half*>(p.y)[(size_t)b * p.ldy + t] = __float2half_rn(v);
+                else
+                    static_cast<float*>(p.y)[(size_t)b * p.ldy + t] = v;
+            } else if constexpr (OM == OUT_RESID) {
+                float* y = static_cast<float*>(p.y) + (size_t)b * p.ldy + t;
+                *y = p.resid_add ? *y + acc[0][b] : acc[0][b];
+            } else if constexpr (OM == OUT_LOGITS) {
+                static_cast<float*>(p.y)[(size_t)b * p.ldy + t] = acc[0][b];
+            } else if constexpr (OM == OUT_SWIGLU) {
+                const float g = acc[0][b], u = acc[1][b];
+                static_cast<__half*>(p.y)[(size_t)b * p.ldy + t] = __float2half_rn(g / (1.0f + expf(-g)) * u);
+            } else if constexpr (OM == OUT_QKV) {
+                const int half = p.D >> 1;
+                const int h = t / half, i = t - h * half;
+                float x1 = acc[0][b], x2 = acc[1][b];
+                if (p.bias) {
+                    x1 += __half2float(p.bias[h * p.D + i]);
+                    x2 += __half2float(p.bias[h * p.D + i + half]);
+                }
+                const int pos = p.pos[b];
+                if (h < p.nq + p.nkv) {
+                    const float2 cs = p.rope[(size_t)pos * half + i];
+                    const float o1 = x1 * cs.x - x2 * cs.y;
+                    const float o2 = x2 * cs.x + x1 * cs.y;
+                    if (h < p.nq) {
+                        __half* q = static_cast<__half*>(p.y) + (size_t)b * p.ldy + h * p.D;
+                        q[i] = __float2half_rn(o1);
+                        q[i + half] = __float2half_rn(o2);
+                    } else {
+                        __half* k = p.kcache + b * p.kv_sb + (int64_t)(h - p.nq) * p.kv_sh + (int64_t)pos * p.D;
+                        k[i] = __float2half_rn(o1);
+                        k[i + half] = __float2half_rn(o2);
+                    }
+                } else {
+                    __half* v = p.vcache + b * p.kv_sb + (int64_t)(h - p.nq - p.nkv) * p.kv_sh + (int64_t)pos * p.D;
+                    v[i] = __float2half_rn(x1);
+                    v[i + half] = __float2half_rn(x2);
+                }
+            }
+        }
+    }
+
+    if constexpr (OM == OUT_LOGITS) {
+        if (lane == 0) {
+#pragma unroll
+            for (int b = 0; b < BT; ++b) s_best[warp][b] = best[b];
+        }
+        __syncthreads();
+        if (threadIdx.x < BT && (int)threadIdx.x < p.B) {
+            unsigned long long m = 0ull;
+            for (int w = 0; w < kGemvWarps; ++w) m = s_best[w][threadIdx.x] > m ? s_best[w][threadIdx.x] : m;
+            if (m) atomicMax(p.argmax + threadIdx.x, m);
+        }
+    }
+}
+
+// ---------------------------------------------------------------------------
+// launch plumbing
+// ---------------------------------------------------------------------------
+
+template <int R, int BT, int XM, int OM, int U>
+static int launch_vec(const GemvParams& p, cudaStream_t s, bool pdl) {
+    auto kern = gemv_vec_kernel<R, BT, XM, OM, U>;
+    const size_t smem = (size_t)BT * p.K * sizeof(__half);
+    // per-device occupancy cache, keyed on the shared-memory footprint
+    static thread_local int last_dev = -1;
+    static thread_local size_t last_smem = (size_t)-1;
+    static thread_local int last_occ = 1;
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (dev != last_dev || smem != last_smem) {
+        B2_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)(smem > 0 ? smem : 1)));
+        int occ = 0;
+        B2_TRY(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, kern, kGemvThreads, smem));
+        last_occ = occ > 0 ? occ : 1;
+        last_dev = dev;
+        last_smem = smem;
+    }
+    const int max_warps = sm_count() * last_occ * kGemvWarps;
+    const int rounds = (p.tasks + max_warps - 1) / max_warps;
+    const int warps = (p.tasks + rounds - 1) / rounds;
+    const int ctas = (warps + kGemvWarps - 1) / kGemvWarps;
+    B2_TRY(launch(kern, dim3(ctas), dim3(kGemvThreads), smem, s, pdl, p));
+    return B2_OK;
+}
+
+int gemv_batch_tile(int K) {
+    // keep two CTAs of x staging per SM within ~200 KB of shared memory
+    const long budget = 100 * 1024;
+    for (int bt = 8; bt > 1; bt >>= 1)
+        if ((long)bt * K * 2 <= budget) return bt;
+    return 1;
+}
+
+template <int R, int XM, int OM, int U>
+static int dispatch_bt(const GemvParams& p, cudaStream_t s, bool pdl) {
+    if (p.B <= 1) return launch_vec<R, 1, XM, OM, U>(p, s, pdl);
+    if (p.B <= 2) return launch_vec<R, 2, XM, OM, U>(p, s, pdl);
+    if (p.B <= 4) return launch_vec<R, 4, XM, OM, U>(p, s, pdl);
+    return launch_vec<R, 8, XM, OM, U>(p, s, pdl);
+}
+
+int gemv_launch(const GemvParams& p, XMode xm, OutMode om, cudaStream_t s, bool pdl) {
+    if (p.tasks <= 0 || p.B <= 0) return B2_OK;
+    if (p.K <= 0 || (p.K & 7) || !aligned16(p.W) || !aligned16(p.x) || (p.ldx & 7)) return B2_ERR_UNSUPPORTED;
+    if (p.B > 8 || p.B > gemv_batch_tile(p.K)) return B2_ERR_UNSUPPORTED;
+    if (om == OUT_SWIGLU && !aligned16(p.W2)) return B2_ERR_UNSUPPORTED;
+    if (xm == X_NORM && (!p.norm_w || !aligned16(p.norm_w))) return B2_ERR_UNSUPPORTED;
+    switch (om) {
+        case OUT_HALF: return dispatch_bt<1, X_HALF, OUT_HALF, 8>(p, s, pdl);
+        case OUT_F32:  return dispatch_bt<1, X_HALF, OUT_F32, 8>(p, s, pdl);
+        case OUT_RESID: return dispatch_bt<1, X_HALF, OUT_RESID, 8>(p, s, pdl);
+        case OUT_QKV:  return xm == X_NORM ? dispatch_bt<2, X_NORM, OUT_QKV, 4>(p, s, pdl) : B2_ERR_UNSUPPORTED;
+        case OUT_SWIGLU: return xm == X_NORM ? dispatch_bt<2, X_NORM, OUT_SWIGLU, 4>(p, s, pdl) : B2_ERR_UNSUPPORTED;
+        case OUT_LOGITS: return xm == X_NORM ? dispatch_bt<1, X_NORM, OUT_LOGITS, 8>(p, s, pdl) : B2_ERR_UNSUPPORTED;
+    }
+    return B2_ERR_UNSUPPORTED;
+}
+
+// ---------------------------------------------------------------------------
+// generic path: any K, any alignment (odd API shapes).  One warp per row.
+// ---------------------------------------------------------------------------
+__global__ void gemv_generic_kernel(const __half* __restrict__ W, const __half* __restrict__ x,
+                                    const __half* __restrict__ extra, void* __restrict__ y, int B, int N,
+                                    int K, int epi, int out_f32) {
+    griddep_wait();
+    const int lane = threadIdx.x & 31;
+    const int nw = (gridDim.x * blockDim.x) >> 5;
+    for (int row = (blockIdx.x * blockDim.x + threadIdx.x) >> 5; row < N; row += nw) {
+        const __half* wr = W + (size_t)row * K;
+        for (int b = 0; b < B; ++b) {
+            const __half* xb = x + (size_t)b * K;
+            float acc = 0.f;
+            for (int k = lane; k < K; k += 32) acc = fmaf(__half2float(wr[k]), __half2float(xb[k]), acc);
+            acc = warp_sum(acc);
+            if (lane == 0) {
+                if (epi == 1) acc += __half2float(extra[row]);
+                if (epi == 2) acc += __half2float(extra[(size_t)b * N + row]);
+                if (out_f32) static_cast<float*>(y)[(size_t)b * N + row] = acc;
+                else static_cast<__half*>(y)[(size_t)b * N + row] = __float2half_rn(acc);
+            }
+        }
+    }
+}
+
+static int gemv_api(const void* W, const void* x, const void* extra, void* y, int B, int N, int K, int epi,
+                    int out_f32, void* stream) {
+    if (N <= 0 || K <= 0 || B <= 0) return B2_OK;
+    B2_REQUIRE(W && x && y && (epi == 0 || extra));
+    B2_REQUIRE(epi >= 0 && epi <= 2);
+    cudaStream_t s = as_stream(stream);
+    const bool vec_ok = (K % 8 == 0) && aligned16(W) && aligned16(x);
+    if (vec_ok) {
+        const int bt = gemv_batch_tile(K);
+        for (int b0 = 0; b0 < B; b0 += bt) {
+            const int nb = B - b0 < bt ? B - b0 : bt;
+            GemvParams p = {};
+            p.W = static_cast<const __half*>(W);
+            p.K = K;
+            p.tasks = N;
+            p.B = nb;
+            p.x = static_cast<const __half*>(x) + (size_t)b0 * K;
+            p.ldx = K;
+            p.bias = epi == 1 ? static_cast<const __half*>(extra) : nullptr;
+            p.resid = epi == 2 ? static_cast<const __half*>(extra) + (size_t)b0 * N : nullptr;
+            p.ld_resid = N;
+            p.y = out_f32 ? (void*)(static_cast<float*>(y) + (size_t)b0 * N)
+                          : (void*)(static_cast<__half*>(y) + (size_t)b0 * N);
+            p.ldy = N;
+            const int rc = gemv_launch(p, X_HALF, out_f32 ? OUT_F32 : OUT_HALF, s, true);
+            if (rc != B2_OK) return rc;
+        }
+        return B2_OK;
+    }
+    const int threads = 256;
+    long ctas = ((long)N * 32 + threads - 1) / threads;
+    const long cap = (long)sm_count() * 8;
+    if (ctas > cap) ctas = cap;
+    B2_TRY(launch(gemv_generic_kernel, dim3((unsigned)ctas), dim3(threads), 0, s, true,
+                  static_cast<const __half*>(W), static_cast<const __half*>(x), static_cast<const __half*>(extra), y,
+                  B, N, K, epi, out_f32));
+    return B2_OK;
+}
+
+}  // namespace b2
+
+extern "C" int b2_gemv(const void* W, const void* x, void* y, int N, int K, void* stream) {
+    return b2::gemv_api(W, x, nullptr, y, 1, N, K, 0, 0, stream);
+}
+
+extern "C" int b2_gemv_bias(const void* W, const void* x, const void* b, void* y, int N, int K, void* stream) {
+    return b2::gemv_api(W, x, b, y, 1, N, K, 1, 0, stream);
+}
+
+extern "C" int b2_gemv_residual(const void* W, const void* x, const void* r, void* y, int N, int K, void* stream) {
+    return b2::gemv_api(W, x, r, y, 1, N, K, 2, 0, stream);
+}
+
+extern "C" int b2_gemv_batched(const void* W, const void* x, const void* extra, void* y, int B, int N, int K,
+                               int epilogue, int out_f32, void* stream) {
+    return b2::gemv_api(W, x, extra, y, B, N, K, epilogue, out_f32, stream);
+}

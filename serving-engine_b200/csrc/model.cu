@@ -1,0 +1,878 @@
+// model.cu -- decode-step runtime: sharded weights, KV cache, seeded
+// initialisation, the per-token step as one captured CUDA graph, greedy
+// generation on the device, and Megatron tensor parallelism over NCCL.
+//
+// One decode step for B sequences (per rank, tp = tensor-parallel degree):
+//   step_begin   hidden[b] = embed[token[b]] (fp32 residual stream),
+//                seq_len[b] = pos[b] + 1, argmax[b] = 0
+//   per layer    qkv     RMSNorm(ln1) prologue, fused q|k|v GEMV, RoPE
+//                        epilogue, K/V written straight into the cache
+//                attn    split-KV GQA attention, splits merged in-kernel
+//                o       GEMV, residual added into hidden (rank 0 only) ...
+//                [tp>1]  ncclAllReduce(hidden, sum)  ... the sum is the new hidden
+//                gateup  RMSNorm(ln2) prologue, gate and up GEMV, SwiGLU epilogue
+//                down    GEMV, residual into hidden; [tp>1] ncclAllReduce
+//   lm_head      RMSNorm(final) prologue, vocabulary-shard GEMV to fp32 logits
+//                with a packed per-sequence argmax; [tp>1] ncclAllReduce(max)
+//   step_end     token[b] = argmax id, pos[b] += 1, history append
+// Everything reads tokens / positions from device memory, so the captured
+// graph is replayed unchanged step after step.
+//
+// Reference replaced: src/model/forward_gpu.cu:30-101 (weights, buffers),
+// :329-520 (prefill), :523-707 (decode_step_gpu: 13 launches per layer on the
+// legacy stream, synchronous H2D/D2H each token, no graph), and the KV layout
+// of src/runtime/kv_cache.h:12-73.
+#include <dlfcn.h>
+#include <nccl.h>
+
+#include <cmath>
+#include <mutex>
+#include <cstdio>
+#include <cstring>
+#include <new>
+#include <string>
+#include <vector>
+
+#include "gemv.cuh"
+
+namespace b2 {
+
+struct AttnParams;
+int attn_pick_splits(int batch, int nq, int nkv, int D, int max_len, size_t cap_floats);
+size_t attn_scratch_floats(int batch, int nq, int nkv, int D, int splits);
+bool attn_head_dim_supported(int D);
+int attn_decode_launch_model(const __half* q, const __half* kbase, const __half* vbase, int64_t sb, int64_t sh,
+                             int64_t ss, const int* seq_lens, __half* out, float* part, int splits, int B, int nq,
+                             int nkv, int D, cudaStream_t s, bool pdl);
+
+// ---------------------------------------------------------------------------
+// seeded initialisation (bit-identical to oracle/b2oracle.c ora_init_value)
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ uint64_t mix64(uint64_t z) {
+    z += 0x9E3779B97F4A7C15ull;
+    z = (z ^ (z >> 30)) * 0xBF58476D1CE4E5B9ull;
+    z = (z ^ (z >> 27)) * 0x94D049BB133111EBull;
+    return z ^ (z >> 31);
+}
+
+// dst[r * cols + c] = value(tensor_id, (row0 + r) * ld_global + col0 + c)
+__global__ void init_tensor_kernel(__half* __restrict__ dst, int64_t rows, int64_t cols, uint64_t seed,
+                                   uint64_t tensor_id, int64_t row0, int64_t col0, int64_t ld_global, float scale) {
+    const uint64_t key = mix64(seed + 0x9E3779B97F4A7C15ull * (tensor_id + 1));
+    const int64_t n = rows * cols;
+    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
+        const int64_t r = i / cols, c = i - (i / cols) * cols;
+        const uint64_t idx = (uint64_t)(row0 + r) * (uint64_t)ld_global + (uint64_t)(col0 + c);
+        const uint64_t h = mix64(key ^ idx);
+        const int32_t s = (int32_t)(h & 0xFFFF) + (int32_t)((h >> 16) & 0xFFFF) + (int32_t)((h >> 32) & 0xFFFF) +
+                          (int32_t)((h >> 48) & 0xFFFF);
+        dst[i] = __float2half_rn(__fmul_rn((float)(s - 131070), scale));
+    }
+}
+
+__global__ void fill_half_kernel(__half* dst, int64_t n, float v) {
+    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x)
+        dst[i] = __float2half_rn(v);
+}
+
+// ---------------------------------------------------------------------------
+// step boundary kernels
+// ---------------------------------------------------------------------------
+__global__ void step_begin_kernel(const int64_t* __restrict__ tokens, const int* __restrict__ positions,
+                                  const __half* __restrict__ embed, float* __restrict__ hidden, int H,
+                                  int* __restrict__ seq_lens, unsigned long long* __restrict__ argmax,
+                                  int64_t* __restrict__ hist, const int* __restrict__ hist_count, int hist_cap) {
+    griddep_wait();
+    griddep_launch_dependents();
+    const int b = blockIdx.x;
+    const int64_t id = tokens[b];
+    const uint4* src = reinterpret_cast<const uint4*>(embed + id * H);
+    float4* dst = reinterpret_cast<float4*>(hidden + (int64_t)b * H);
+    for (int i = threadIdx.x; i < H / 8; i += blockDim.x) {
+        float f[8];
+        unpack8(ldg16(src + i), f);
+        dst[2 * i] = make_float4(f[0], f[1], f[2], f[3]);
+        dst[2 * i + 1] = make_float4(f[4], f[5], f[6], f[7]);
+    }
+    if (threadIdx.x == 0) {
+        seq_lens[b] = positions[b] + 1;
+        argmax[b] = 0ull;
+        // the history records the token each step consumes
+        const int c = *hist_count;
+        if (c < hist_cap) hist[(int64_t)c * gridDim.x + b] = id;
+    }
+}
+
+// token[b] = argmax id, pos[b] += 1, history counter += 1.
+__global__ void step_end_kernel(const unsigned long long* __restrict__ argmax, int64_t* __restrict__ tokens,
+                                int* __restrict__ positions, int B, int* __restrict__ hist_count, int hist_cap) {
+    griddep_wait();
+    const int b = threadIdx.x;
+    if (b < B) {
+        tokens[b] = (int64_t)argmax_key_id(argmax[b]);
+        positions[b] += 1;
+    }
+    if (b == 0) {
+        const int c = *hist_count;
+        if (c < hist_cap) *hist_count = c + 1;
+    }
+}
+
+// ---------------------------------------------------------------------------
+// NCCL, resolved at run time.  Linking libnccl would pin whichever
+// libnccl.so.2 the loader meets first for the whole process (and a host
+// framework loaded later may need a newer one), so the library binds the few
+// entry points it uses only when a tensor-parallel model is created: an NCCL
+// already loaded in the process is preferred, then $B2_NCCL_LIB, then the
+// default search path.
+// ---------------------------------------------------------------------------
+struct NcclApi {
+    ncclResult_t (*GetUniqueId)(ncclUniqueId*) = nullptr;
+    ncclResult_t (*CommInitRank)(ncclComm_t*, int, ncclUniqueId, int) = nullptr;
+    ncclResult_t (*CommDestroy)(ncclComm_t) = nullptr;
+    ncclResult_t (*AllReduce)(const void*, void*, size_t, ncclDataType_t, ncclRedOp_t, ncclComm_t,
+                              cudaStream_t) = nullptr;
+    ncclResult_t (*AllGather)(const void*, void*, size_t, ncclDataType_t, ncclComm_t, cudaStream_t) = nullptr;
+    bool ok = false;
+};
+
+static NcclApi& nccl() {
+    static NcclApi api;
+    static std::once_flag once;
+    std::call_once(once, []() {
+        void* h = dlopen("libnccl.so.2", RTLD_NOW | RTLD_NOLOAD);
+        const char* env = getenv("B2_NCCL_LIB");
+        if (!h && env && env[0]) h = dlopen(env, RTLD_NOW | RTLD_GLOBAL);
+        if (!h) h = dlopen("libnccl.so.2", RTLD_NOW | RTLD_GLOBAL);
+        if (!h) return;
+        api.GetUniqueId = reinterpret_cast<decltype(api.GetUniqueId)>(dlsym(h, "ncclGetUniqueId"));
+        api.CommInitRank = reinterpret_cast<decltype(api.CommInitRank)>(dlsym(h, "ncclCommInitRank"));
+        api.CommDestroy = reinterpret_cast<decltype(api.CommDestroy)>(dlsym(h, "ncclCommDestroy"));
+        api.AllReduce = reinterpret_cast<decltype(api.AllReduce)>(dlsym(h, "ncclAllReduce"));
+        api.AllGather = reinterpret_cast<decltype(api.AllGather)>(dlsym(h, "ncclAllGather"));
+        api.ok = api.GetUniqueId && api.CommInitRank && api.CommDestroy && api.AllReduce && api.AllGather;
+    });
+    return api;
+}
+
+}  // namespace b2
+
+using namespace b2;
+
+// ---------------------------------------------------------------------------
+// model object
+// ---------------------------------------------------------------------------
+struct LayerW {
+    __half *wqkv = nullptr, *bqkv = nullptr, *wo = nullptr, *wg = nullptr, *wu = nullptr, *wd = nullptr;
+    __half *ln1 = nullptr, *ln2 = nullptr;
+};
+
+struct b2_model {
+    b2_model_config cfg{};
+    int rank = 0, tp = 1, device = 0;
+    int nq = 0, nkv = 0, inter = 0, vocab_l = 0, vocab_off = 0;  // per-rank sizes
+    int qkv_rows = 0;
+    cudaStream_t stream = nullptr;
+    ncclComm_t comm = nullptr;
+
+    std::vector<void*> allocs;
+    __half* embed = nullptr;
+    __half* lm_head = nullptr;  // local vocabulary shard
+    __half* final_norm = nullptr;
+    std::vector<LayerW> layers;
+
+    __half* kv = nullptr;
+    int64_t kv_s_layer = 0, kv_s_batch = 0, kv_s_kv = 0, kv_s_head = 0;
+    float2* rope = nullptr;
+
+    float* hidden = nullptr;
+    __half* q = nullptr;
+    __half* attn = nullptr;
+    __half* act = nullptr;
+    float* logits = nullptr;
+    float* logits_gather = nullptr;  // [tp][B][vocab_l] (tp > 1)
+    float* part = nullptr;
+    size_t part_floats = 0;
+    unsigned long long* argmax = nullptr;
+    int64_t* tokens = nullptr;
+    int* positions = nullptr;
+    int* seq_lens = nullptr;
+    int64_t* hist = nullptr;
+    int* hist_count = nullptr;
+    int hist_cap = 0;
+
+    // pinned staging
+    int64_t* h_tokens = nullptr;
+    int* h_pos = nullptr;
+    unsigned long long* h_argmax = nullptr;
+    float* h_logits = nullptr;
+
+    std::vector<cudaGraphExec_t> graphs;  // per batch size
+    int splits = 1;
+    int last_B = 0;  // batch of the most recent prefill / decode step
+};
+
+static int model_alloc(b2_model* m, void** p, size_t bytes) {
+    cudaError_t e = cudaMalloc(p, bytes > 0 ? bytes : 16);
+    if (e != cudaSuccess) return (int)e;
+    m->allocs.push_back(*p);
+    return B2_OK;
+}
+
+#define M_ALLOC(ptr, bytes)                                              \
+    do {                                                                 \
+        int rc_ = model_alloc(m, reinterpret_cast<void**>(&(ptr)), (bytes)); \
+        if (rc_ != B2_OK) { b2_model_destroy(m); return rc_; }           \
+    } while (0)
+
+extern "C" int b2_nccl_unique_id(void* out128) {
+    B2_REQUIRE(out128);
+    ncclUniqueId id;
+    if (!nccl().ok || nccl().GetUniqueId(&id) != ncclSuccess) return B2_ERR_NCCL;
+    static_assert(sizeof(ncclUniqueId) == 128, "ncclUniqueId size");
+    memcpy(out128, &id, sizeof(id));
+    return B2_OK;
+}
+
+extern "C" int b2_model_destroy(b2_model* m) {
+    if (!m) return B2_OK;
+    if (m->stream) cudaStreamSynchronize(m->stream);
+    for (auto g : m->graphs)
+        if (g) cudaGraphExecDestroy(g);
+    m->graphs.clear();
+    if (m->comm) nccl().CommDestroy(m->comm);
+    for (void* p : m->allocs) cudaFree(p);
+    cudaFreeHost(m->h_tokens);
+    cudaFreeHost(m->h_pos);
+    cudaFreeHost(m->h_argmax);
+    cudaFreeHost(m->h_logits);
+    if (m->stream) cudaStreamDestroy(m->stream);
+    delete m;
+    return B2_OK;
+}
+
+extern "C" int b2_model_create(const b2_model_config* cfg, int tp_rank, int tp_size, const void* nccl_id,
+                               b2_model** out) {
+    B2_REQUIRE(cfg && out && tp_size >= 1 && tp_rank >= 0 && tp_rank < tp_size);
+    *out = nullptr;
+    const b2_model_config& c = *cfg;
+    B2_REQUIRE(c.vocab_size > 0 && c.hidden_size > 0 && c.intermediate_size > 0 && c.num_layers > 0);
+    B2_REQUIRE(c.num_q_heads > 0 && c.num_kv_heads > 0 && c.num_q_heads % c.num_kv_heads == 0);
+    B2_REQUIRE(c.max_batch >= 1 && c.max_batch <= 8 && c.max_seq >= 1);
+    if (c.num_kv_heads % tp_size || c.intermediate_size % tp_size || c.vocab_size % tp_size) return B2_ERR_UNSUPPORTED;
+    if (!attn_head_dim_supported(c.head_dim) || c.hidden_size % 8 || (c.intermediate_size / tp_size) % 8 ||
+        (c.num_q_heads / tp_size * c.head_dim) % 8)
+        return B2_ERR_UNSUPPORTED;
+    if (tp_size > 1 && !nccl_id) return B2_ERR_INVALID;
+
+    b2_model* m = new (std::nothrow) b2_model();
+    if (!m) return B2_ERR_INVALID;
+    m->cfg = c;
+    m->rank = tp_rank;
+    m->tp = tp_size;
+    cudaGetDevice(&m->device);
+    const int H = c.hidden_size, D = c.head_dim, L = c.num_layers, B = c.max_batch;
+    m->nq = c.num_q_heads / tp_size;
+    m->nkv = c.num_kv_heads / tp_size;
+    m->inter = c.intermediate_size / tp_size;
+    m->vocab_l = c.vocab_size / tp_size;
+    m->vocab_off = tp_rank * m->vocab_l;
+    m->qkv_rows = (m->nq + 2 * m->nkv) * D;
+    {
+        cudaError_t e = cudaStreamCreateWithFlags(&m->stream, cudaStreamNonBlocking);
+        if (e != cudaSuccess) { b2_model_destroy(m); return (int)e; }
+    }
+    if (tp_size > 1) {
+        ncclUniqueId id;
+        memcpy(&id, nccl_id, sizeof(id));
+        if (!nccl().ok || nccl().CommInitRank(&m->comm, tp_size, id, tp_rank) != ncclSuccess) {
+            m->comm = nullptr;
+            b2_model_destroy(m);
+            return B2_ERR_NCCL;
+        }
+    }
+
+    const size_t hs = sizeof(__half);
+    M_ALLOC(m->embed, (size_t)c.vocab_size * H * hs);
+    if (c.tie_word_embeddings) {
+        m->lm_head = m->embed + (size_t)m->vocab_off * H;
+    } else {
+        M_ALLOC(m->lm_head, (size_t)m->vocab_l * H * hs);
+    }
+    M_ALLOC(m->final_norm, (size_t)H * hs);
+    m->layers.resize(L);
+    for (int l = 0; l < L; ++l) {
+        LayerW& w = m->layers[l];
+        M_ALLOC(w.wqkv, (size_t)m->qkv_rows * H * hs);
+        if (c.has_qkv_bias) M_ALLOC(w.bqkv, (size_t)m->qkv_rows * hs);
+        M_ALLOC(w.wo, (size_t)H * m->nq * D * hs);
+        M_ALLOC(w.wg, (size_t)m->inter * H * hs);
+        M_ALLOC(w.wu, (size_t)m->inter * H * hs);
+        M_ALLOC(w.wd, (size_t)H * m->inter * hs);
+        M_ALLOC(w.ln1, (size_t)H * hs);
+        M_ALLOC(w.ln2, (size_t)H * hs);
+    }
+    // KV cache [layer][batch][K/V][kv head][max_seq][D]
+    m->kv_s_head = (int64_t)c.max_seq * D;
+    m->kv_s_kv = m->kv_s_head * m->nkv;
+    m->kv_s_batch = m->kv_s_kv * 2;
+    m->kv_s_layer = m->kv_s_batch * B;
+    M_ALLOC(m->kv, (size_t)m->kv_s_layer * L * hs);
+    {
+        cudaError_t e = cudaMemset(m->kv, 0, (size_t)m->kv_s_layer * L * hs);
+        if (e != cudaSuccess) { b2_model_destroy(m); return (int)e; }
+    }
+    // RoPE table with the reference CPU arithmetic (src/cpu/ops.cpp:174-189)
+    {
+        const int half = D / 2;
+        std::vector<float> inv(half);
+        for (int i = 0; i < half; ++i) inv[i] = 1.0f / powf(c.rope_theta, (float)(2 * i) / (float)D);
+        std::vector<float2> tab((size_t)c.max_seq * half);
+        for (int p = 0; p < c.max_seq; ++p)
+            for (int i = 0; i < half; ++i) {
+                const float a = (float)p * inv[i];
+                tab[(size_t)p * half + i] = make_float2(cosf(a), sinf(a));
+            }
+        M_ALLOC(m->rope, tab.size() * sizeof(float2));
+        cudaError_t e = cudaMemcpy(m->rope, tab.data(), tab.size() * sizeof(float2), cudaMemcpyHostToDevice);
+        if (e != cudaSuccess) { b2_model_destroy(m); return (int)e; }
+    }
+    M_ALLOC(m->hidden, (size_t)B * H * sizeof(float));
+    M_ALLOC(m->q, (size_t)B * m->nq * D * hs);
+    M_ALLOC(m->attn, (size_t)B * m->nq * D * hs);
+    M_ALLOC(m->act, (size_t)B * m->inter * hs);
+    M_ALLOC(m->logits, (size_t)B * m->vocab_l * sizeof(float));
+    if (tp_size > 1) M_ALLOC(m->logits_gather, (size_t)B * c.vocab_size * sizeof(float));
+    m->splits = attn_pick_splits(B, m->nq, m->nkv, D, c.max_seq, (size_t)1 << 40);
+    m->part_floats = attn_scratch_floats(B, m->nq, m->nkv, D, m->splits);
+    M_ALLOC(m->part, m->part_floats * sizeof(float));
+    {   // arrival counters start at zero; the attention kernel resets them after each use
+        cudaError_t e = cudaMemset(m->part, 0, m->part_floats * sizeof(float));
+        if (e != cudaSuccess) { b2_model_destroy(m); return (int)e; }
+    }
+    M_ALLOC(m->argmax, (size_t)B * sizeof(unsigned long long));
+    M_ALLOC(m->tokens, (size_t)B * sizeof(int64_t));
+    M_ALLOC(m->positions, (size_t)B * sizeof(int));
+    M_ALLOC(m->seq_lens, (size_t)B * sizeof(int));
+    m->hist_cap = 4096;
+    M_ALLOC(m->hist, (size_t)m->hist_cap * B * sizeof(int64_t));
+    M_ALLOC(m->hist_count, sizeof(int));
+    {
+        cudaError_t e = cudaMemset(m->tokens, 0, (size_t)B * sizeof(int64_t));
+        if (e == cudaSuccess) e = cudaMemset(m->positions, 0, (size_t)B * sizeof(int));
+        if (e == cudaSuccess) e = cudaMemset(m->hist_count, 0, sizeof(int));
+        if (e == cudaSuccess) e = cudaMallocHost(&m->h_tokens, (size_t)B * sizeof(int64_t));
+        if (e == cudaSuccess) e = cudaMallocHost(&m->h_pos, (size_t)B * sizeof(int));
+        if (e == cudaSuccess) e = cudaMallocHost(&m->h_argmax, (size_t)B * sizeof(unsigned long long));
+        if (e == cudaSuccess) e = cudaMallocHost(&m->h_logits, (size_t)B * c.vocab_size * sizeof(float));
+        if (e != cudaSuccess) { b2_model_destroy(m); return (int)e; }
+    }
+    m->graphs.assign(B + 1, nullptr);
+    *out = m;
+    return B2_OK;
+}
+
+// ---------------------------------------------------------------------------
+// weights
+// ---------------------------------------------------------------------------
+static int init_block(b2_model* m, __half* dst, int64_t rows, int64_t cols, uint64_t seed, uint64_t tid, int64_t row0,
+                      int64_t col0, int64_t ld, float scale) {
+    if (rows <= 0 || cols <= 0) return B2_OK;
+    const int64_t n = rows * cols;
+    int64_t blocks = (n + 255) / 256;
+    if (blocks > (int64_t)sm_count() * 32) blocks = (int64_t)sm_count() * 32;
+    init_tensor_kernel<<<(unsigned)blocks, 256, 0, m->stream>>>(dst, rows, cols, seed, tid, row0, col0, ld, scale);
+    B2_CHECK_LAUNCH();
+    return B2_OK;
+}
+
+static int fill_block(b2_model* m, __half* dst, int64_t n, float v) {
+    int64_t blocks = (n + 255) / 256;
+    if (blocks > 4096) blocks = 4096;
+    fill_half_kernel<<<(unsigned)blocks, 256, 0, m->stream>>>(dst, n, v);
+    B2_CHECK_LAUNCH();
+    return B2_OK;
+}
+
+enum : uint64_t { T_EMBED = 1, T_LM_HEAD = 2, T_FINAL_NORM = 3 };
+static uint64_t layer_tid(int l, int k) { return 16 + 16 * (uint64_t)l + (uint64_t)k; }
+enum { K_WQ = 0, K_WK = 1, K_WV = 2, K_WO = 3, K_WG = 4, K_WU = 5, K_WD = 6, K_LN1 = 7, K_LN2 = 8, K_BQ = 9,
+       K_BK = 10, K_BV = 11 };
+
+#define M_TRY(expr)                       \
+    do {                                  \
+        int rc_ = (expr);                 \
+        if (rc_ != B2_OK) return rc_;     \
+    } while (0)
+
+extern "C" int b2_model_init_random(b2_model* m, uint64_t seed, float stddev) {
+    B2_REQUIRE(m);
+    const b2_model_config& c = m->cfg;
+    const int64_t H = c.hidden_size, D = c.head_dim;
+    const double var1 = (65536.0 * 65536.0 - 1.0) / 12.0;
+    const float scale = (float)((double)stddev / sqrt(4.0 * var1));
+    M_TRY(init_block(m, m->embed, c.vocab_size, H, seed, T_EMBED, 0, 0, H, scale));
+    if (!c.tie_word_embeddings) M_TRY(init_block(m, m->lm_head, m->vocab_l, H, seed, T_LM_HEAD, m->vocab_off, 0, H, scale));
+    M_TRY(fill_block(m, m->final_norm, H, 1.0f));
+    const int64_t qd = (int64_t)m->nq * D, kvd = (int64_t)m->nkv * D;
+    const int64_t qd_g = (int64_t)c.num_q_heads * D, kvd_g = (int64_t)c.num_kv_heads * D;
+    for (int l = 0; l < c.num_layers; ++l) {
+        LayerW& w = m->layers[l];
+        M_TRY(init_block(m, w.wqkv, qd, H, seed, layer_tid(l, K_WQ), m->rank * qd, 0, H, scale));
+        M_TRY(init_block(m, w.wqkv + qd * H, kvd, H, seed, layer_tid(l, K_WK), m->rank * kvd, 0, H, scale));
+        M_TRY(init_block(m, w.wqkv + (qd + kvd) * H, kvd, H, seed, layer_tid(l, K_WV), m->rank * kvd, 0, H, scale));
+        if (w.bqkv) {
+            M_TRY(init_block(m, w.bqkv, 1, qd, seed, layer_tid(l, K_BQ), 0, m->rank * qd, qd_g, scale));
+            M_TRY(init_block(m, w.bqkv + qd, 1, kvd, seed, layer_tid(l, K_BK), 0, m->rank * kvd, kvd_g, scale));
+            M_TRY(init_block(m, w.bqkv + qd + kvd, 1, kvd, seed, layer_tid(l, K_BV), 0, m->rank * kvd, kvd_g, scale));
+        }
+        M_TRY(init_block(m, w.wo, H, qd, seed, layer_tid(l, K_WO), 0, m->rank * qd, qd_g, scale));
+        M_TRY(init_block(m, w.wg, m->inter, H, seed, layer_tid(l, K_WG), (int64_t)m->rank * m->inter, 0, H, scale));
+        M_TRY(init_block(m, w.wu, m->inter, H, seed, layer_tid(l, K_WU), (int64_t)m->rank * m->inter, 0, H, scale));
+        M_TRY(init_block(m, w.wd, H, m->inter, seed, layer_tid(l, K_WD), 0, (int64_t)m->rank * m->inter,
+                         c.intermediate_size, scale));
+        M_TRY(fill_block(m, w.ln1, H, 1.0f));
+        M_TRY(fill_block(m, w.ln2, H, 1.0f));
+    }
+    B2_TRY(cudaStreamSynchronize(m->stream));
+    return B2_OK;
+}
+
+// Copy the [rows, cols] sub-block at (row0, col0) of a host [*, ld] fp16 tensor.
+static int upload_block(b2_model* m, __half* dst, const uint16_t* src, int64_t rows, int64_t cols, int64_t row0,
+                        int64_t col0, int64_t ld) {
+    B2_TRY(cudaMemcpy2DAsync(dst, cols * 2, src + row0 * ld + col0, ld * 2, cols * 2, rows, cudaMemcpyHostToDevice,
+                             m->stream));
+    return B2_OK;
+}
+
+extern "C" int b2_model_set_tensor(b2_model* m, const char* name, const uint16_t* src, int64_t rows, int64_t cols) {
+    B2_REQUIRE(m && name && src);
+    const b2_model_config& c = m->cfg;
+    const int64_t H = c.hidden_size, D = c.head_dim;
+    const int64_t qd = (int64_t)m->nq * D, kvd = (int64_t)m->nkv * D;
+    std::string n(name);
+    int rc = B2_ERR_INVALID;
+    auto shape = [&](int64_t r, int64_t cc) { return rows == r && cols == cc; };
+    if (n == "embed" && shape(c.vocab_size, H)) {
+        rc = upload_block(m, m->embed, src, c.vocab_size, H, 0, 0, H);
+    } else if (n == "lm_head" && shape(c.vocab_size, H) && !c.tie_word_embeddings) {
+        rc = upload_block(m, m->lm_head, src, m->vocab_l, H, m->vocab_off, 0, H);
+    } else if (n == "final_norm" && rows * cols == H) {
+        rc = upload_block(m, m->final_norm, src, 1, H, 0, 0, H);
+    } else {
+        const size_t dot = n.find('.');
+        if (dot == std::string::npos) return B2_ERR_INVALID;
+        const int l = atoi(n.substr(0, dot).c_str());
+        const std::string t = n.substr(dot + 1);
+        if (l < 0 || l >= c.num_layers) return B2_ERR_INVALID;
+        LayerW& w = m->layers[l];
+        const int64_t I = c.intermediate_size;
+        if (t == "ln1" && rows * cols == H) rc = upload_block(m, w.ln1, src, 1, H, 0, 0, H);
+        else if (t == "ln2" && rows * cols == H) rc = upload_block(m, w.ln2, src, 1, H, 0, 0, H);
+        else if (t == "wq" && shape((int64_t)c.num_q_heads * D, H)) rc = upload_block(m, w.wqkv, src, qd, H, m->rank * qd, 0, H);
+        else if (t == "wk" && shape((int64_t)c.num_kv_heads * D, H))
+            rc = upload_block(m, w.wqkv + qd * H, src, kvd, H, m->rank * kvd, 0, H);
+        else if (t == "wv" && shape((int64_t)c.num_kv_heads * D, H))
+            rc = upload_block(m, w.wqkv + (qd + kvd) * H, src, kvd, H, m->rank * kvd, 0, H);
+        else if (t == "bq" && w.bqkv && rows * cols == (int64_t)c.num_q_heads * D)
+            rc = upload_block(m, w.bqkv, src, 1, qd, 0, m->rank * qd, rows * cols);
+        else if (t == "bk" && w.bqkv && rows * cols == (int64_t)c.num_kv_heads * D)
+            rc = upload_block(m, w.bqkv + qd, src, 1, kvd, 0, m->rank * kvd, rows * cols);
+        else if (t == "bv" && w.bqkv && rows * cols == (int64_t)c.num_kv_heads * D)
+            rc = upload_block(m, w.bqkv + qd + kvd, src, 1, kvd, 0, m->rank * kvd, rows * cols);
+        else if (t == "wo" && shape(H, (int64_t)c.num_q_heads * D))
+            rc = upload_block(m, w.wo, src, H, qd, 0, m->rank * qd, (int64_t)c.num_q_heads * D);
+        else if (t == "wg" && shape(I, H)) rc = upload_block(m, w.wg, src, m->inter, H, (int64_t)m->rank * m->inter, 0, H);
+        else if (t == "wu" && shape(I, H)) rc = upload_block(m, w.wu, src, m->inter, H, (int64_t)m->rank * m->inter, 0, H);
+        else if (t == "wd" && shape(H, I)) rc = upload_block(m, w.wd, src, H, m->inter, 0, (int64_t)m->rank * m->inter, I);
+    }
+    if (rc != B2_OK) return rc;
+    B2_TRY(cudaStreamSynchronize(m->stream));
+    return B2_OK;
+}
+
+// ---------------------------------------------------------------------------
+// the decode step
+// ---------------------------------------------------------------------------
+static int nccl_sum_hidden(b2_model* m, int B) {
+    if (m->tp == 1) return B2_OK;
+    if (nccl().AllReduce(m->hidden, m->hidden, (size_t)B * m->cfg.hidden_size, ncclFloat, ncclSum, m->comm, m->stream) !=
+        ncclSuccess)
+        return B2_ERR_NCCL;
+    return B2_OK;
+}
+
+static int launch_qkv(b2_model* m, int l, int B, bool pdl) {
+    const b2_model_config& c = m->cfg;
+    LayerW& w = m->layers[l];
+    __half* kbase = m->kv + (int64_t)l * m->kv_s_layer;
+    GemvParams p = {};
+    p.W = w.wqkv;
+    p.K = c.hidden_size;
+    p.tasks = m->qkv_rows / 2;
+    p.B = B;
+    p.x = m->hidden;
+    p.ldx = c.hidden_size;
+    p.norm_w = w.ln1;
+    p.eps = c.rms_norm_eps;
+    p.bias = w.bqkv;
+    p.y = m->q;
+    p.ldy = (int64_t)m->nq * c.head_dim;
+    p.nq = m->nq;
+    p.nkv = m->nkv;
+    p.D = c.head_dim;
+    p.rope = m->rope;
+    p.pos = m->positions;
+    p.kcache = kbase;
+    p.vcache = kbase + m->kv_s_kv;
+    p.kv_sb = m->kv_s_batch;
+    p.kv_sh = m->kv_s_head;
+    return gemv_launch(p, X_NORM, OUT_QKV, m->stream, pdl);
+}
+
+static int launch_attn(b2_model* m, int l, int B, bool pdl) {
+    const int D = m->cfg.head_dim;
+    __half* kbase = m->kv + (int64_t)l * m->kv_s_layer;
+    return attn_decode_launch_model(m->q, kbase, kbase + m->kv_s_kv, m->kv_s_batch, m->kv_s_head, D, m->seq_lens,
+                                    m->attn, m->part, m->splits, B, m->nq, m->nkv, D, m->stream, pdl);
+}
+
+static int launch_o(b2_model* m, int l, int B, bool pdl) {
+    const b2_model_config& c = m->cfg;
+    GemvParams p = {};
+    p.W = m->layers[l].wo;
+    p.K = m->nq * c.head_dim;
+    p.tasks = c.hidden_size;
+    p.B = B;
+    p.x = m->attn;
+    p.ldx = (int64_t)m->nq * c.head_dim;
+    p.resid_add = m->rank == 0 ? 1 : 0;
+    p.y = m->hidden;
+    p.ldy = c.hidden_size;
+    return gemv_launch(p, X_HALF, OUT_RESID, m->stream, pdl);
+}
+
+static int launch_gateup(b2_model* m, int l, int B, bool pdl) {
+    const b2_model_config& c = m->cfg;
+    LayerW& w = m->layers[l];
+    GemvParams p = {};
+    p.W = w.wg;
+    p.W2 = w.wu;
+    p.K = c.hidden_size;
+    p.tasks = m->inter;
+    p.B = B;
+    p.x = m->hidden;
+    p.ldx = c.hidden_size;
+    p.norm_w = w.ln2;
+    p.eps = c.rms_norm_eps;
+    p.y = m->act;
+    p.ldy = m->inter;
+    return gemv_launch(p, X_NORM, OUT_SWIGLU, m->stream, pdl);
+}
+
+static int launch_down(b2_model* m, int l, int B, bool pdl) {
+    const b2_model_config& c = m->cfg;
+    GemvParams p = {};
+    p.W = m->layers[l].wd;
+    p.K = m->inter;
+    p.tasks = c.hidden_size;
+    p.B = B;
+    p.x = m->act;
+    p.ldx = m->inter;
+    p.resid_add = m->rank == 0 ? 1 : 0;
+    p.y = m->hidden;
+    p.ldy = c.hidden_size;
+    return gemv_launch(p, X_HALF, OUT_RESID, m->stream, pdl);
+}
+
+static int launch_lm_head(b2_model* m, int B, bool pdl) {
+    const b2_model_config& c = m->cfg;
+    GemvParams p = {};
+    p.W = m->lm_head;
+    p.K = c.hidden_size;
+    p.tasks = m->vocab_l;
+    p.B = B;
+    p.x = m->hidden;
+    p.ldx = c.hidden_size;
+    p.norm_w = m->final_norm;
+    p.eps = c.rms_norm_eps;
+    p.y = m->logits;
+    p.ldy = m->vocab_l;
+    p.argmax = m->argmax;
+    p.row_offset = m->vocab_off;
+    p.argmax_limit = c.vocab_size > 151665 ? 151665 : c.vocab_size;
+    return gemv_launch(p, X_NORM, OUT_LOGITS, m->stream, pdl);
+}
+
+// Issue every launch of one decode step for B sequences on m->stream.
+static int enqueue_step(b2_model* m, int B) {
+    const b2_model_config& c = m->cfg;
+    cudaStream_t s = m->stream;
+    const bool pdl = true;
+    B2_TRY(launch(step_begin_kernel, dim3(B), dim3(256), 0, s, pdl, (const int64_t*)m->tokens,
+                  (const int*)m->positions, (const __half*)m->embed, m->hidden, c.hidden_size, m->seq_lens, m->argmax,
+                  m->hist, (const int*)m->hist_count, m->hist_cap));
+    for (int l = 0; l < c.num_layers; ++l) {
+        M_TRY(launch_qkv(m, l, B, pdl));
+        M_TRY(launch_attn(m, l, B, pdl));
+        M_TRY(launch_o(m, l, B, pdl));
+        M_TRY(nccl_sum_hidden(m, B));
+        M_TRY(launch_gateup(m, l, B, pdl));
+        M_TRY(launch_down(m, l, B, pdl));
+        M_TRY(nccl_sum_hidden(m, B));
+    }
+    M_TRY(launch_lm_head(m, B, pdl));
+    if (m->tp > 1) {
+        if (nccl().AllReduce(m->argmax, m->argmax, (size_t)B, ncclUint64, ncclMax, m->comm, s) != ncclSuccess)
+            return B2_ERR_NCCL;
+    }
+    B2_TRY(launch(step_end_kernel, dim3(1), dim3(32), 0, s, pdl, (const unsigned long long*)m->argmax, m->tokens,
+                  m->positions, B, m->hist_count, m->hist_cap));
+    return B2_OK;
+}
+
+static int ensure_graph(b2_model* m, int B) {
+    if (m->graphs[B]) return B2_OK;
+    cudaGraph_t g = nullptr;
+    B2_TRY(cudaStreamBeginCapture(m->stream, cudaStreamCaptureModeThreadLocal));
+    const int rc = enqueue_step(m, B);
+    cudaError_t e = cudaStreamEndCapture(m->stream, &g);
+    if (rc != B2_OK) {
+        if (g) cudaGraphDestroy(g);
+        return rc;
+    }
+    if (e != cudaSuccess) return (int)e;
+    cudaGraphExec_t ex = nullptr;
+    e = cudaGraphInstantiate(&ex, g, 0);
+    cudaGraphDestroy(g);
+    if (e != cudaSuccess) return (int)e;
+    m->graphs[B] = ex;
+    return B2_OK;
+}
+
+static int run_step(b2_model* m, int B) {
+    static int use_graph = -1;
+    if (use_graph < 0) {
+        const char* e = getenv("B2_GRAPH");
+        use_graph = (e && e[0] == '0') ? 0 : 1;
+    }
+    if (!use_graph) return enqueue_step(m, B);
+    M_TRY(ensure_graph(m, B));
+    B2_TRY(cudaGraphLaunch(m->graphs[B], m->stream));
+    return B2_OK;
+}
+
+extern "C" int b2_model_reset(b2_model* m) {
+    B2_REQUIRE(m);
+    B2_TRY(cudaMemsetAsync(m->positions, 0, (size_t)m->cfg.max_batch * sizeof(int), m->stream));
+    B2_TRY(cudaMemsetAsync(m->hist_count, 0, sizeof(int), m->stream));
+    B2_TRY(cudaStreamSynchronize(m->stream));
+    return B2_OK;
+}
+
+static int copy_logits_out(b2_model* m, int B, float* host_logits) {
+    const int V = m->cfg.vocab_size;
+    if (m->tp == 1) {
+        B2_TRY(cudaMemcpyAsync(m->h_logits, m->logits, (size_t)B * V * sizeof(float), cudaMemcpyDeviceToHost, m->stream));
+        B2_TRY(cudaStreamSynchronize(m->stream));
+        memcpy(host_logits, m->h_logits, (size_t)B * V * sizeof(float));
+        return B2_OK;
+    }
+    const size_t nl = (size_t)B * m->vocab_l;
+    if (nccl().AllGather(m->logits, m->logits_gather, nl, ncclFloat, m->comm, m->stream) != ncclSuccess) return B2_ERR_NCCL;
+    B2_TRY(cudaMemcpyAsync(m->h_logits, m->logits_gather, nl * m->tp * sizeof(float), cudaMemcpyDeviceToHost, m->stream));
+    B2_TRY(cudaStreamSynchronize(m->stream));
+    for (int r = 0; r < m->tp; ++r)
+        for (int b = 0; b < B; ++b)
+            memcpy(host_logits + (size_t)b * V + (size_t)r * m->vocab_l, m->h_logits + r * nl + (size_t)b * m->vocab_l,
+                   (size_t)m->vocab_l * sizeof(float));
+    return B2_OK;
+}
+
+static int read_next(b2_model* m, int B, int64_t* host_next) {
+    B2_TRY(cudaMemcpyAsync(m->h_tokens, m->tokens, (size_t)B * sizeof(int64_t), cudaMemcpyDeviceToHost, m->stream));
+    B2_TRY(cudaStreamSynchronize(m->stream));
+    memcpy(host_next, m->h_tokens, (size_t)B * sizeof(int64_t));
+    return B2_OK;
+}
+
+extern "C" int b2_model_decode_step(b2_model* m, const int64_t* host_tokens, const int* host_positions, int B,
+                                    float* host_logits, int64_t* host_next) {
+    B2_REQUIRE(m && host_tokens && host_positions && B >= 1 && B <= m->cfg.max_batch);
+    for (int b = 0; b < B; ++b) {
+        if (host_positions[b] < 0 || host_positions[b] >= m->cfg.max_seq) return B2_ERR_INVALID;
+        if (host_tokens[b] < 0 || host_tokens[b] >= m->cfg.vocab_size) return B2_ERR_INVALID;
+    }
+    memcpy(m->h_tokens, host_tokens, (size_t)B * sizeof(int64_t));
+    memcpy(m->h_pos, host_positions, (size_t)B * sizeof(int));
+    B2_TRY(cudaMemcpyAsync(m->tokens, m->h_tokens, (size_t)B * sizeof(int64_t), cudaMemcpyHostToDevice, m->stream));
+    B2_TRY(cudaMemcpyAsync(m->positions, m->h_pos, (size_t)B * sizeof(int), cudaMemcpyHostToDevice, m->stream));
+    M_TRY(run_step(m, B));
+    m->last_B = B;
+    if (host_logits) M_TRY(copy_logits_out(m, B, host_logits));
+    if (host_next) M_TRY(read_next(m, B, host_next));
+    B2_TRY(cudaStreamSynchronize(m->stream));
+    return B2_OK;
+}
+
+extern "C" int b2_model_prefill(b2_model* m, const int64_t* host_ids, int B, int S, float* host_logits) {
+    B2_REQUIRE(m && host_ids && B >= 1 && B <= m->cfg.max_batch && S >= 1 && S <= m->cfg.max_seq);
+    for (int64_t i = 0; i < (int64_t)B * S; ++i)
+        if (host_ids[i] < 0 || host_ids[i] >= m->cfg.vocab_size) return B2_ERR_INVALID;
+    // prompt ids as [S][B] int64 and positions [S][B] on the device, one step per prompt position
+    int64_t* d_ids = nullptr;
+    int* d_pos = nullptr;
+    B2_TRY(cudaMalloc(&d_ids, (size_t)S * B * sizeof(int64_t)));
+    cudaError_t e = cudaMalloc(&d_pos, (size_t)S * B * sizeof(int));
+    if (e != cudaSuccess) { cudaFree(d_ids); return (int)e; }
+    std::vector<int64_t> ids((size_t)S * B);
+    std::vector<int> pos((size_t)S * B);
+    for (int t = 0; t < S; ++t)
+        for (int b = 0; b < B; ++b) {
+            ids[(size_t)t * B + b] = host_ids[(size_t)b * S + t];
+            pos[(size_t)t * B + b] = t;
+        }
+    int rc = B2_OK;
+    e = cudaMemcpyAsync(d_ids, ids.data(), ids.size() * sizeof(int64_t), cudaMemcpyHostToDevice, m->stream);
+    if (e == cudaSuccess) e = cudaMemcpyAsync(d_pos, pos.data(), pos.size() * sizeof(int), cudaMemcpyHostToDevice, m->stream);
+    if (e == cudaSuccess) e = cudaMemsetAsync(m->hist_count, 0, sizeof(int), m->stream);
+    for (int t = 0; t < S && e == cudaSuccess && rc == B2_OK; ++t) {
+        e = cudaMemcpyAsync(m->tokens, d_ids + (size_t)t * B, B * sizeof(int64_t), cudaMemcpyDeviceToDevice, m->stream);
+        if (e == cudaSuccess)
+            e = cudaMemcpyAsync(m->positions, d_pos + (size_t)t * B, B * sizeof(int), cudaMemcpyDeviceToDevice, m->stream);
+        if (e == cudaSuccess) rc = run_step(m, B);
+    }
+    if (e == cudaSuccess && rc == B2_OK) m->last_B = B;
+    if (e == cudaSuccess && rc == B2_OK && host_logits) rc = copy_logits_out(m, B, host_logits);
+    cudaError_t e2 = cudaStreamSynchronize(m->stream);
+    cudaFree(d_ids);
+    cudaFree(d_pos);
+    if (e != cudaSuccess) return (int)e;
+    if (rc != B2_OK) return rc;
+    if (e2 != cudaSuccess) return (int)e2;
+    return B2_OK;
+}
+
+extern "C" int b2_model_generate_greedy(b2_model* m, int steps, int64_t* host_tokens_out) {
+    B2_REQUIRE(m && steps >= 0);
+    if (m->last_B <= 0) return B2_ERR_STATE;
+    const int B = m->last_B;
+    if (host_tokens_out && steps > m->hist_cap) return B2_ERR_INVALID;
+    B2_TRY(cudaMemsetAsync(m->hist_count, 0, sizeof(int), m->stream));
+    for (int i = 0; i < steps; ++i) M_TRY(run_step(m, B));
+    if (host_tokens_out && steps > 0) {
+        B2_TRY(cudaMemcpyAsync(host_tokens_out, m->hist, (size_t)steps * B * sizeof(int64_t), cudaMemcpyDeviceToHost,
+                               m->stream));
+        B2_TRY(cudaStreamSynchronize(m->stream));
+    }
+    return B2_OK;
+}
+
+extern "C" int b2_model_sync(b2_model* m) {
+    B2_REQUIRE(m);
+    B2_TRY(cudaStreamSynchronize(m->stream));
+    return B2_OK;
+}
+
+extern "C" void* b2_model_stream(b2_model* m) { return m ? (void*)m->stream : nullptr; }
+
+extern "C" void* b2_model_buffer(b2_model* m, const char* name) {
+    if (!m || !name) return nullptr;
+    std::string n(name);
+    if (n == "logits") return m->logits;
+    if (n == "hidden") return m->hidden;
+    if (n == "kv") return m->kv;
+    if (n == "tokens") return m->tokens;
+    if (n == "positions") return m->positions;
+    if (n == "history") return m->hist;
+    if (n == "history_count") return m->hist_count;
+    return nullptr;
+}
+
+extern "C" int b2_model_read(b2_model* m, const char* name, void* dst, size_t offset, size_t bytes) {
+    B2_REQUIRE(m && name && dst);
+    char* src = static_cast<char*>(b2_model_buffer(m, name));
+    B2_REQUIRE(src);
+    B2_TRY(cudaStreamSynchronize(m->stream));
+    B2_TRY(cudaMemcpy(dst, src + offset, bytes, cudaMemcpyDeviceToHost));
+    return B2_OK;
+}
+
+extern "C" int b2_model_kv_layout(const b2_model* m, int64_t* sl, int64_t* sb, int64_t* skv, int64_t* sh, int64_t* sp) {
+    B2_REQUIRE(m && sl && sb && skv && sh && sp);
+    *sl = m->kv_s_layer;
+    *sb = m->kv_s_batch;
+    *skv = m->kv_s_kv;
+    *sh = m->kv_s_head;
+    *sp = m->cfg.head_dim;
+    return B2_OK;
+}
+
+extern "C" double b2_model_step_bytes(const b2_model* m, int B, int ctx) {
+    if (!m) return 0.0;
+    const b2_model_config& c = m->cfg;
+    const double H = c.hidden_size, D = c.head_dim, L = c.num_layers;
+    const double lin = L * ((double)m->qkv_rows * H + H * m->nq * D + 2.0 * m->inter * H + H * m->inter) +
+                       (double)m->vocab_l * H;
+    double bytes = 2.0 * lin;
+    if (c.has_qkv_bias) bytes += 2.0 * L * m->qkv_rows;
+    bytes += 2.0 * B * H;                               // embedding rows
+    bytes += 2.0 * (2.0 * L + 1.0) * H;                 // norm weights
+    bytes += (double)B * L * 2.0 * m->nkv * D * 2.0 * ctx;  // KV read
+    bytes += (double)B * L * 2.0 * m->nkv * D * 2.0;        // KV write
+    bytes += 4.0 * B * m->vocab_l;                      // logits
+    return bytes;
+}
+
+extern "C" int b2_model_time_kernel(b2_model* m, int kind, int B, int reps, float* avg_ms) {
+    B2_REQUIRE(m && avg_ms && B >= 1 && B <= m->cfg.max_batch && reps >= 1 && kind >= 0 && kind <= 5);
+    const int L = m->cfg.num_layers;
+    auto one = [&](int l) -> int {
+        switch (kind) {
+            case 0: return launch_qkv(m, l, B, true);
+            case 1: return launch_attn(m, l, B, true);
+            case 2: return launch_o(m, l, B, true);
+            case 3: return launch_gateup(m, l, B, true);
+            case 4: return launch_down(m, l, B, true);
+            default: return launch_lm_head(m, B, true);
+        }
+    };
+    // warm-up pass
+    for (int l = 0; l < L; ++l) M_TRY(one(l));
+    cudaEvent_t e0, e1;
+    B2_TRY(cudaEventCreate(&e0));
+    B2_TRY(cudaEventCreate(&e1));
+    B2_TRY(cudaEventRecord(e0, m->stream));
+    int n = 0;
+    for (int r = 0; r < reps; ++r)
+        for (int l = 0; l < L; ++l, ++n) M_TRY(one(l));
+    B2_TRY(cudaEventRecord(e1, m->stream));
+    B2_TRY(cudaEventSynchronize(e1));
+    float ms = 0.f;
+    B2_TRY(cudaEventElapsedTime(&ms, e0, e1));
+    cudaEventDestroy(e0);
+    cudaEventDestroy(e1);
+    *avg_ms = ms / (float)n;
+    return B2_OK;
+}
+
+extern "C" double b2_model_kernel_bytes(const b2_model* m, int kind, int B, int ctx) {
+    if (!m) return 0.0;
+    const b2_model_config& c = m->cfg;
+    const double H = c.hidden_size, D = c.head_dim;
+    switch (kind) {
+        case 0: return 2.0 * m->qkv_rows * H + 4.0 * B * H + 2.0 * H + 2.0 * B * m->qkv_rows;
+        case 1: return 2.0 * B * m->nkv * D * 2.0 * ctx + 2.0 * 2.0 * B * m->nq * D;
+        case 2: return 2.0 * H * m->nq * D + 2.0 * B * m->nq * D + 8.0 * B * H;
+        case 3: return 2.0 * 2.0 * m->inter * H + 4.0 * B * H + 2.0 * H + 2.0 * B * m->inter;
+        case 4: return 2.0 * H * m->inter + 2.0 * B * m->inter + 8.0 * B * H;
+        default: return 2.0 * m->vocab_l * H + 4.0 * B * H + 2.0 * H + 4.0 * B * m->vocab_l;
+    }
+}
+
+extern "C" int b2_model_step_launches(const b2_model* m, int B) {
+    if (!m) return 0;
+    // step_begin, per layer {qkv, attention (merges its own splits), o, gateup, down}, lm_head, step_end
+    return 3 + m->cfg.num_layers * 5;
+}

@@ -1,0 +1,202 @@
+"""Decode path end to end vs the CPU oracle (the reference's forward_cpu
+restated, full recompute, fp32 with fp16-rounded weights).
+
+Weights come from the seeded generator, which produces bit-identical fp16
+tensors on the device (b2_model_init_random) and in the oracle
+(oracle.seeded_weights).  Criteria:
+  * logits within max-abs 2e-2 and cosine >= 0.9999 at every position;
+  * greedy tokens equal the oracle's argmax, except where the oracle's top-1 /
+    top-2 margin is below 0.05 (the reference's near-tie rule, docs/GATES.md);
+  * KV-cache indexing bit-exact.
+"""
+import numpy as np
+import pytest
+
+import b2engine as b2
+import oracle as O
+
+pytestmark = pytest.mark.gpu
+
+LOGIT_TOL = 2e-2
+COS_TOL = 0.9999
+TIE_MARGIN = 0.05
+
+
+def make_model(cfg: O.Config, seed: int, max_batch=1, max_seq=256):
+    m = b2.Model(cfg.vocab, cfg.hidden, cfg.inter, cfg.layers, cfg.nq, cfg.nkv, cfg.head_dim, eps=cfg.eps,
+                 theta=cfg.theta, tied=cfg.tied, bias=cfg.has_bias, max_batch=max_batch, max_seq=max_seq)
+    m.init_random(seed, 0.02)
+    return m
+
+
+def check_logits(gpu, ref, where=""):
+    gpu = np.asarray(gpu, np.float64).reshape(-1)
+    ref = np.asarray(ref, np.float64).reshape(-1)
+    d = float(np.max(np.abs(gpu - ref)))
+    cos = float(gpu @ ref / (np.linalg.norm(gpu) * np.linalg.norm(ref) + 1e-30))
+    assert d <= LOGIT_TOL and cos >= COS_TOL, f"{where}: max-abs {d:.3g} cos {cos:.7f}"
+    return d, cos
+
+
+def check_greedy(tokens, ref_logits, where=""):
+    """tokens[i] must be argmax(ref_logits[i]) unless that row is a near tie."""
+    for i, t in enumerate(tokens):
+        row = ref_logits[i]
+        top = int(np.argmax(row))
+        if t != top:
+            s = np.sort(row)[::-1]
+            assert s[0] - s[1] < TIE_MARGIN, f"{where} step {i}: gpu {t} oracle {top} margin {s[0] - s[1]:.4f}"
+
+
+SMALL = O.Config(vocab=1000, hidden=256, inter=704, layers=2, nq=8, nkv=2, head_dim=32, theta=10000.0)
+
+
+def run_teacher_forced(cfg, seed, prompt, cont, max_seq=256):
+    m = make_model(cfg, seed, max_seq=max_seq)
+    W = O.seeded_weights(cfg, seed)
+    S0 = len(prompt)
+    seq = np.concatenate([prompt, cont]).astype(np.int64)
+    ref = O.forward(cfg, W, seq, logit_row0=S0 - 1)
+    lg = m.prefill(prompt[None, :])
+    check_logits(lg[0], ref[0], "prefill")
+    for i, t in enumerate(cont):
+        lg, _ = m.decode_step([t], [S0 + i])
+        check_logits(lg[0], ref[i + 1], f"decode {i}")
+    m.close()
+
+
+def test_small_llama_teacher_forced(cuda):
+    rng = np.random.default_rng(7)
+    prompt = rng.integers(0, SMALL.vocab, 13)
+    cont = rng.integers(0, SMALL.vocab, 11)
+    run_teacher_forced(SMALL, 1234, prompt, cont)
+
+
+def test_tied_with_bias(cuda):
+    cfg = O.Config(vocab=512, hidden=128, inter=352, layers=2, nq=4, nkv=4, head_dim=32, theta=1e6, tied=True,
+                   has_bias=True, eps=1e-6)
+    rng = np.random.default_rng(8)
+    run_teacher_forced(cfg, 99, rng.integers(0, cfg.vocab, 9), rng.integers(0, cfg.vocab, 6))
+
+
+def test_head_dim_64_and_128(cuda):
+    for D, nq, nkv in [(64, 4, 1), (128, 4, 2)]:
+        cfg = O.Config(vocab=300, hidden=nq * D, inter=512, layers=1, nq=nq, nkv=nkv, head_dim=D, theta=5e5)
+        rng = np.random.default_rng(D)
+        run_teacher_forced(cfg, 5 + D, rng.integers(0, cfg.vocab, 7), rng.integers(0, cfg.vocab, 5))
+
+
+def test_greedy_generation_matches_oracle(cuda):
+    cfg = SMALL
+    rng = np.random.default_rng(11)
+    prompt = rng.integers(0, cfg.vocab, 10)
+    m = make_model(cfg, 4321)
+    m.prefill(prompt[None, :], want_logits=False)
+    steps = 24
+    gen = m.generate_greedy(steps)[:, 0]
+    # the first generated id comes from the prefill's last position
+    W = O.seeded_weights(cfg, 4321)
+    seq = np.concatenate([prompt, gen[:-1]]).astype(np.int64)
+    ref = O.forward(cfg, W, seq, logit_row0=len(prompt) - 1)
+    check_greedy(gen, ref, "greedy")
+    m.close()
+
+
+def test_batched_decode_matches_single(cuda):
+    cfg = SMALL
+    B = 3
+    rng = np.random.default_rng(12)
+    prompts = rng.integers(0, cfg.vocab, (B, 8))
+    conts = rng.integers(0, cfg.vocab, (B, 5))
+    m = make_model(cfg, 777, max_batch=B)
+    W = O.seeded_weights(cfg, 777)
+    lg = m.prefill(prompts)
+    refs = [O.forward(cfg, W, np.concatenate([prompts[b], conts[b]]), logit_row0=7) for b in range(B)]
+    for b in range(B):
+        check_logits(lg[b], refs[b][0], f"prefill b{b}")
+    for i in range(conts.shape[1]):
+        lg, _ = m.decode_step(conts[:, i], [8 + i] * B)
+        for b in range(B):
+            check_logits(lg[b], refs[b][i + 1], f"decode {i} b{b}")
+    m.close()
+
+
+def test_kv_cache_indexing_bit_exact(cuda):
+    """V rows land in [layer][batch][V][head][pos][d] exactly.
+
+    Embedding rows are +-1 so the RMSNorm output is exactly +-1 in fp16, W_v
+    selects hidden dims one-hot, and W_o = W_down = 0 keep the residual stream
+    equal to the embedding in every layer: each V cache row must then equal the
+    selected signs of the token at that position, bit for bit, and every other
+    slot must stay zero."""
+    V, H, L, nq, nkv, D, I, B, MS = 64, 64, 2, 2, 2, 16, 64, 2, 40
+    m = b2.Model(V, H, I, L, nq, nkv, D, max_batch=B, max_seq=MS)
+    m.init_random(1, 0.02)
+    rng = np.random.default_rng(3)
+    emb = np.where(rng.random((V, H)) < 0.5, -1.0, 1.0).astype(np.float16)
+    m.set_tensor("embed", emb)
+    sel = rng.permutation(H)[: nkv * D]
+    wv = np.zeros((nkv * D, H), np.float16)
+    wv[np.arange(nkv * D), sel] = 1.0
+    for l in range(L):
+        m.set_tensor(f"{l}.wv", wv)
+        m.set_tensor(f"{l}.wo", np.zeros((H, nq * D), np.float16))
+        m.set_tensor(f"{l}.wd", np.zeros((H, I), np.float16))
+    S = 9
+    ids = rng.integers(0, V, (B, S))
+    m.prefill(ids, want_logits=False)
+    extra = rng.integers(0, V, B)
+    m.decode_step(extra, [S] * B, want_logits=False)
+    sl, sb, skv, sh, sp = m.kv_layout()
+    assert (sb, skv, sh, sp) == (2 * nkv * MS * D, nkv * MS * D, MS * D, D) and sl == B * sb
+    host = m.read("kv", np.float16, sl * L)
+    cache = host.reshape(L, B, 2, nkv, MS, D)
+    seqs = np.concatenate([ids, extra[:, None]], axis=1)
+    for l in range(L):
+        for b in range(B):
+            for h in range(nkv):
+                for p in range(MS):
+                    row = cache[l, b, 1, h, p]
+                    if p <= S:
+                        want = emb[seqs[b, p], sel[h * D:(h + 1) * D]]
+                        assert np.array_equal(row.view(np.uint16), want.view(np.uint16)), (l, b, h, p)
+                    else:
+                        assert not np.any(row.view(np.uint16)), (l, b, h, p)
+                        assert not np.any(cache[l, b, 0, h, p].view(np.uint16))
+    m.close()
+
+
+def _full_width_check(cfg, seed, S0, n_dec, max_seq=128):
+    rng = np.random.default_rng(seed)
+    prompt = rng.integers(0, cfg.vocab, S0)
+    m = make_model(cfg, seed, max_seq=max_seq)
+    lg0 = m.prefill(prompt[None, :])
+    gen = m.generate_greedy(n_dec)[:, 0]
+    W = O.seeded_weights(cfg, seed)
+    seq = np.concatenate([prompt, gen[:-1]]).astype(np.int64)
+    ref = O.forward(cfg, W, seq, logit_row0=S0 - 1)
+    check_logits(lg0[0], ref[0], "prefill")
+    check_greedy(gen, ref, "greedy")
+    # teacher-forced logits for the first generated positions
+    m.reset()
+    m.prefill(prompt[None, :], want_logits=False)
+    for i in range(min(4, n_dec - 1)):
+        lg, _ = m.decode_step([gen[i]], [S0 + i])
+        check_logits(lg[0], ref[i + 1], f"decode {i}")
+    m.close()
+
+
+@pytest.mark.slow
+def test_tinyllama_full_width_reduced_depth(cuda):
+    """TinyLlama-1.1B widths (H 2048, 32/4 heads, D 64, FFN 5632, vocab 32000,
+    theta 1e4) at 4 layers."""
+    cfg = O.Config(vocab=32000, hidden=2048, inter=5632, layers=4, nq=32, nkv=4, head_dim=64, theta=10000.0)
+    _full_width_check(cfg, 2024, 24, 16)
+
+
+@pytest.mark.slow
+def test_llama8b_full_width_reduced_depth(cuda):
+    """Llama-3-8B widths (H 4096, 32/8 heads, D 128, FFN 14336, vocab 128256,
+    theta 5e5) at 2 layers."""
+    cfg = O.Config(vocab=128256, hidden=4096, inter=14336, layers=2, nq=32, nkv=8, head_dim=128, theta=500000.0)
+    _full_width_check(cfg, 88, 16, 8)
