@@ -12,7 +12,7 @@
  *   - against the known-answer cases of the reference's tests/test_cpu_ops.cpp
  *     (restated in tests/test_oracle.py), and
  *   - against the reference's own src/cpu + forward_cpu compiled from its
- *     sources into oracle/_ref (tests/test_oracle_vs_ref.py), with committed
+ *     sources into oracle/_ref (tests/test_oracle.py), with committed
  *     golden vectors under tests/golden generated from that build.
  *
  * Every function keeps the reference's accumulation order (double partial sums
