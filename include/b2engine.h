@@ -107,6 +107,24 @@ int b2_decode_gqa_split(const void* q, b2_kv_view k_view, b2_kv_view v_view, con
                         int max_seq_len, float* split_buffer, size_t split_buffer_floats,
                         void* stream);
 
+/* b2_decode_gqa_split for callers that cannot allocate device memory (code
+ * running inside an allocator or memory-pool callback, plugin hosts that own
+ * every device byte, hot paths that must avoid allocator locks).  It has no
+ * counterpart in the reference.  Same arguments and result as
+ * b2_decode_gqa_split minus the scratch buffer: the partial results live in a
+ * fixed 4 MiB array inside the library's device image, which every GPU that
+ * loads the library keeps until the process exits.  The call allocates
+ * nothing.  Limit: the partial results for the split count the shape prefers
+ * must fit in 4 MiB (every head_dim <= 128 configuration does); larger
+ * problems return B2_ERR_WORKSPACE.  The first call on a device looks up the
+ * array's device address (with that device current); make that first call
+ * before any stream capture.  All calls on one device share the array, so
+ * calls that overlap on the GPU race; the arrival counters in it are cleared
+ * by each call. */
+int b2_decode_gqa_split_noalloc(const void* q, b2_kv_view k_view, b2_kv_view v_view, const int* seq_lens,
+                                void* out, int batch_size, int num_q_heads, int num_kv_heads, int head_dim,
+                                int max_seq_len, void* stream);
+
 /* Causal GQA prefill attention, q/out [B,S,nq,D], k/v [B,S,nkv,D], half.
  * Replaces engine::cuda::flash_prefill_gqa (src/cuda/kernels.h:136-147). */
 int b2_flash_prefill_gqa(const void* q, const void* k, const void* v, void* out, int64_t seq_len,

@@ -54,6 +54,7 @@ _SIGS = {
     "b2_softmax": (i32, [vp, vp, i64, i64, vp]),
     "b2_decode_gqa": (i32, [vp, vp, vp, vp, i32, i32, i32, i32, i32, vp]),
     "b2_decode_gqa_split": (i32, [vp, KVView, KVView, vp, vp, i32, i32, i32, i32, i32, vp, C.c_size_t, vp]),
+    "b2_decode_gqa_split_noalloc": (i32, [vp, KVView, KVView, vp, vp, i32, i32, i32, i32, i32, vp]),
     "b2_flash_prefill_gqa": (i32, [vp, vp, vp, vp, i64, i32, i32, i32, i32, vp]),
     "b2_swiglu": (i32, [vp, vp, vp, i64, vp]),
     "b2_matmul_transB": (i32, [vp, vp, vp, i32, i32, i32, vp]),
