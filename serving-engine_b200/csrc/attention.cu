@@ -15,12 +15,19 @@
 //
 // The grid carries the maximum split count, fixed on the host from
 // max_seq_len (so a captured graph stays valid as the context grows); each
-// CTA derives the live split count from seq_lens[b] on the device (at least
-// kMinChunk positions per split) and idle splits exit at once.  The splits of
-// one (sequence, kv head) are merged by whichever CTA finishes last: every
-// CTA publishes its partial, fences, and bumps a per-(sequence, kv head)
-// counter; the CTA that sees the final count merges all partials from L2 and
-// resets the counter to zero, so no second kernel is launched.
+// CTA derives the live split count from seq_lens[b] on the device (a split
+// covers at least one iteration of all its warps) and idle splits exit at
+// once.  The splits of one (sequence, kv head) are merged by whichever CTA
+// finishes last: every CTA publishes its partial, fences, and bumps a
+// per-(sequence, kv head) counter; the CTA that sees the final count stages
+// the normalised split weights in shared memory, sums the partials from L2
+// with independent loads and resets the counter to zero, so no second kernel
+// is launched.
+//
+// In the decode step each warp requests its first tile of K/V rows older
+// than the newest position before it waits on the q|k|v kernel that precedes
+// it (those rows were written by earlier steps), so that DRAM latency
+// overlaps the previous kernel's tail.
 //
 // Reference replaced: src/cuda/decode_attention_split.cu:28-214 (one CTA per
 // (q head, sequence), head_dim fixed at 64, no split and no combine) and
@@ -48,10 +55,16 @@ struct AttnParams {
     int splits;     // maximum splits (grid.x)
     int nq, nkv, group, hg;
     float scale_log2;
+    // Decode-step form only: seq_lens and every K/V row except the newest
+    // (position seq_len - 1, written by the kernel just before) were written
+    // at least two kernels earlier, so they may be read before the
+    // programmatic-launch wait.
+    int early_kv;
 };
 
 constexpr int kAttnWarps = 4;
-constexpr int kMinChunk = 64;  // positions per split at least
+constexpr int kAttnThreads = kAttnWarps * 32;
+constexpr int kMaxSplits = 128;
 
 template <int C8>
 struct LaneMap {
@@ -60,14 +73,16 @@ struct LaneMap {
 };
 
 template <int D, int G>
-__global__ void __launch_bounds__(kAttnWarps * 32) attn_decode_kernel(const AttnParams p) {
+__global__ void __launch_bounds__(kAttnThreads) attn_decode_kernel(const AttnParams p) {
     constexpr int C8 = D / 8;
     constexpr int LP = LaneMap<C8>::LP;
     constexpr int PPW = LaneMap<C8>::PPW;
     constexpr int UNR = G <= 4 ? 4 : 2;
-    constexpr int WT = PPW * UNR;
+    constexpr int WT = PPW * UNR;             // positions one warp covers per iteration
+    constexpr int kMinChunk = kAttnWarps * WT;  // a split is at least one CTA iteration
     __shared__ float s_m[kAttnWarps][G], s_l[kAttnWarps][G];
     __shared__ __align__(16) float s_acc[kAttnWarps][G][D];
+    __shared__ float s_w[G][kMaxSplits];
 
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const int split = blockIdx.x;
@@ -78,16 +93,51 @@ __global__ void __launch_bounds__(kAttnWarps * 32) attn_decode_kernel(const Attn
     const int pidx = lane / LP, c = lane - (lane / LP) * LP;
     const bool cact = c < C8;
 
-    griddep_wait();
-    griddep_launch_dependents();
+    if (!p.early_kv) {
+        griddep_wait();
+        griddep_launch_dependents();
+    }
 
     const int L = p.causal_base >= 0 ? p.causal_base + b + 1 : (p.seq_lens ? p.seq_lens[b] : p.len_const);
     int chunk = (L + p.splits - 1) / p.splits;
     chunk = max(chunk, kMinChunk);
     const int n_used = L > 0 ? (L + chunk - 1) / chunk : 1;
-    if (split >= n_used) return;  // idle split at this context length
+    if (split >= n_used) {  // idle split at this context length
+        if (p.early_kv) griddep_launch_dependents();
+        return;
+    }
     const int start = split * chunk;
     const int end = min(L, start + chunk);
+
+    const __half* kb = p.k + (int64_t)b * p.sb + (int64_t)kvh * p.sh + c * 8;
+    const __half* vb = p.v + (int64_t)b * p.sb + (int64_t)kvh * p.sh + c * 8;
+
+    // first tile of this warp; in the decode-step form the rows older than
+    // the newest are requested before waiting on the previous kernel
+    uint4 kr[UNR], vr[UNR];
+    int base = start + warp * WT;
+    {
+        const int lim = p.early_kv ? min(end, L - 1) : end;
+#pragma unroll
+        for (int u = 0; u < UNR; ++u) {
+            const int pos = base + u * PPW + pidx;
+            const bool ok = cact && pos < lim;
+            kr[u] = ok ? ldg16(kb + (int64_t)pos * p.ss) : make_uint4(0, 0, 0, 0);
+            vr[u] = ok ? ldg16(vb + (int64_t)pos * p.ss) : make_uint4(0, 0, 0, 0);
+        }
+    }
+    if (p.early_kv) {
+        griddep_wait();
+        griddep_launch_dependents();
+#pragma unroll
+        for (int u = 0; u < UNR; ++u) {
+            const int pos = base + u * PPW + pidx;
+            if (cact && pos == L - 1 && pos < end) {
+                kr[u] = ldg16(kb + (int64_t)pos * p.ss);
+                vr[u] = ldg16(vb + (int64_t)pos * p.ss);
+            }
+        }
+    }
 
     float qf[G][8];
 #pragma unroll
@@ -112,17 +162,15 @@ __global__ void __launch_bounds__(kAttnWarps * 32) attn_decode_kernel(const Attn
         for (int j = 0; j < 8; ++j) acc[g][j] = 0.f;
     }
 
-    const __half* kb = p.k + (int64_t)b * p.sb + (int64_t)kvh * p.sh + c * 8;
-    const __half* vb = p.v + (int64_t)b * p.sb + (int64_t)kvh * p.sh + c * 8;
-
-    for (int base = start + warp * WT; base < end; base += kAttnWarps * WT) {
-        uint4 kr[UNR], vr[UNR];
+    for (bool first = true; base < end; base += kAttnWarps * WT, first = false) {
+        if (!first) {
 #pragma unroll
-        for (int u = 0; u < UNR; ++u) {
-            const int pos = base + u * PPW + pidx;
-            const bool ok = cact && pos < end;
-            kr[u] = ok ? ldg16(kb + (int64_t)pos * p.ss) : make_uint4(0, 0, 0, 0);
-            vr[u] = ok ? ldg16(vb + (int64_t)pos * p.ss) : make_uint4(0, 0, 0, 0);
+            for (int u = 0; u < UNR; ++u) {
+                const int pos = base + u * PPW + pidx;
+                const bool ok = cact && pos < end;
+                kr[u] = ok ? ldg16(kb + (int64_t)pos * p.ss) : make_uint4(0, 0, 0, 0);
+                vr[u] = ok ? ldg16(vb + (int64_t)pos * p.ss) : make_uint4(0, 0, 0, 0);
+            }
         }
         float s[UNR][G];
 #pragma unroll
@@ -190,7 +238,7 @@ __global__ void __launch_bounds__(kAttnWarps * 32) attn_decode_kernel(const Attn
     __syncthreads();
 
     const bool direct = n_used <= 1;
-    for (int idx = threadIdx.x; idx < nh * D; idx += kAttnWarps * 32) {
+    for (int idx = threadIdx.x; idx < nh * D; idx += kAttnThreads) {
         const int g = idx / D, d = idx - (idx / D) * D;
         float M = s_m[0][g];
 #pragma unroll
@@ -224,20 +272,40 @@ __global__ void __launch_bounds__(kAttnWarps * 32) attn_decode_kernel(const Attn
     __syncthreads();
     if (!s_last) return;
     __threadfence();
-    for (int idx = threadIdx.x; idx < nh * D; idx += kAttnWarps * 32) {
-        const int g = idx / D, d = idx - (idx / D) * D;
+    // per head: normalised weight of every split, exp2(m_s - M) / sum, in shared memory
+    for (int g = warp; g < nh; g += kAttnWarps) {
         const int64_t r0 = ((int64_t)b * p.nq + h0 + g) * p.splits;
+        float2 t[kMaxSplits / 32];
         float M = -INFINITY;
-        for (int sp = 0; sp < n_used; ++sp) M = fmaxf(M, __ldcg(&p.ml[r0 + sp]).x);
-        float A = 0.f, Ls = 0.f;
-#pragma unroll 4
-        for (int sp = 0; sp < n_used; ++sp) {
-            const float2 t = __ldcg(&p.ml[r0 + sp]);
-            const float sc = exp2f(t.x - M);
-            Ls = fmaf(t.y, sc, Ls);
-            A = fmaf(__ldcg(&p.part[(r0 + sp) * D + d]), sc, A);
+#pragma unroll
+        for (int i = 0; i < kMaxSplits / 32; ++i) {
+            const int sp = lane + 32 * i;
+            t[i] = sp < n_used ? __ldcg(&p.ml[r0 + sp]) : make_float2(-INFINITY, 0.f);
+            M = fmaxf(M, t[i].x);
         }
-        p.out[(int64_t)b * p.o_sb + (int64_t)(h0 + g) * D + d] = __float2half_rn(Ls > 0.f ? A / Ls : 0.f);
+        M = warp_max(M);
+        float Ls = 0.f;
+#pragma unroll
+        for (int i = 0; i < kMaxSplits / 32; ++i) {
+            t[i].x = t[i].x == -INFINITY ? 0.f : exp2f(t[i].x - M);
+            Ls = fmaf(t[i].y, t[i].x, Ls);
+        }
+        Ls = warp_sum(Ls);
+        const float inv = Ls > 0.f ? 1.f / Ls : 0.f;
+#pragma unroll
+        for (int i = 0; i < kMaxSplits / 32; ++i) {
+            const int sp = lane + 32 * i;
+            if (sp < n_used) s_w[g][sp] = t[i].x * inv;
+        }
+    }
+    __syncthreads();
+    for (int idx = threadIdx.x; idx < nh * D; idx += kAttnThreads) {
+        const int g = idx / D, d = idx - (idx / D) * D;
+        const float* pp = p.part + ((int64_t)b * p.nq + h0 + g) * p.splits * D + d;
+        float A = 0.f;
+#pragma unroll 8
+        for (int sp = 0; sp < n_used; ++sp) A = fmaf(__ldcg(pp + (int64_t)sp * D), s_w[g][sp], A);
+        p.out[(int64_t)b * p.o_sb + (int64_t)(h0 + g) * D + d] = __float2half_rn(A);
     }
     if (threadIdx.x == 0) *ctr = 0;
 }
@@ -245,10 +313,10 @@ __global__ void __launch_bounds__(kAttnWarps * 32) attn_decode_kernel(const Attn
 template <int D>
 static cudaError_t launch_decode_d(const AttnParams& p, dim3 grid, int G, cudaStream_t s, bool pdl) {
     switch (G) {
-        case 1: return launch(attn_decode_kernel<D, 1>, grid, dim3(kAttnWarps * 32), 0, s, pdl, p);
-        case 2: return launch(attn_decode_kernel<D, 2>, grid, dim3(kAttnWarps * 32), 0, s, pdl, p);
-        case 4: return launch(attn_decode_kernel<D, 4>, grid, dim3(kAttnWarps * 32), 0, s, pdl, p);
-        default: return launch(attn_decode_kernel<D, 8>, grid, dim3(kAttnWarps * 32), 0, s, pdl, p);
+        case 1: return launch(attn_decode_kernel<D, 1>, grid, dim3(kAttnThreads), 0, s, pdl, p);
+        case 2: return launch(attn_decode_kernel<D, 2>, grid, dim3(kAttnThreads), 0, s, pdl, p);
+        case 4: return launch(attn_decode_kernel<D, 4>, grid, dim3(kAttnThreads), 0, s, pdl, p);
+        default: return launch(attn_decode_kernel<D, 8>, grid, dim3(kAttnThreads), 0, s, pdl, p);
     }
 }
 
@@ -274,8 +342,9 @@ int attn_pick_splits(int batch, int nq, int nkv, int D, int max_len, size_t cap_
     const long ctas1 = (long)batch * nkv * attn_head_groups(nq, nkv);
     const long target = 4L * sm_count();
     long splits = (target + ctas1 - 1) / ctas1;
-    const long by_len = (max_len + kMinChunk - 1) / kMinChunk;
+    const long by_len = (max_len + 15) / 16;  // the kernel runs at least 16 positions per split
     if (splits > by_len) splits = by_len;
+    if (splits > kMaxSplits) splits = kMaxSplits;
     while (splits > 1 && attn_scratch_floats(batch, nq, nkv, D, (int)splits) > cap_floats) --splits;
     if (splits < 1) splits = 1;
     return (int)splits;
@@ -446,5 +515,33 @@ int attn_decode_launch_model(const __half* q, const __half* kbase, const __half*
     p.part = part;
     p.splits = splits;
     return attn_decode_launch(p, B, D, s, pdl);
+}
+
+// Decode-step launch: as attn_decode_launch_model, and in addition the K/V
+// rows older than seq_lens[b] - 1 and seq_lens itself are read before the
+// programmatic-launch wait (valid only when the preceding kernel writes no
+// more than the newest row).
+int attn_decode_launch_step(const __half* q, const __half* kbase, const __half* vbase, int64_t sb, int64_t sh,
+                            int64_t ss, const int* seq_lens, __half* out, float* part, int splits, int B, int nq,
+                            int nkv, int D, cudaStream_t s) {
+    AttnParams p = {};
+    p.q = q;
+    p.q_sb = (int64_t)nq * D;
+    p.k = kbase;
+    p.v = vbase;
+    p.sb = sb;
+    p.sh = sh;
+    p.ss = ss;
+    p.seq_lens = seq_lens;
+    p.causal_base = -1;
+    p.out = out;
+    p.o_sb = (int64_t)nq * D;
+    p.nq = nq;
+    p.nkv = nkv;
+    p.scale_log2 = 1.4426950408889634f / sqrtf((float)D);
+    p.part = part;
+    p.splits = splits;
+    p.early_kv = 1;
+    return attn_decode_launch(p, B, D, s, true);
 }
 }  // namespace b2

@@ -85,6 +85,7 @@ template <int R, int BT, int XM, int OM, int U>
 __global__ void __launch_bounds__(kGemvThreads, 2) gemv_vec_kernel(const GemvParams p) {
     extern __shared__ __align__(16) uint4 xs[];  // [BT][K8] packed half
     __shared__ float s_rs[BT];
+    __shared__ float s_ss[BT][kGemvWarps];
     __shared__ unsigned long long s_best[kGemvWarps][BT];
 
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
@@ -106,19 +107,34 @@ __global__ void __launch_bounds__(kGemvThreads, 2) gemv_vec_kernel(const GemvPar
 
     // ---- stage x in shared memory --------------------------------------
     if constexpr (XM == X_NORM) {
+        // Sum of squares of each sequence's fp32 residual row, spread over the
+        // whole CTA so the loads are independent (one L2 round trip, not K/128).
         const float* h = static_cast<const float*>(p.x);
-        for (int b = warp; b < BT; b += kGemvWarps) {
-            float ss = 0.f;
-            if (b < p.B) {
-                const float4* hr = reinterpret_cast<const float4*>(h + (size_t)b * p.ldx);
-                for (int i = lane; i < (p.K >> 2); i += 32) {
-                    const float4 v = hr[i];
-                    ss = fmaf(v.x, v.x, ss); ss = fmaf(v.y, v.y, ss);
-                    ss = fmaf(v.z, v.z, ss); ss = fmaf(v.w, v.w, ss);
+        float ss[BT];
+#pragma unroll
+        for (int b = 0; b < BT; ++b) ss[b] = 0.f;
+#pragma unroll 4
+        for (int i = threadIdx.x; i < (p.K >> 2); i += kGemvThreads) {
+#pragma unroll
+            for (int b = 0; b < BT; ++b) {
+                if (b < p.B) {
+                    const float4 v = reinterpret_cast<const float4*>(h + (size_t)b * p.ldx)[i];
+                    ss[b] = fmaf(v.x, v.x, ss[b]); ss[b] = fmaf(v.y, v.y, ss[b]);
+                    ss[b] = fmaf(v.z, v.z, ss[b]); ss[b] = fmaf(v.w, v.w, ss[b]);
                 }
             }
-            ss = warp_sum(ss);
-            if (lane == 0) s_rs[b] = rsqrtf(ss / (float)p.K + p.eps);
+        }
+#pragma unroll
+        for (int b = 0; b < BT; ++b) {
+            const float v = warp_sum(ss[b]);
+            if (lane == 0) s_ss[b][warp] = v;
+        }
+        __syncthreads();
+        if (threadIdx.x < BT) {
+            float tot = 0.f;
+#pragma unroll
+            for (int w = 0; w < kGemvWarps; ++w) tot += s_ss[threadIdx.x][w];
+            s_rs[threadIdx.x] = rsqrtf(tot / (float)p.K + p.eps);
         }
         __syncthreads();
         for (int i = threadIdx.x; i < BT * K8; i += kGemvThreads) {

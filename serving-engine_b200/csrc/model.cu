@@ -41,9 +41,9 @@ struct AttnParams;
 int attn_pick_splits(int batch, int nq, int nkv, int D, int max_len, size_t cap_floats);
 size_t attn_scratch_floats(int batch, int nq, int nkv, int D, int splits);
 bool attn_head_dim_supported(int D);
-int attn_decode_launch_model(const __half* q, const __half* kbase, const __half* vbase, int64_t sb, int64_t sh,
-                             int64_t ss, const int* seq_lens, __half* out, float* part, int splits, int B, int nq,
-                             int nkv, int D, cudaStream_t s, bool pdl);
+int attn_decode_launch_step(const __half* q, const __half* kbase, const __half* vbase, int64_t sb, int64_t sh,
+                            int64_t ss, const int* seq_lens, __half* out, float* part, int splits, int B, int nq,
+                            int nkv, int D, cudaStream_t s);
 
 // ---------------------------------------------------------------------------
 // seeded initialisation (bit-identical to oracle/b2oracle.c ora_init_value)
@@ -532,10 +532,11 @@ static int launch_qkv(b2_model* m, int l, int B, bool pdl) {
 }
 
 static int launch_attn(b2_model* m, int l, int B, bool pdl) {
+    (void)pdl;  // the step form always uses programmatic launch
     const int D = m->cfg.head_dim;
     __half* kbase = m->kv + (int64_t)l * m->kv_s_layer;
-    return attn_decode_launch_model(m->q, kbase, kbase + m->kv_s_kv, m->kv_s_batch, m->kv_s_head, D, m->seq_lens,
-                                    m->attn, m->part, m->splits, B, m->nq, m->nkv, D, m->stream, pdl);
+    return attn_decode_launch_step(m->q, kbase, kbase + m->kv_s_kv, m->kv_s_batch, m->kv_s_head, D, m->seq_lens,
+                                   m->attn, m->part, m->splits, B, m->nq, m->nkv, D, m->stream);
 }
 
 static int launch_o(b2_model* m, int l, int B, bool pdl) {
