@@ -38,6 +38,13 @@ const char* b2_status_string(int status);
 /* Build identification, e.g. "b2engine 0.1 sm_100a". */
 const char* b2_version(void);
 
+/* Synchronises the current device and reports whether a bounded device-side
+ * wait of a tensor-core kernel gave up since the last clear: B2_OK, or
+ * B2_ERR_TIMEOUT (its pipeline stalled; the kernel skipped its remaining work
+ * and exited).  clear != 0 resets the record.  No reference counterpart: the
+ * reference's kernels have no device-side waits. */
+int b2_device_status(int clear);
+
 /* Strided view over a K or V cache: element (b, h, s, d) lives at
  * data + b*stride_b + h*stride_h + s*stride_s + d*stride_d (elements of half).
  * Replaces engine::cuda::KVView (src/cuda/kv_view.h:17-31). stride_d must be 1. */
@@ -94,7 +101,7 @@ int b2_decode_gqa(const void* q, const void* k_cache, const void* v_cache, void*
  * [B, nq, D] half, seq_lens int32 [B] on the device (read by the kernel, so
  * the call is graph-capturable across steps), K/V through strided views.
  * The positions of each (sequence, kv head) are cut into splits of at least
- * 64 positions, as many as split_buffer holds (about
+ * one kernel iteration (16 to 64 positions), as many as split_buffer holds (about
  * split_buffer_floats / (B*nq*(D+2)); a few floats hold per-(sequence,
  * kv head) counters).  Each split writes a partial output and its (max, sum)
  * pair into split_buffer and the last split to finish merges them, in the
@@ -215,6 +222,10 @@ typedef struct b2_model_config {
 } b2_model_config;
 
 typedef struct b2_model b2_model;
+
+/* Writes a fresh 128-byte ncclUniqueId (rank 0 calls it and shares the bytes
+ * with the other ranks).  B2_ERR_NCCL when NCCL cannot be loaded. */
+int b2_nccl_unique_id(void* out128);
 
 /* Creates a model shard on the current CUDA device (allocates all weights,
  * the KV cache and activations).  tp_size > 1 shards heads / FFN rows /

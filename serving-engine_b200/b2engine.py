@@ -45,6 +45,7 @@ class ModelConfig(C.Structure):
 _SIGS = {
     "b2_version": (C.c_char_p, []),
     "b2_status_string": (C.c_char_p, [i32]),
+    "b2_device_status": (i32, [i32]),
     "b2_embedding_lookup": (i32, [vp, vp, vp, i64, i64, vp]),
     "b2_rmsnorm": (i32, [vp, vp, vp, i64, i64, f32, vp]),
     "b2_bias_add": (i32, [vp, vp, vp, i64, i64, vp]),
@@ -123,6 +124,12 @@ def lib():
 
 def status_string(s: int) -> str:
     return lib().b2_status_string(s).decode()
+
+
+def device_status(clear: bool = True) -> int:
+    """Synchronise the device; 0, or B2_ERR_TIMEOUT (-6) if a bounded wait of a
+    tensor-core kernel gave up since the last clear."""
+    return lib().b2_device_status(1 if clear else 0)
 
 
 def call(name: str, *args) -> None:
