@@ -132,10 +132,21 @@ int b2_decode_gqa_split_noalloc(const void* q, b2_kv_view k_view, b2_kv_view v_v
                                 void* out, int batch_size, int num_q_heads, int num_kv_heads, int head_dim,
                                 int max_seq_len, void* stream);
 
-/* Causal GQA prefill attention, q/out [B,S,nq,D], k/v [B,S,nkv,D], half.
+/* Causal GQA prefill attention, q/out [B,S,nq,D], k/v [B,S,nkv,D], half,
+ * scale 1/sqrt(D).  head_dim 64 and 128 run on the tcgen05 tensor cores
+ * (fp32 accumulation in TMEM); other head dims through the split-KV kernel.
  * Replaces engine::cuda::flash_prefill_gqa (src/cuda/kernels.h:136-147). */
 int b2_flash_prefill_gqa(const void* q, const void* k, const void* v, void* out, int64_t seq_len,
                          int num_q_heads, int num_kv_heads, int head_dim, int batch_size, void* stream);
+
+/* b2_flash_prefill_gqa with a choice of element type (bf16 != 0: bf16
+ * q/k/v/out, else half) and rotate-half RoPE applied inside the kernel to q
+ * and k at positions start_pos + s when rope_theta > 0 (q, k in memory are
+ * left unrotated).  head_dim 64 or 128 only.  New API (the reference applies
+ * RoPE as a separate apply_rope launch, src/model/forward_gpu.cu:419-421). */
+int b2_flash_prefill_gqa_ex(const void* q, const void* k, const void* v, void* out, int64_t seq_len,
+                            int num_q_heads, int num_kv_heads, int head_dim, int batch_size, int bf16,
+                            float rope_theta, int64_t start_pos, void* stream);
 
 /* out = silu(gate) * up, half. Replaces engine::cuda::swiglu (src/cuda/kernels.h:151-157). */
 int b2_swiglu(const void* gate, const void* up, void* out, int64_t count, void* stream);

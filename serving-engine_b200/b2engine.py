@@ -57,6 +57,7 @@ _SIGS = {
     "b2_decode_gqa_split": (i32, [vp, KVView, KVView, vp, vp, i32, i32, i32, i32, i32, vp, C.c_size_t, vp]),
     "b2_decode_gqa_split_noalloc": (i32, [vp, KVView, KVView, vp, vp, i32, i32, i32, i32, i32, vp]),
     "b2_flash_prefill_gqa": (i32, [vp, vp, vp, vp, i64, i32, i32, i32, i32, vp]),
+    "b2_flash_prefill_gqa_ex": (i32, [vp, vp, vp, vp, i64, i32, i32, i32, i32, i32, f32, i64, vp]),
     "b2_swiglu": (i32, [vp, vp, vp, i64, vp]),
     "b2_matmul_transB": (i32, [vp, vp, vp, i32, i32, i32, vp]),
     "b2_matmul_transB_f32": (i32, [vp, vp, vp, i32, i32, i32, vp]),

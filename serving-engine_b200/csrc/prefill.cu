@@ -1,15 +1,427 @@
-// prefill.cu -- causal GQA prefill attention (operator API flash_prefill_gqa).
+// prefill.cu -- causal GQA flash prefill on the tcgen05 tensor cores
+// (operator API flash_prefill_gqa, plus a bf16 / fused-RoPE form).
 //
-// Current form: every query row is run as a decode query of length i+1
-// through the split-KV attention kernel (attention.cu), which streams K/V
-// once per kv head for the whole query-head group with online softmax.
-// Reference replaced: src/cuda/flash_prefill.cu:43-240.
-#include "common.cuh"
+// One CTA computes the attention output of one 128-query tile of one query
+// head.  Q, K and V tiles (128 rows x D, 128-byte swizzled) arrive by TMA;
+// both products run on the tensor cores with fp32 accumulation in TMEM:
+//   S_j = Q K_j^T    M=128 queries, N=128 keys, K=D   (TMEM columns 0-255,
+//                    two buffers, so S_{j+1} is computed while row j's
+//                    softmax runs)
+//   O  += P_j V_j    M=128 queries, N=D, K=128 keys  (TMEM columns 256..)
+// Warp roles (192 threads, 320 with RoPE):
+//   warp 4      TMA producer: Q once, then K_j / V_j into 2-stage rings;
+//   warp 5      MMA issuer (one thread): S_j, then P_{j-1} V_{j-1};
+//   warps 0..3  softmax, one query row per thread: row max of S_j (scale
+//               and causal mask applied on the fly), P_j = exp2(S - m) as
+//               half/bf16 into a swizzled shared-memory operand, running
+//               row sum; the output O / l at the end;
+//   warps 6..9  (RoPE form) rotate the Q tile and every K tile in shared
+//               memory before the MMA issuer may use them.
+// Online softmax without a rescale per tile: the reference max m of a row
+// only moves when the tile max exceeds it by more than 8 (log2 units); P
+// values stay <= 2^8 otherwise, and when m moves the O row in TMEM is scaled
+// by exp2(m_old - m_new) before the next P V accumulates into it.
+// Causal: tile qt needs KV tiles 0..qt; the diagonal tile is masked, tiles
+// are scheduled heaviest first.  Every mbarrier wait is bounded (tc.cuh).
+//
+// Shapes the tensor-core kernel does not take (head_dim other than 64/128,
+// unaligned bases) run each query row as a decode query of length i+1
+// through the split-KV attention kernel (attention.cu).
+// Reference replaced: src/cuda/flash_prefill.cu:43-240 (16 threads per CTA,
+// one query row per thread, scalar FMA, head_dim fixed at 64).
+#include <cmath>
+#include <type_traits>
+
+#include "tc.cuh"
 
 namespace b2 {
 int causal_attention_rows(const __half* q, const __half* k, const __half* v, __half* out, int64_t S, int nq,
                           int nkv, int D, int batch, cudaStream_t s);
 bool attn_head_dim_supported(int D);
+
+template <int D, bool ROPE>
+struct FlashCfg {
+    static constexpr int ATOMS = D / 64;                    // 128-byte swizzle atoms per row
+    static constexpr uint32_t ATOM = 128 * 128;             // bytes of one 128-row atom
+    static constexpr uint32_t TILE = 128 * D * 2;           // Q, K or V tile
+    static constexpr uint32_t P_BYTES = 128 * 128 * 2;
+    static constexpr uint32_t OFF_Q = 0;
+    static constexpr uint32_t OFF_K = TILE;                 // 2 stages
+    static constexpr uint32_t OFF_V = 3 * TILE;             // 2 stages
+    static constexpr uint32_t OFF_P = 5 * TILE;
+    static constexpr uint32_t OFF_BAR = OFF_P + P_BYTES;
+    // 1 KB alignment slack; at least 120 KB so that one CTA (and its 512 TMEM
+    // columns) owns an SM
+    static constexpr size_t SMEM_NEED = OFF_BAR + 256 + 1024;
+    static constexpr size_t SMEM = SMEM_NEED > 122880 ? SMEM_NEED : 122880;
+    static constexpr int THREADS = ROPE ? 320 : 192;
+    static constexpr uint32_t TMEM_COLS = 512;
+};
+
+template <bool BF16>
+__device__ __forceinline__ uint32_t pack2(float a, float b) {
+    if constexpr (BF16) {
+        __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
+        return *reinterpret_cast<uint32_t*>(&h);
+    } else {
+        __half2 h = __floats2half2_rn(a, b);
+        return *reinterpret_cast<uint32_t*>(&h);
+    }
+}
+
+template <bool BF16>
+__device__ __forceinline__ float2 unpack2(uint32_t v) {
+    if constexpr (BF16) {
+        __nv_bfloat162 h = *reinterpret_cast<__nv_bfloat162*>(&v);
+        return __bfloat1622float2(h);
+    } else {
+        __half2 h = *reinterpret_cast<__half2*>(&v);
+        return __half22float2(h);
+    }
+}
+
+// Byte offset of element e of row `row` in a 128-byte-swizzled tile made of
+// 128-row atoms of 64 elements.
+__device__ __forceinline__ uint32_t sw128_off(int row, int e) {
+    return (uint32_t)(e >> 6) * (128u * 128u) + (uint32_t)row * 128u + ((((uint32_t)(e & 63) >> 3) ^ (row & 7)) << 4) +
+           ((uint32_t)(e & 7) << 1);
+}
+
+// Rotate-half RoPE of one tile row in shared memory at position `pos`:
+// x[i], x[i+D/2] -> x[i] cos - x[i+D/2] sin, x[i+D/2] cos + x[i] sin with
+// angle = pos * inv_freq[i] (the reference's float arithmetic,
+// src/cpu/ops.cpp:174-189).
+template <int D, bool BF16>
+__device__ __forceinline__ void rope_row(uint8_t* tile, int row, int pos, const float* invf) {
+    constexpr int H = D / 2;
+#pragma unroll 1
+    for (int e1 = 0; e1 < H; e1 += 8) {
+        uint4* p1 = reinterpret_cast<uint4*>(tile + sw128_off(row, e1));
+        uint4* p2 = reinterpret_cast<uint4*>(tile + sw128_off(row, e1 + H));
+        uint4 a = *p1, c = *p2;
+        uint32_t* aw = reinterpret_cast<uint32_t*>(&a);
+        uint32_t* cw = reinterpret_cast<uint32_t*>(&c);
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+            const float2 x1 = unpack2<BF16>(aw[k]), x2 = unpack2<BF16>(cw[k]);
+            float s0, c0, s1, c1;
+            sincosf((float)pos * invf[e1 + 2 * k], &s0, &c0);
+            sincosf((float)pos * invf[e1 + 2 * k + 1], &s1, &c1);
+            aw[k] = pack2<BF16>(x1.x * c0 - x2.x * s0, x1.y * c1 - x2.y * s1);
+            cw[k] = pack2<BF16>(x2.x * c0 + x1.x * s0, x2.y * c1 + x1.y * s1);
+        }
+        *p1 = a;
+        *p2 = c;
+    }
+}
+
+template <int D, bool BF16, bool ROPE>
+__global__ void __launch_bounds__(FlashCfg<D, ROPE>::THREADS, 1)
+    flash_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
+                    const __grid_constant__ CUtensorMap tmV, void* __restrict__ out, int S, int nq, int nkv,
+                    float scale_log2, float rope_theta, int pos0, int* err) {
+    using Cfg = FlashCfg<D, ROPE>;
+    constexpr uint32_t TILE = Cfg::TILE;
+    extern __shared__ uint8_t smem_raw[];
+    __shared__ float s_invf[64];
+    uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint8_t* sQ = sm + Cfg::OFF_Q;
+    uint8_t* sK = sm + Cfg::OFF_K;
+    uint8_t* sV = sm + Cfg::OFF_V;
+    uint8_t* sP = sm + Cfg::OFF_P;
+    uint64_t* bar = reinterpret_cast<uint64_t*>(sm + Cfg::OFF_BAR);
+    uint64_t* q_full = bar + 0;
+    uint64_t* q_ready = bar + 1;
+    uint64_t* k_full = bar + 2;   // [2]
+    uint64_t* k_ready = bar + 4;  // [2]
+    uint64_t* k_empty = bar + 6;  // [2]
+    uint64_t* v_full = bar + 8;   // [2]
+    uint64_t* v_empty = bar + 10; // [2]
+    uint64_t* s_full = bar + 12;  // [2]
+    uint64_t* p_full = bar + 14;
+    uint64_t* o_done = bar + 15;
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bar + 16);
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int qt = (int)gridDim.x - 1 - (int)blockIdx.x;  // heaviest tiles first
+    const int h = blockIdx.y, b = blockIdx.z;
+    const int kvh = h / (nq / nkv);
+    const int q0 = qt * 128;
+    const int nt = qt + 1;
+
+    if (threadIdx.x == 0) {
+        tc::mbar_init(q_full, 1);
+        tc::mbar_init(q_ready, 128);
+        for (int s = 0; s < 2; ++s) {
+            tc::mbar_init(&k_full[s], 1);
+            tc::mbar_init(&k_ready[s], 128);
+            tc::mbar_init(&k_empty[s], 1);
+            tc::mbar_init(&v_full[s], 1);
+            tc::mbar_init(&v_empty[s], 1);
+            tc::mbar_init(&s_full[s], 1);
+        }
+        tc::mbar_init(p_full, 128);
+        tc::mbar_init(o_done, 1);
+        tc::fence_barrier_init();
+    }
+    if (ROPE && threadIdx.x < D / 2) s_invf[threadIdx.x] = 1.0f / powf(rope_theta, (float)(2 * threadIdx.x) / (float)D);
+    if (warp == 0) tc::tmem_alloc(tmem_slot, Cfg::TMEM_COLS);
+    tc::fence_before_sync();
+    __syncthreads();
+    tc::fence_after_sync();
+    const uint32_t tmem = *tmem_slot;
+    const uint32_t tO = tmem + 256;
+
+    griddep_wait();  // Q / K / V may be the previous kernel's output
+    griddep_launch_dependents();
+
+    if (warp == 4) {
+        // ---------------- TMA producer ----------------
+        if (lane == 0) {
+            tc::mbar_arrive_expect_tx(q_full, TILE);
+#pragma unroll
+            for (int a = 0; a < Cfg::ATOMS; ++a) tc::tma_load_4d(sQ + a * Cfg::ATOM, &tmQ, q_full, a * 64, h, q0, b);
+            for (int j = 0; j < nt; ++j) {
+                const int s = j & 1;
+                const uint32_t u = (uint32_t)j >> 1;
+                if (j >= 2 && !tc::mbar_wait(&k_empty[s], (u - 1) & 1u, err, 11)) break;
+                tc::mbar_arrive_expect_tx(&k_full[s], TILE);
+#pragma unroll
+                for (int a = 0; a < Cfg::ATOMS; ++a)
+                    tc::tma_load_4d(sK + s * TILE + a * Cfg::ATOM, &tmK, &k_full[s], a * 64, kvh, j * 128, b);
+                if (j >= 2 && !tc::mbar_wait(&v_empty[s], (u - 1) & 1u, err, 12)) break;
+                tc::mbar_arrive_expect_tx(&v_full[s], TILE);
+#pragma unroll
+                for (int a = 0; a < Cfg::ATOMS; ++a)
+                    tc::tma_load_4d(sV + s * TILE + a * Cfg::ATOM, &tmV, &v_full[s], a * 64, kvh, j * 128, b);
+            }
+        }
+    } else if (warp == 5) {
+        // ---------------- MMA issuer ----------------
+        if (lane == 0) {
+            constexpr uint32_t idS = tc::idesc_f16(128, 128, BF16, false);
+            constexpr uint32_t idO = tc::idesc_f16(128, D, BF16, true);
+            const uint32_t aQ = tc::smem_u32(sQ), aK = tc::smem_u32(sK), aV = tc::smem_u32(sV),
+                           aP = tc::smem_u32(sP);
+            bool ok = tc::mbar_wait(ROPE ? q_ready : q_full, 0, err, 13);
+            for (int j = 0; ok && j <= nt; ++j) {
+                if (j < nt) {
+                    const int s = j & 1;
+                    const uint32_t u = (uint32_t)j >> 1;
+                    ok = tc::mbar_wait(ROPE ? &k_ready[s] : &k_full[s], u & 1u, err, 14);
+                    if (!ok) break;
+                    tc::fence_after_sync();
+#pragma unroll
+                    for (int kk = 0; kk < D / 16; ++kk) {
+                        const uint32_t off = (uint32_t)(kk >> 2) * Cfg::ATOM + (uint32_t)(kk & 3) * 32;
+                        tc::mma_f16(tmem + s * 128, tc::desc_k_sw128(aQ + off), tc::desc_k_sw128(aK + s * TILE + off),
+                                    idS, kk > 0 ? 1u : 0u);
+                    }
+                    tc::mma_commit(&s_full[s]);
+                    tc::mma_commit(&k_empty[s]);
+                }
+                if (j > 0) {
+                    const int jj = j - 1, s = jj & 1;
+                    const uint32_t u = (uint32_t)jj >> 1;
+                    ok = tc::mbar_wait(p_full, (uint32_t)jj & 1u, err, 15) && tc::mbar_wait(&v_full[s], u & 1u, err, 16);
+                    if (!ok) break;
+                    tc::fence_after_sync();
+#pragma unroll
+                    for (int kk = 0; kk < 8; ++kk) {
+                        const uint32_t offp = (uint32_t)(kk >> 2) * Cfg::ATOM + (uint32_t)(kk & 3) * 32;
+                        tc::mma_f16(tO, tc::desc_k_sw128(aP + offp),
+                                    tc::desc_mn_sw128(aV + s * TILE + (uint32_t)kk * 2048u, Cfg::ATOM), idO,
+                                    (jj > 0 || kk > 0) ? 1u : 0u);
+                    }
+                    tc::mma_commit(o_done);
+                    tc::mma_commit(&v_empty[s]);
+                }
+            }
+        }
+    } else if (ROPE && warp >= 6) {
+        // ---------------- RoPE warps ----------------
+        const int t = threadIdx.x - 192;
+        bool ok = __all_sync(0xffffffffu, tc::mbar_wait(q_full, 0, err, 17));
+        if (ok) {
+            rope_row<D, BF16>(sQ, t, pos0 + q0 + t, s_invf);
+            tc::fence_proxy_async_smem();
+            tc::mbar_arrive(q_ready);
+        }
+        for (int j = 0; ok && j < nt; ++j) {
+            const int s = j & 1;
+            const uint32_t u = (uint32_t)j >> 1;
+            ok = __all_sync(0xffffffffu, tc::mbar_wait(&k_full[s], u & 1u, err, 18));
+            if (!ok) break;
+            rope_row<D, BF16>(sK + s * TILE, t, pos0 + j * 128 + t, s_invf);
+            tc::fence_proxy_async_smem();
+            tc::mbar_arrive(&k_ready[s]);
+        }
+    } else if (warp < 4) {
+        // ---------------- softmax and output ----------------
+        const int r = warp * 32 + lane;
+        const int qpos = q0 + r;
+        const uint32_t lane_base = (uint32_t)(warp * 32) << 16;
+        float m = -INFINITY, l = 0.f;
+        bool ok = true;
+        for (int j = 0; j < nt; ++j) {
+            const int s = j & 1;
+            const uint32_t u = (uint32_t)j >> 1;
+            ok = __all_sync(0xffffffffu, tc::mbar_wait(&s_full[s], u & 1u, err, 19));
+            if (!ok) break;
+            tc::fence_after_sync();
+            const uint32_t srow = tmem + lane_base + s * 128;
+            const int kbase = j * 128;
+            const bool masked = kbase + 127 > q0 || kbase + 128 > S;
+            // pass 1: row max of the scaled, masked scores
+            float mx = -INFINITY;
+#pragma unroll 1
+            for (int c = 0; c < 128; c += 32) {
+                uint32_t v[32];
+                tc::tmem_ld32(srow + c, v);
+                tc::tmem_wait_ld();
+#pragma unroll
+                for (int e = 0; e < 32; ++e) {
+                    const int key = kbase + c + e;
+                    float x = __uint_as_float(v[e]) * scale_log2;
+                    if (masked && (key > qpos || key >= S)) x = -INFINITY;
+                    mx = fmaxf(mx, x);
+                }
+            }
+            const float m_new = fmaxf(m, mx);
+            const bool resc = m_new > m + 8.f;
+            const float m_use = resc ? m_new : m;
+            const float alpha = exp2f(m - m_use);
+            // P buffer free and O stable once P_{j-1} V_{j-1} has completed
+            if (j > 0) {
+                ok = __all_sync(0xffffffffu, tc::mbar_wait(o_done, (uint32_t)(j - 1) & 1u, err, 20));
+                if (!ok) break;
+                tc::fence_after_sync();
+                if (__any_sync(0xffffffffu, resc)) {
+#pragma unroll 1
+                    for (int c = 0; c < D; c += 32) {
+                        uint32_t v[32];
+                        tc::tmem_ld32(tO + lane_base + c, v);
+                        tc::tmem_wait_ld();
+#pragma unroll
+                        for (int e = 0; e < 32; ++e) v[e] = __float_as_uint(__uint_as_float(v[e]) * alpha);
+                        tc::tmem_st32(tO + lane_base + c, v);
+                    }
+                    tc::tmem_wait_st();
+                }
+            }
+            l *= alpha;
+            m = m_use;
+            // pass 2: P = exp2(x - m) into the swizzled operand tile, row sum
+#pragma unroll 1
+            for (int c = 0; c < 128; c += 32) {
+                uint32_t v[32];
+                tc::tmem_ld32(srow + c, v);
+                tc::tmem_wait_ld();
+                uint32_t pk[16];
+#pragma unroll
+                for (int e = 0; e < 32; e += 2) {
+                    float x0 = __uint_as_float(v[e]) * scale_log2, x1 = __uint_as_float(v[e + 1]) * scale_log2;
+                    const int key = kbase + c + e;
+                    if (masked && (key > qpos || key >= S)) x0 = -INFINITY;
+                    if (masked && (key + 1 > qpos || key + 1 >= S)) x1 = -INFINITY;
+                    const float p0 = exp2f(x0 - m), p1 = exp2f(x1 - m);
+                    l += p0 + p1;
+                    pk[e >> 1] = pack2<BF16>(p0, p1);
+                }
+#pragma unroll
+                for (int q = 0; q < 4; ++q) {
+                    *reinterpret_cast<uint4*>(sP + sw128_off(r, c + q * 8)) =
+                        make_uint4(pk[4 * q], pk[4 * q + 1], pk[4 * q + 2], pk[4 * q + 3]);
+                }
+            }
+            tc::fence_proxy_async_smem();
+            tc::fence_before_sync();
+            tc::mbar_arrive(p_full);
+        }
+        if (ok) ok = __all_sync(0xffffffffu, tc::mbar_wait(o_done, (uint32_t)(nt - 1) & 1u, err, 21));
+        tc::fence_after_sync();
+        const float inv_l = l > 0.f ? 1.f / l : 0.f;
+        using T = typename std::conditional<BF16, __nv_bfloat16, __half>::type;
+        T* orow = static_cast<T*>(out) + (((int64_t)b * S + qpos) * nq + h) * D;
+#pragma unroll 1
+        for (int c = 0; c < D; c += 32) {
+            uint32_t v[32];
+            tc::tmem_ld32(tO + lane_base + c, v);
+            tc::tmem_wait_ld();
+            if (!ok || qpos >= S) continue;
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+                uint4 w;
+                w.x = pack2<BF16>(__uint_as_float(v[8 * q + 0]) * inv_l, __uint_as_float(v[8 * q + 1]) * inv_l);
+                w.y = pack2<BF16>(__uint_as_float(v[8 * q + 2]) * inv_l, __uint_as_float(v[8 * q + 3]) * inv_l);
+                w.z = pack2<BF16>(__uint_as_float(v[8 * q + 4]) * inv_l, __uint_as_float(v[8 * q + 5]) * inv_l);
+                w.w = pack2<BF16>(__uint_as_float(v[8 * q + 6]) * inv_l, __uint_as_float(v[8 * q + 7]) * inv_l);
+                *reinterpret_cast<uint4*>(orow + c + 8 * q) = w;
+            }
+        }
+    }
+    tc::fence_before_sync();
+    __syncthreads();
+    if (warp == 0) {
+        tc::fence_after_sync();
+        tc::tmem_dealloc(tmem, Cfg::TMEM_COLS);
+    }
+}
+
+template <int D, bool BF16, bool ROPE>
+static int launch_flash(const void* q, const void* k, const void* v, void* out, int S, int nq, int nkv, int batch,
+                        float rope_theta, int pos0, cudaStream_t s) {
+    using Cfg = FlashCfg<D, ROPE>;
+    int* err = wait_error_word();
+    if (!err) return B2_ERR_STATE;
+    const CUtensorMapDataType dt = BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+    CUtensorMap tq, tk, tv;
+    const uint32_t box[4] = {64, 1, 128, 1};
+    {
+        const uint64_t dims[4] = {(uint64_t)D, (uint64_t)nq, (uint64_t)S, (uint64_t)batch};
+        const uint64_t st[3] = {(uint64_t)D * 2, (uint64_t)nq * D * 2, (uint64_t)S * nq * D * 2};
+        const int rc = make_tensor_map(&tq, dt, 4, q, dims, st, box);
+        if (rc != B2_OK) return rc;
+    }
+    {
+        const uint64_t dims[4] = {(uint64_t)D, (uint64_t)nkv, (uint64_t)S, (uint64_t)batch};
+        const uint64_t st[3] = {(uint64_t)D * 2, (uint64_t)nkv * D * 2, (uint64_t)S * nkv * D * 2};
+        int rc = make_tensor_map(&tk, dt, 4, k, dims, st, box);
+        if (rc != B2_OK) return rc;
+        rc = make_tensor_map(&tv, dt, 4, v, dims, st, box);
+        if (rc != B2_OK) return rc;
+    }
+    auto kern = flash_tc_kernel<D, BF16, ROPE>;
+    B2_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)Cfg::SMEM));
+    dim3 grid((unsigned)((S + 127) / 128), (unsigned)nq, (unsigned)batch);
+    const float scale_log2 = 1.4426950408889634f / sqrtf((float)D);
+    B2_TRY(launch(kern, grid, dim3(Cfg::THREADS), Cfg::SMEM, s, true, tq, tk, tv, out, S, nq, nkv, scale_log2,
+                  rope_theta, pos0, err));
+    return B2_OK;
+}
+
+template <bool BF16, bool ROPE>
+static int flash_dispatch_d(const void* q, const void* k, const void* v, void* out, int S, int nq, int nkv, int D,
+                            int batch, float theta, int pos0, cudaStream_t s) {
+    if (D == 64) return launch_flash<64, BF16, ROPE>(q, k, v, out, S, nq, nkv, batch, theta, pos0, s);
+    if (D == 128) return launch_flash<128, BF16, ROPE>(q, k, v, out, S, nq, nkv, batch, theta, pos0, s);
+    return B2_ERR_UNSUPPORTED;
+}
+
+// Tensor-core flash prefill; B2_ERR_UNSUPPORTED for shapes it does not take.
+int flash_prefill_tc(const void* q, const void* k, const void* v, void* out, int64_t S, int nq, int nkv, int D,
+                     int batch, bool bf16, float rope_theta, int pos0, cudaStream_t s) {
+    if ((D != 64 && D != 128) || S <= 0 || S > (1 << 30) || !aligned16(q) || !aligned16(k) || !aligned16(v) ||
+        !aligned16(out) || batch > 65535 || nq > 65535)
+        return B2_ERR_UNSUPPORTED;
+    const bool rope = rope_theta > 0.f;
+    if (bf16)
+        return rope ? flash_dispatch_d<true, true>(q, k, v, out, (int)S, nq, nkv, D, batch, rope_theta, pos0, s)
+                    : flash_dispatch_d<true, false>(q, k, v, out, (int)S, nq, nkv, D, batch, 0.f, 0, s);
+    return rope ? flash_dispatch_d<false, true>(q, k, v, out, (int)S, nq, nkv, D, batch, rope_theta, pos0, s)
+                : flash_dispatch_d<false, false>(q, k, v, out, (int)S, nq, nkv, D, batch, 0.f, 0, s);
+}
+
 }  // namespace b2
 
 extern "C" int b2_flash_prefill_gqa(const void* q, const void* k, const void* v, void* out, int64_t S, int nq,
@@ -17,8 +429,21 @@ extern "C" int b2_flash_prefill_gqa(const void* q, const void* k, const void* v,
     using namespace b2;
     if (S <= 0 || batch <= 0) return B2_OK;
     B2_REQUIRE(q && k && v && out && nq > 0 && nkv > 0 && nq % nkv == 0);
+    const int rc = flash_prefill_tc(q, k, v, out, S, nq, nkv, D, batch, false, 0.f, 0, as_stream(stream));
+    if (rc != B2_ERR_UNSUPPORTED) return rc;
     if (!attn_head_dim_supported(D) || !aligned16(q) || !aligned16(k) || !aligned16(v) || !aligned16(out))
         return B2_ERR_UNSUPPORTED;
     return causal_attention_rows((const __half*)q, (const __half*)k, (const __half*)v, (__half*)out, S, nq, nkv, D,
                                  batch, as_stream(stream));
+}
+
+extern "C" int b2_flash_prefill_gqa_ex(const void* q, const void* k, const void* v, void* out, int64_t S, int nq,
+                                       int nkv, int D, int batch, int bf16, float rope_theta, int64_t start_pos,
+                                       void* stream) {
+    using namespace b2;
+    if (S <= 0 || batch <= 0) return B2_OK;
+    B2_REQUIRE(q && k && v && out && nq > 0 && nkv > 0 && nq % nkv == 0 && rope_theta >= 0.f && start_pos >= 0);
+    B2_REQUIRE(start_pos + S < (int64_t)1 << 24);  // positions stay exact in float
+    return flash_prefill_tc(q, k, v, out, S, nq, nkv, D, batch, bf16 != 0, rope_theta, (int)start_pos,
+                            as_stream(stream));
 }
