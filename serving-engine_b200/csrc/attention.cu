@@ -449,21 +449,23 @@ extern "C" int b2_decode_gqa(const void* q, const void* kc, const void* vc, void
 
 namespace b2 {
 // Causal attention through the decode kernel: query row i of batch element
-// bb is a "sequence" of length i+1 over the token-major K/V of bb.
-int causal_attention_rows(const __half* q, const __half* k, const __half* v, __half* out, int64_t S, int nq,
-                          int nkv, int D, int batch, cudaStream_t s) {
+// bb is a "sequence" of length i+1 over the token-major K/V of bb.  ldq,
+// ldkv, ldo: elements between consecutive tokens (heads D apart in a row).
+int causal_attention_rows_ld(const __half* q, int64_t ldq, const __half* k, const __half* v, int64_t ldkv,
+                             __half* out, int64_t ldo, int64_t S, int nq, int nkv, int D, int batch,
+                             cudaStream_t s) {
     for (int bb = 0; bb < batch; ++bb) {
         AttnParams p = {};
-        p.q = q + (int64_t)bb * S * nq * D;
-        p.q_sb = (int64_t)nq * D;
-        p.k = k + (int64_t)bb * S * nkv * D;
-        p.v = v + (int64_t)bb * S * nkv * D;
+        p.q = q + (int64_t)bb * S * ldq;
+        p.q_sb = ldq;
+        p.k = k + (int64_t)bb * S * ldkv;
+        p.v = v + (int64_t)bb * S * ldkv;
         p.sb = 0;
         p.sh = D;
-        p.ss = (int64_t)nkv * D;
+        p.ss = ldkv;
         p.causal_base = 0;
-        p.out = out + (int64_t)bb * S * nq * D;
-        p.o_sb = (int64_t)nq * D;
+        p.out = out + (int64_t)bb * S * ldo;
+        p.o_sb = ldo;
         p.nq = nq;
         p.nkv = nkv;
         p.scale_log2 = 1.4426950408889634f / sqrtf((float)D);
@@ -479,6 +481,12 @@ int causal_attention_rows(const __half* q, const __half* k, const __half* v, __h
         }
     }
     return B2_OK;
+}
+
+int causal_attention_rows(const __half* q, const __half* k, const __half* v, __half* out, int64_t S, int nq,
+                          int nkv, int D, int batch, cudaStream_t s) {
+    return causal_attention_rows_ld(q, (int64_t)nq * D, k, v, (int64_t)nkv * D, out, (int64_t)nq * D, S, nq, nkv, D,
+                                    batch, s);
 }
 }  // namespace b2
 

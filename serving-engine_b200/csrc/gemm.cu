@@ -33,7 +33,10 @@ struct TcGemmCfg {
     static constexpr size_t SMEM = (size_t)STAGES * STAGE_BYTES + 256 + 1024;
 };
 
-template <int BN, bool OUT_F32>
+// Epilogue forms: half C, fp32 C, or fp32 C += A B^T (residual stream).
+enum TcEpi : int { TC_HALF = 0, TC_F32 = 1, TC_F32_ADD = 2 };
+
+template <int BN, int EPI>
 __global__ void __launch_bounds__(192, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                    void* __restrict__ C, int M, int N, int K, int* err) {
@@ -109,7 +112,24 @@ __global__ void __launch_bounds__(192, 1)
             tc::tmem_wait_ld();
             if (!ok || row >= M || n0 + c >= N) continue;
             const int ncol = min(32, N - (n0 + c));
-            if constexpr (OUT_F32) {
+            if constexpr (EPI == TC_F32_ADD) {
+                float* dst = static_cast<float*>(C) + (size_t)row * N + n0 + c;
+                if (ncol == 32 && (N & 3) == 0) {
+#pragma unroll
+                    for (int j = 0; j < 32; j += 4) {
+                        float4 o = *reinterpret_cast<float4*>(dst + j);
+                        o.x += __uint_as_float(r[j]);
+                        o.y += __uint_as_float(r[j + 1]);
+                        o.z += __uint_as_float(r[j + 2]);
+                        o.w += __uint_as_float(r[j + 3]);
+                        *reinterpret_cast<float4*>(dst + j) = o;
+                    }
+                } else {
+#pragma unroll
+                    for (int j = 0; j < 32; ++j)
+                        if (j < ncol) dst[j] += __uint_as_float(r[j]);
+                }
+            } else if constexpr (EPI == TC_F32) {
                 float* dst = static_cast<float*>(C) + (size_t)row * N + n0 + c;
                 if (ncol == 32 && (N & 3) == 0) {
 #pragma unroll
@@ -146,10 +166,10 @@ __global__ void __launch_bounds__(192, 1)
     }
 }
 
-template <int BN, bool F32>
+template <int BN, int EPI>
 static int launch_tc(const CUtensorMap& ta, const CUtensorMap& tb, void* C, int M, int N, int K, int* err,
                      cudaStream_t s) {
-    auto kern = gemm_tc_kernel<BN, F32>;
+    auto kern = gemm_tc_kernel<BN, EPI>;
     const size_t smem = TcGemmCfg<BN>::SMEM;
     B2_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
     dim3 grid((unsigned)((N + BN - 1) / BN), (unsigned)((M + kTcBM - 1) / kTcBM));
@@ -157,9 +177,21 @@ static int launch_tc(const CUtensorMap& ta, const CUtensorMap& tb, void* C, int 
     return B2_OK;
 }
 
-// C[M,N] = A[M,K] * B[N,K]^T on the tensor cores.  Requires 16-byte aligned
-// A and B and K % 8 == 0 (TMA row strides are multiples of 16 bytes).
-int gemm_tc(const __half* A, const __half* B, void* C, int M, int N, int K, bool f32, cudaStream_t s) {
+template <int BN>
+static int launch_tc_epi(const CUtensorMap& ta, const CUtensorMap& tb, void* C, int M, int N, int K, int epi,
+                         int* err, cudaStream_t s) {
+    switch (epi) {
+        case TC_HALF: return launch_tc<BN, TC_HALF>(ta, tb, C, M, N, K, err, s);
+        case TC_F32: return launch_tc<BN, TC_F32>(ta, tb, C, M, N, K, err, s);
+        default: return launch_tc<BN, TC_F32_ADD>(ta, tb, C, M, N, K, err, s);
+    }
+}
+
+// C[M,N] (=, or += for TC_F32_ADD) A[M,K] * B[N,K]^T on the tensor cores.
+// Requires 16-byte aligned A, B, C and K % 8 == 0 (TMA row strides are
+// multiples of 16 bytes); B2_ERR_UNSUPPORTED otherwise.
+int gemm_tc(const __half* A, const __half* B, void* C, int M, int N, int K, int epi, cudaStream_t s) {
+    if (M <= 0 || N <= 0 || K <= 0) return B2_ERR_UNSUPPORTED;
     if ((K & 7) || !aligned16(A) || !aligned16(B) || !aligned16(C)) return B2_ERR_UNSUPPORTED;
     int* err = wait_error_word();
     if (!err) return B2_ERR_STATE;
@@ -174,8 +206,8 @@ int gemm_tc(const __half* A, const __half* B, void* C, int M, int N, int K, bool
     if (rc != B2_OK) return rc;
     rc = make_tensor_map(&tb, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, B, db, sb, bb);
     if (rc != B2_OK) return rc;
-    if (BN == 256) return f32 ? launch_tc<256, true>(ta, tb, C, M, N, K, err, s) : launch_tc<256, false>(ta, tb, C, M, N, K, err, s);
-    return f32 ? launch_tc<128, true>(ta, tb, C, M, N, K, err, s) : launch_tc<128, false>(ta, tb, C, M, N, K, err, s);
+    return BN == 256 ? launch_tc_epi<256>(ta, tb, C, M, N, K, epi, err, s)
+                     : launch_tc_epi<128>(ta, tb, C, M, N, K, epi, err, s);
 }
 
 // ---------------------------------------------------------------------------
@@ -236,7 +268,7 @@ static int gemm_api(const void* A, const void* B, void* C, int M, int K, int N, 
     cudaStream_t s = as_stream(stream);
     if (M == 1 && K > 0) return b2_gemv_batched(B, A, nullptr, C, 1, N, K, 0, f32 ? 1 : 0, stream);
     if (K > 0) {
-        const int rc = gemm_tc((const __half*)A, (const __half*)B, C, M, N, K, f32, s);
+        const int rc = gemm_tc((const __half*)A, (const __half*)B, C, M, N, K, f32 ? TC_F32 : TC_HALF, s);
         if (rc != B2_ERR_UNSUPPORTED) return rc;
     }
     dim3 grid((unsigned)((N + TN - 1) / TN), (unsigned)((M + TM - 1) / TM));

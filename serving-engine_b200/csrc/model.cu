@@ -45,6 +45,23 @@ int attn_decode_launch_step(const __half* q, const __half* kbase, const __half* 
                             int64_t ss, const int* seq_lens, __half* out, float* part, int splits, int B, int nq,
                             int nkv, int D, cudaStream_t s);
 
+struct FlashArgs {
+    const void* q;
+    const void* k;
+    const void* v;
+    void* out;
+    int S, nq, nkv, D, batch;
+    int64_t ldq, ldkv, ldo;
+    bool bf16;
+    float rope_theta;
+    int pos0;
+};
+int flash_prefill_tc(const FlashArgs& a, cudaStream_t s);
+int causal_attention_rows_ld(const __half* q, int64_t ldq, const __half* k, const __half* v, int64_t ldkv,
+                             __half* out, int64_t ldo, int64_t S, int nq, int nkv, int D, int batch, cudaStream_t s);
+enum TcEpi : int { TC_HALF = 0, TC_F32 = 1, TC_F32_ADD = 2 };
+int gemm_tc(const __half* A, const __half* B, void* C, int M, int N, int K, int epi, cudaStream_t s);
+
 // ---------------------------------------------------------------------------
 // seeded initialisation (bit-identical to oracle/b2oracle.c ora_init_value)
 // ---------------------------------------------------------------------------
@@ -115,6 +132,95 @@ __global__ void step_end_kernel(const unsigned long long* __restrict__ argmax, i
     if (b == 0) {
         const int c = *hist_count;
         if (c < hist_cap) *hist_count = c + 1;
+    }
+}
+
+// ---------------------------------------------------------------------------
+// prefill kernels (all prompt tokens of all sequences at once, token-major
+// rows t = b * S + s)
+// ---------------------------------------------------------------------------
+// hidden[t] = embed[ids[t]] as fp32
+__global__ void embed_rows_kernel(const int64_t* __restrict__ ids, const __half* __restrict__ embed,
+                                  float* __restrict__ hidden, int H) {
+    const int64_t t = blockIdx.x;
+    const uint4* src = reinterpret_cast<const uint4*>(embed + ids[t] * H);
+    float4* dst = reinterpret_cast<float4*>(hidden + t * H);
+    for (int i = threadIdx.x; i < H / 8; i += blockDim.x) {
+        float f[8];
+        unpack8(ldg16(src + i), f);
+        dst[2 * i] = make_float4(f[0], f[1], f[2], f[3]);
+        dst[2 * i + 1] = make_float4(f[4], f[5], f[6], f[7]);
+    }
+}
+
+// out[t] = half(h * rsqrt(mean(h^2) + eps) * w) for the fp32 row h = hidden[t]
+// (the arithmetic of the decode GEMV's RMSNorm prologue)
+__global__ void rmsnorm_rows_kernel(const float* __restrict__ hidden, const __half* __restrict__ w,
+                                    __half* __restrict__ out, int H, float eps) {
+    __shared__ float red[32];
+    const int64_t t = blockIdx.x;
+    const float4* h = reinterpret_cast<const float4*>(hidden + t * H);
+    float ss = 0.f;
+    for (int i = threadIdx.x; i < H / 4; i += blockDim.x) {
+        const float4 v = h[i];
+        ss = fmaf(v.x, v.x, ss); ss = fmaf(v.y, v.y, ss); ss = fmaf(v.z, v.z, ss); ss = fmaf(v.w, v.w, ss);
+    }
+    const float r = rsqrtf(block_sum(ss, red) / (float)H + eps);
+    uint4* o = reinterpret_cast<uint4*>(out + t * H);
+    for (int c = threadIdx.x; c < H / 8; c += blockDim.x) {
+        const float4 a0 = h[2 * c], a1 = h[2 * c + 1];
+        float wv[8];
+        unpack8(ldg16(reinterpret_cast<const uint4*>(w) + c), wv);
+        float f[8] = {a0.x * r * wv[0], a0.y * r * wv[1], a0.z * r * wv[2], a0.w * r * wv[3],
+                      a1.x * r * wv[4], a1.y * r * wv[5], a1.z * r * wv[6], a1.w * r * wv[7]};
+        o[c] = pack8(f);
+    }
+}
+
+// Rotate-half RoPE (model table) on the q and k heads of the fused q|k|v rows
+// in place, and K / V of every token written into this layer's cache.
+// grid (T, nq + 2 nkv), D/2 threads.
+__global__ void rope_append_kernel(__half* __restrict__ qkv, int64_t ld, const float2* __restrict__ rope, int S,
+                                   int nq, int nkv, int D, __half* __restrict__ kcache, __half* __restrict__ vcache,
+                                   int64_t kv_sb, int64_t kv_sh) {
+    const int64_t t = blockIdx.x;
+    const int b = (int)(t / S), pos = (int)(t - (int64_t)b * S);
+    const int head = blockIdx.y, half = D >> 1, i = threadIdx.x;
+    __half* row = qkv + t * ld + (int64_t)head * D;
+    float x1 = __half2float(row[i]), x2 = __half2float(row[i + half]);
+    if (head < nq + nkv) {
+        const float2 cs = rope[(int64_t)pos * half + i];
+        const float o1 = x1 * cs.x - x2 * cs.y;
+        const float o2 = x2 * cs.x + x1 * cs.y;
+        row[i] = __float2half_rn(o1);
+        row[i + half] = __float2half_rn(o2);
+        if (head >= nq) {
+            __half* k = kcache + b * kv_sb + (int64_t)(head - nq) * kv_sh + (int64_t)pos * D;
+            k[i] = __float2half_rn(o1);
+            k[i + half] = __float2half_rn(o2);
+        }
+    } else {
+        __half* v = vcache + b * kv_sb + (int64_t)(head - nq - nkv) * kv_sh + (int64_t)pos * D;
+        v[i] = row[i];
+        v[i + half] = row[i + half];
+    }
+}
+
+// out[b] = hidden[b * S + S - 1] (the last prompt position of each sequence)
+__global__ void gather_last_kernel(const float* __restrict__ hidden, float* __restrict__ out, int S, int H) {
+    const int b = blockIdx.x;
+    const float* src = hidden + ((int64_t)b * S + S - 1) * H;
+    for (int i = threadIdx.x; i < H; i += blockDim.x) out[(int64_t)b * H + i] = src[i];
+}
+
+// decode state after a prefill of S tokens: next token = argmax, position S
+__global__ void prefill_end_kernel(const unsigned long long* __restrict__ argmax, int64_t* __restrict__ tokens,
+                                   int* __restrict__ positions, int B, int S) {
+    griddep_wait();
+    const int b = threadIdx.x;
+    if (b < B) {
+        tokens[b] = (int64_t)argmax_key_id(argmax[b]);
+        positions[b] = S;
     }
 }
 
@@ -207,6 +313,16 @@ struct b2_model {
     unsigned long long* h_argmax = nullptr;
     float* h_logits = nullptr;
 
+    // prefill workspace, grown on demand: rows of all prompt tokens
+    int64_t pf_tokens = 0;
+    float* pf_hidden = nullptr;  // [T, H] fp32 residual stream
+    __half* pf_xn = nullptr;     // [T, H] normed activations
+    __half* pf_qkv = nullptr;    // [T, qkv_rows]
+    __half* pf_attn = nullptr;   // [T, nq * D]
+    __half* pf_gate = nullptr;   // [T, inter] (SwiGLU output in place)
+    __half* pf_up = nullptr;     // [T, inter]
+    int64_t* pf_ids = nullptr;   // [T]
+
     std::vector<cudaGraphExec_t> graphs;  // per batch size
     int splits = 1;
     int last_B = 0;  // batch of the most recent prefill / decode step
@@ -242,6 +358,9 @@ extern "C" int b2_model_destroy(b2_model* m) {
     m->graphs.clear();
     if (m->comm) nccl().CommDestroy(m->comm);
     for (void* p : m->allocs) cudaFree(p);
+    for (void* p : {(void*)m->pf_hidden, (void*)m->pf_xn, (void*)m->pf_qkv, (void*)m->pf_attn, (void*)m->pf_gate,
+                    (void*)m->pf_up, (void*)m->pf_ids})
+        cudaFree(p);
     cudaFreeHost(m->h_tokens);
     cudaFreeHost(m->h_pos);
     cudaFreeHost(m->h_argmax);
@@ -717,41 +836,109 @@ extern "C" int b2_model_decode_step(b2_model* m, const int64_t* host_tokens, con
     return B2_OK;
 }
 
+static int ensure_prefill_ws(b2_model* m, int64_t T) {
+    if (T <= m->pf_tokens) return B2_OK;
+    for (void* p : {(void*)m->pf_hidden, (void*)m->pf_xn, (void*)m->pf_qkv, (void*)m->pf_attn, (void*)m->pf_gate,
+                    (void*)m->pf_up, (void*)m->pf_ids})
+        cudaFree(p);
+    m->pf_hidden = nullptr; m->pf_xn = m->pf_qkv = m->pf_attn = m->pf_gate = m->pf_up = nullptr; m->pf_ids = nullptr;
+    m->pf_tokens = 0;
+    const b2_model_config& c = m->cfg;
+    const size_t H = c.hidden_size, hs = sizeof(__half);
+    B2_TRY(cudaMalloc(&m->pf_hidden, T * H * sizeof(float)));
+    B2_TRY(cudaMalloc(&m->pf_xn, T * H * hs));
+    B2_TRY(cudaMalloc(&m->pf_qkv, T * (size_t)m->qkv_rows * hs));
+    B2_TRY(cudaMalloc(&m->pf_attn, T * (size_t)m->nq * c.head_dim * hs));
+    B2_TRY(cudaMalloc(&m->pf_gate, T * (size_t)m->inter * hs));
+    B2_TRY(cudaMalloc(&m->pf_up, T * (size_t)m->inter * hs));
+    B2_TRY(cudaMalloc(&m->pf_ids, T * sizeof(int64_t)));
+    m->pf_tokens = T;
+    return B2_OK;
+}
+
+static int nccl_sum_rows(b2_model* m, float* buf, int64_t rows) {
+    if (m->tp == 1) return B2_OK;
+    if (nccl().AllReduce(buf, buf, (size_t)rows * m->cfg.hidden_size, ncclFloat, ncclSum, m->comm, m->stream) !=
+        ncclSuccess)
+        return B2_ERR_NCCL;
+    return B2_OK;
+}
+
+// All prompt tokens of all sequences through the layers at once: tensor-core
+// GEMMs for every projection, the tensor-core flash prefill for attention,
+// K/V written into the cache, then the lm_head (with argmax) of each
+// sequence's last position through the decode GEMV.
+static int prefill_batched(b2_model* m, int B, int S) {
+    const b2_model_config& c = m->cfg;
+    cudaStream_t st = m->stream;
+    const int64_t T = (int64_t)B * S;
+    const int H = c.hidden_size, D = c.head_dim, I = m->inter, qd = m->nq * D;
+    const int rows = (int)T;
+    embed_rows_kernel<<<(unsigned)T, 128, 0, st>>>(m->pf_ids, m->embed, m->pf_hidden, H);
+    B2_CHECK_LAUNCH();
+    const int norm_threads = H >= 1024 ? 256 : 128;
+    for (int l = 0; l < c.num_layers; ++l) {
+        LayerW& w = m->layers[l];
+        __half* kbase = m->kv + (int64_t)l * m->kv_s_layer;
+        rmsnorm_rows_kernel<<<(unsigned)T, norm_threads, 0, st>>>(m->pf_hidden, w.ln1, m->pf_xn, H, c.rms_norm_eps);
+        B2_CHECK_LAUNCH();
+        M_TRY(gemm_tc(m->pf_xn, w.wqkv, m->pf_qkv, rows, m->qkv_rows, H, TC_HALF, st));
+        if (w.bqkv) M_TRY(b2_bias_add(m->pf_qkv, w.bqkv, m->pf_qkv, T, m->qkv_rows, st));
+        rope_append_kernel<<<dim3((unsigned)T, (unsigned)(m->nq + 2 * m->nkv)), D / 2, 0, st>>>(
+            m->pf_qkv, m->qkv_rows, m->rope, S, m->nq, m->nkv, D, kbase, kbase + m->kv_s_kv, m->kv_s_batch,
+            m->kv_s_head);
+        B2_CHECK_LAUNCH();
+        FlashArgs fa = {};
+        fa.q = m->pf_qkv;
+        fa.k = m->pf_qkv + qd;
+        fa.v = m->pf_qkv + qd + m->nkv * D;
+        fa.out = m->pf_attn;
+        fa.S = S;
+        fa.nq = m->nq;
+        fa.nkv = m->nkv;
+        fa.D = D;
+        fa.batch = B;
+        fa.ldq = fa.ldkv = m->qkv_rows;
+        fa.ldo = qd;
+        int rc = flash_prefill_tc(fa, st);
+        if (rc == B2_ERR_UNSUPPORTED)
+            rc = causal_attention_rows_ld(m->pf_qkv, m->qkv_rows, m->pf_qkv + qd, m->pf_qkv + qd + m->nkv * D,
+                                          m->qkv_rows, m->pf_attn, qd, S, m->nq, m->nkv, D, B, st);
+        M_TRY(rc);
+        M_TRY(gemm_tc(m->pf_attn, w.wo, m->pf_hidden, rows, H, qd, m->rank == 0 ? TC_F32_ADD : TC_F32, st));
+        M_TRY(nccl_sum_rows(m, m->pf_hidden, T));
+        rmsnorm_rows_kernel<<<(unsigned)T, norm_threads, 0, st>>>(m->pf_hidden, w.ln2, m->pf_xn, H, c.rms_norm_eps);
+        B2_CHECK_LAUNCH();
+        M_TRY(gemm_tc(m->pf_xn, w.wg, m->pf_gate, rows, I, H, TC_HALF, st));
+        M_TRY(gemm_tc(m->pf_xn, w.wu, m->pf_up, rows, I, H, TC_HALF, st));
+        M_TRY(b2_swiglu(m->pf_gate, m->pf_up, m->pf_gate, T * I, st));
+        M_TRY(gemm_tc(m->pf_gate, w.wd, m->pf_hidden, rows, H, I, m->rank == 0 ? TC_F32_ADD : TC_F32, st));
+        M_TRY(nccl_sum_rows(m, m->pf_hidden, T));
+    }
+    gather_last_kernel<<<B, 256, 0, st>>>(m->pf_hidden, m->hidden, S, H);
+    B2_CHECK_LAUNCH();
+    B2_TRY(cudaMemsetAsync(m->argmax, 0, (size_t)B * sizeof(unsigned long long), st));
+    M_TRY(launch_lm_head(m, B, false));
+    if (m->tp > 1) {
+        if (nccl().AllReduce(m->argmax, m->argmax, (size_t)B, ncclUint64, ncclMax, m->comm, st) != ncclSuccess)
+            return B2_ERR_NCCL;
+    }
+    prefill_end_kernel<<<1, 32, 0, st>>>(m->argmax, m->tokens, m->positions, B, S);
+    B2_CHECK_LAUNCH();
+    return B2_OK;
+}
+
 extern "C" int b2_model_prefill(b2_model* m, const int64_t* host_ids, int B, int S, float* host_logits) {
     B2_REQUIRE(m && host_ids && B >= 1 && B <= m->cfg.max_batch && S >= 1 && S <= m->cfg.max_seq);
     for (int64_t i = 0; i < (int64_t)B * S; ++i)
         if (host_ids[i] < 0 || host_ids[i] >= m->cfg.vocab_size) return B2_ERR_INVALID;
-    // prompt ids as [S][B] int64 and positions [S][B] on the device, one step per prompt position
-    int64_t* d_ids = nullptr;
-    int* d_pos = nullptr;
-    B2_TRY(cudaMalloc(&d_ids, (size_t)S * B * sizeof(int64_t)));
-    cudaError_t e = cudaMalloc(&d_pos, (size_t)S * B * sizeof(int));
-    if (e != cudaSuccess) { cudaFree(d_ids); return (int)e; }
-    std::vector<int64_t> ids((size_t)S * B);
-    std::vector<int> pos((size_t)S * B);
-    for (int t = 0; t < S; ++t)
-        for (int b = 0; b < B; ++b) {
-            ids[(size_t)t * B + b] = host_ids[(size_t)b * S + t];
-            pos[(size_t)t * B + b] = t;
-        }
-    int rc = B2_OK;
-    e = cudaMemcpyAsync(d_ids, ids.data(), ids.size() * sizeof(int64_t), cudaMemcpyHostToDevice, m->stream);
-    if (e == cudaSuccess) e = cudaMemcpyAsync(d_pos, pos.data(), pos.size() * sizeof(int), cudaMemcpyHostToDevice, m->stream);
-    if (e == cudaSuccess) e = cudaMemsetAsync(m->hist_count, 0, sizeof(int), m->stream);
-    for (int t = 0; t < S && e == cudaSuccess && rc == B2_OK; ++t) {
-        e = cudaMemcpyAsync(m->tokens, d_ids + (size_t)t * B, B * sizeof(int64_t), cudaMemcpyDeviceToDevice, m->stream);
-        if (e == cudaSuccess)
-            e = cudaMemcpyAsync(m->positions, d_pos + (size_t)t * B, B * sizeof(int), cudaMemcpyDeviceToDevice, m->stream);
-        if (e == cudaSuccess) rc = run_step(m, B);
-    }
-    if (e == cudaSuccess && rc == B2_OK) m->last_B = B;
-    if (e == cudaSuccess && rc == B2_OK && host_logits) rc = copy_logits_out(m, B, host_logits);
-    cudaError_t e2 = cudaStreamSynchronize(m->stream);
-    cudaFree(d_ids);
-    cudaFree(d_pos);
-    if (e != cudaSuccess) return (int)e;
-    if (rc != B2_OK) return rc;
-    if (e2 != cudaSuccess) return (int)e2;
+    M_TRY(ensure_prefill_ws(m, (int64_t)B * S));
+    B2_TRY(cudaMemcpyAsync(m->pf_ids, host_ids, (size_t)B * S * sizeof(int64_t), cudaMemcpyHostToDevice, m->stream));
+    B2_TRY(cudaMemsetAsync(m->hist_count, 0, sizeof(int), m->stream));
+    M_TRY(prefill_batched(m, B, S));
+    m->last_B = B;
+    if (host_logits) M_TRY(copy_logits_out(m, B, host_logits));
+    B2_TRY(cudaStreamSynchronize(m->stream));
     return B2_OK;
 }
 

@@ -39,6 +39,18 @@ int causal_attention_rows(const __half* q, const __half* k, const __half* v, __h
                           int nkv, int D, int batch, cudaStream_t s);
 bool attn_head_dim_supported(int D);
 
+struct FlashArgs {
+    const void* q;
+    const void* k;
+    const void* v;
+    void* out;
+    int S, nq, nkv, D, batch;
+    int64_t ldq, ldkv, ldo;  // elements between consecutive tokens
+    bool bf16;
+    float rope_theta;  // > 0: rotate q and k in-kernel
+    int pos0;
+};
+
 template <int D, bool ROPE>
 struct FlashCfg {
     static constexpr int ATOMS = D / 64;                    // 128-byte swizzle atoms per row
@@ -118,8 +130,8 @@ __device__ __forceinline__ void rope_row(uint8_t* tile, int row, int pos, const 
 template <int D, bool BF16, bool ROPE>
 __global__ void __launch_bounds__(FlashCfg<D, ROPE>::THREADS, 1)
     flash_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
-                    const __grid_constant__ CUtensorMap tmV, void* __restrict__ out, int S, int nq, int nkv,
-                    float scale_log2, float rope_theta, int pos0, int* err) {
+                    const __grid_constant__ CUtensorMap tmV, void* __restrict__ out, int64_t ldo, int S, int nq,
+                    int nkv, float scale_log2, float rope_theta, int pos0, int* err) {
     using Cfg = FlashCfg<D, ROPE>;
     constexpr uint32_t TILE = Cfg::TILE;
     extern __shared__ uint8_t smem_raw[];
@@ -342,7 +354,7 @@ __global__ void __launch_bounds__(FlashCfg<D, ROPE>::THREADS, 1)
         tc::fence_after_sync();
         const float inv_l = l > 0.f ? 1.f / l : 0.f;
         using T = typename std::conditional<BF16, __nv_bfloat16, __half>::type;
-        T* orow = static_cast<T*>(out) + (((int64_t)b * S + qpos) * nq + h) * D;
+        T* orow = static_cast<T*>(out) + ((int64_t)b * S + qpos) * ldo + (int64_t)h * D;
 #pragma unroll 1
         for (int c = 0; c < D; c += 32) {
             uint32_t v[32];
@@ -369,8 +381,7 @@ __global__ void __launch_bounds__(FlashCfg<D, ROPE>::THREADS, 1)
 }
 
 template <int D, bool BF16, bool ROPE>
-static int launch_flash(const void* q, const void* k, const void* v, void* out, int S, int nq, int nkv, int batch,
-                        float rope_theta, int pos0, cudaStream_t s) {
+static int launch_flash(const FlashArgs& a, cudaStream_t s) {
     using Cfg = FlashCfg<D, ROPE>;
     int* err = wait_error_word();
     if (!err) return B2_ERR_STATE;
@@ -378,58 +389,78 @@ static int launch_flash(const void* q, const void* k, const void* v, void* out, 
     CUtensorMap tq, tk, tv;
     const uint32_t box[4] = {64, 1, 128, 1};
     {
-        const uint64_t dims[4] = {(uint64_t)D, (uint64_t)nq, (uint64_t)S, (uint64_t)batch};
-        const uint64_t st[3] = {(uint64_t)D * 2, (uint64_t)nq * D * 2, (uint64_t)S * nq * D * 2};
-        const int rc = make_tensor_map(&tq, dt, 4, q, dims, st, box);
+        const uint64_t dims[4] = {(uint64_t)D, (uint64_t)a.nq, (uint64_t)a.S, (uint64_t)a.batch};
+        const uint64_t st[3] = {(uint64_t)D * 2, (uint64_t)a.ldq * 2, (uint64_t)a.S * a.ldq * 2};
+        const int rc = make_tensor_map(&tq, dt, 4, a.q, dims, st, box);
         if (rc != B2_OK) return rc;
     }
     {
-        const uint64_t dims[4] = {(uint64_t)D, (uint64_t)nkv, (uint64_t)S, (uint64_t)batch};
-        const uint64_t st[3] = {(uint64_t)D * 2, (uint64_t)nkv * D * 2, (uint64_t)S * nkv * D * 2};
-        int rc = make_tensor_map(&tk, dt, 4, k, dims, st, box);
+        const uint64_t dims[4] = {(uint64_t)D, (uint64_t)a.nkv, (uint64_t)a.S, (uint64_t)a.batch};
+        const uint64_t st[3] = {(uint64_t)D * 2, (uint64_t)a.ldkv * 2, (uint64_t)a.S * a.ldkv * 2};
+        int rc = make_tensor_map(&tk, dt, 4, a.k, dims, st, box);
         if (rc != B2_OK) return rc;
-        rc = make_tensor_map(&tv, dt, 4, v, dims, st, box);
+        rc = make_tensor_map(&tv, dt, 4, a.v, dims, st, box);
         if (rc != B2_OK) return rc;
     }
     auto kern = flash_tc_kernel<D, BF16, ROPE>;
     B2_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)Cfg::SMEM));
-    dim3 grid((unsigned)((S + 127) / 128), (unsigned)nq, (unsigned)batch);
+    dim3 grid((unsigned)((a.S + 127) / 128), (unsigned)a.nq, (unsigned)a.batch);
     const float scale_log2 = 1.4426950408889634f / sqrtf((float)D);
-    B2_TRY(launch(kern, grid, dim3(Cfg::THREADS), Cfg::SMEM, s, true, tq, tk, tv, out, S, nq, nkv, scale_log2,
-                  rope_theta, pos0, err));
+    B2_TRY(launch(kern, grid, dim3(Cfg::THREADS), Cfg::SMEM, s, true, tq, tk, tv, a.out, a.ldo, a.S, a.nq, a.nkv,
+                  scale_log2, a.rope_theta, a.pos0, err));
     return B2_OK;
 }
 
 template <bool BF16, bool ROPE>
-static int flash_dispatch_d(const void* q, const void* k, const void* v, void* out, int S, int nq, int nkv, int D,
-                            int batch, float theta, int pos0, cudaStream_t s) {
-    if (D == 64) return launch_flash<64, BF16, ROPE>(q, k, v, out, S, nq, nkv, batch, theta, pos0, s);
-    if (D == 128) return launch_flash<128, BF16, ROPE>(q, k, v, out, S, nq, nkv, batch, theta, pos0, s);
+static int flash_dispatch_d(const FlashArgs& a, cudaStream_t s) {
+    if (a.D == 64) return launch_flash<64, BF16, ROPE>(a, s);
+    if (a.D == 128) return launch_flash<128, BF16, ROPE>(a, s);
     return B2_ERR_UNSUPPORTED;
 }
 
-// Tensor-core flash prefill; B2_ERR_UNSUPPORTED for shapes it does not take.
-int flash_prefill_tc(const void* q, const void* k, const void* v, void* out, int64_t S, int nq, int nkv, int D,
-                     int batch, bool bf16, float rope_theta, int pos0, cudaStream_t s) {
-    if ((D != 64 && D != 128) || S <= 0 || S > (1 << 30) || !aligned16(q) || !aligned16(k) || !aligned16(v) ||
-        !aligned16(out) || batch > 65535 || nq > 65535)
+// Tensor-core flash prefill over token-major rows with explicit row strides
+// (elements between consecutive tokens of q, of k/v and of out; heads are D
+// apart inside a row); B2_ERR_UNSUPPORTED for shapes it does not take.
+int flash_prefill_tc(const FlashArgs& a, cudaStream_t s) {
+    if ((a.D != 64 && a.D != 128) || a.S <= 0 || a.S > (1 << 30) || !aligned16(a.q) || !aligned16(a.k) ||
+        !aligned16(a.v) || !aligned16(a.out) || a.batch > 65535 || a.nq > 65535 || (a.ldq & 7) || (a.ldkv & 7) ||
+        (a.ldo & 7))
         return B2_ERR_UNSUPPORTED;
-    const bool rope = rope_theta > 0.f;
-    if (bf16)
-        return rope ? flash_dispatch_d<true, true>(q, k, v, out, (int)S, nq, nkv, D, batch, rope_theta, pos0, s)
-                    : flash_dispatch_d<true, false>(q, k, v, out, (int)S, nq, nkv, D, batch, 0.f, 0, s);
-    return rope ? flash_dispatch_d<false, true>(q, k, v, out, (int)S, nq, nkv, D, batch, rope_theta, pos0, s)
-                : flash_dispatch_d<false, false>(q, k, v, out, (int)S, nq, nkv, D, batch, 0.f, 0, s);
+    const bool rope = a.rope_theta > 0.f;
+    if (a.bf16) return rope ? flash_dispatch_d<true, true>(a, s) : flash_dispatch_d<true, false>(a, s);
+    return rope ? flash_dispatch_d<false, true>(a, s) : flash_dispatch_d<false, false>(a, s);
 }
 
 }  // namespace b2
+
+static b2::FlashArgs dense_args(const void* q, const void* k, const void* v, void* out, int64_t S, int nq, int nkv,
+                                int D, int batch, bool bf16, float theta, int pos0) {
+    b2::FlashArgs a;
+    a.q = q;
+    a.k = k;
+    a.v = v;
+    a.out = out;
+    a.S = (int)S;
+    a.nq = nq;
+    a.nkv = nkv;
+    a.D = D;
+    a.batch = batch;
+    a.ldq = (int64_t)nq * D;
+    a.ldkv = (int64_t)nkv * D;
+    a.ldo = (int64_t)nq * D;
+    a.bf16 = bf16;
+    a.rope_theta = theta;
+    a.pos0 = pos0;
+    return a;
+}
 
 extern "C" int b2_flash_prefill_gqa(const void* q, const void* k, const void* v, void* out, int64_t S, int nq,
                                     int nkv, int D, int batch, void* stream) {
     using namespace b2;
     if (S <= 0 || batch <= 0) return B2_OK;
     B2_REQUIRE(q && k && v && out && nq > 0 && nkv > 0 && nq % nkv == 0);
-    const int rc = flash_prefill_tc(q, k, v, out, S, nq, nkv, D, batch, false, 0.f, 0, as_stream(stream));
+    if (S > (1 << 30)) return B2_ERR_UNSUPPORTED;
+    const int rc = flash_prefill_tc(dense_args(q, k, v, out, S, nq, nkv, D, batch, false, 0.f, 0), as_stream(stream));
     if (rc != B2_ERR_UNSUPPORTED) return rc;
     if (!attn_head_dim_supported(D) || !aligned16(q) || !aligned16(k) || !aligned16(v) || !aligned16(out))
         return B2_ERR_UNSUPPORTED;
@@ -444,6 +475,6 @@ extern "C" int b2_flash_prefill_gqa_ex(const void* q, const void* k, const void*
     if (S <= 0 || batch <= 0) return B2_OK;
     B2_REQUIRE(q && k && v && out && nq > 0 && nkv > 0 && nq % nkv == 0 && rope_theta >= 0.f && start_pos >= 0);
     B2_REQUIRE(start_pos + S < (int64_t)1 << 24);  // positions stay exact in float
-    return flash_prefill_tc(q, k, v, out, S, nq, nkv, D, batch, bf16 != 0, rope_theta, (int)start_pos,
+    return flash_prefill_tc(dense_args(q, k, v, out, S, nq, nkv, D, batch, bf16 != 0, rope_theta, (int)start_pos),
                             as_stream(stream));
 }

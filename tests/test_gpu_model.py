@@ -200,3 +200,27 @@ def test_llama8b_full_width_reduced_depth(cuda):
     theta 5e5) at 2 layers."""
     cfg = O.Config(vocab=128256, hidden=4096, inter=14336, layers=2, nq=32, nkv=8, head_dim=128, theta=500000.0)
     _full_width_check(cfg, 88, 16, 8)
+
+
+def test_batched_prefill_matches_token_by_token(cuda):
+    """The tensor-core prefill (all prompt tokens at once) and the decode step
+    run token by token fill the same KV cache and give the same last logits,
+    up to fp16 rounding of the activations they round at different points."""
+    cfg = O.Config(vocab=800, hidden=512, inter=1024, layers=2, nq=8, nkv=2, head_dim=64, theta=5e5)
+    B, S = 2, 150  # S crosses a 128-query tile boundary
+    rng = np.random.default_rng(21)
+    ids = rng.integers(0, cfg.vocab, (B, S))
+    a = make_model(cfg, 31, max_batch=B, max_seq=160)
+    lg_a = a.prefill(ids)
+    b = make_model(cfg, 31, max_batch=B, max_seq=160)
+    b.prefill(ids[:, :1], want_logits=False)
+    for s in range(1, S):
+        lg_b, _ = b.decode_step(ids[:, s], [s] * B, want_logits=(s == S - 1))
+    sl = a.kv_layout()[0]
+    kv_a = a.read("kv", np.float16, sl * cfg.layers).astype(np.float32)
+    kv_b = b.read("kv", np.float16, sl * cfg.layers).astype(np.float32)
+    assert float(np.max(np.abs(kv_a - kv_b))) < 2e-2
+    for bb in range(B):
+        check_logits(lg_a[bb], lg_b[bb], f"b{bb}")
+    a.close()
+    b.close()
