@@ -369,6 +369,10 @@ def main():
         run_reference(args, rank, world)
         return
     if world > 1:
+        # one node: NCCL's bootstrap goes over loopback (its default pick, the
+        # first non-loopback interface, may not route between local processes);
+        # the data path is NVLink either way
+        os.environ.setdefault("NCCL_SOCKET_IFNAME", "lo")
         import torch.distributed as dist
         dist.init_process_group("gloo", timeout=dt.timedelta(seconds=300))
     try:

@@ -35,6 +35,9 @@ enum {
 
 /* Human-readable text for a status value (static storage). */
 const char* b2_status_string(int status);
+/* Detail text of the last failure a call on this host thread recorded (for
+ * instance NCCL's own message when B2_ERR_NCCL is returned); "" if none. */
+const char* b2_last_error(void);
 /* Build identification, e.g. "b2engine 0.1 sm_100a". */
 const char* b2_version(void);
 

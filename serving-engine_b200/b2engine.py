@@ -23,7 +23,8 @@ u64 = C.c_uint64
 class B2Error(RuntimeError):
     def __init__(self, fn: str, status: int):
         self.status = status
-        super().__init__(f"{fn} failed: status {status} ({status_string(status)})")
+        detail = lib().b2_last_error().decode()
+        super().__init__(f"{fn} failed: status {status} ({status_string(status)})" + (f": {detail}" if detail else ""))
 
 
 class KVView(C.Structure):
@@ -46,6 +47,7 @@ _SIGS = {
     "b2_version": (C.c_char_p, []),
     "b2_status_string": (C.c_char_p, [i32]),
     "b2_device_status": (i32, [i32]),
+    "b2_last_error": (C.c_char_p, []),
     "b2_embedding_lookup": (i32, [vp, vp, vp, i64, i64, vp]),
     "b2_rmsnorm": (i32, [vp, vp, vp, i64, i64, f32, vp]),
     "b2_bias_add": (i32, [vp, vp, vp, i64, i64, vp]),

@@ -239,6 +239,8 @@ struct NcclApi {
     ncclResult_t (*AllReduce)(const void*, void*, size_t, ncclDataType_t, ncclRedOp_t, ncclComm_t,
                               cudaStream_t) = nullptr;
     ncclResult_t (*AllGather)(const void*, void*, size_t, ncclDataType_t, ncclComm_t, cudaStream_t) = nullptr;
+    const char* (*GetErrorString)(ncclResult_t) = nullptr;
+    const char* (*GetLastError)(ncclComm_t) = nullptr;
     bool ok = false;
 };
 
@@ -256,6 +258,8 @@ static NcclApi& nccl() {
         api.CommDestroy = reinterpret_cast<decltype(api.CommDestroy)>(dlsym(h, "ncclCommDestroy"));
         api.AllReduce = reinterpret_cast<decltype(api.AllReduce)>(dlsym(h, "ncclAllReduce"));
         api.AllGather = reinterpret_cast<decltype(api.AllGather)>(dlsym(h, "ncclAllGather"));
+        api.GetErrorString = reinterpret_cast<decltype(api.GetErrorString)>(dlsym(h, "ncclGetErrorString"));
+        api.GetLastError = reinterpret_cast<decltype(api.GetLastError)>(dlsym(h, "ncclGetLastError"));
         api.ok = api.GetUniqueId && api.CommInitRank && api.CommDestroy && api.AllReduce && api.AllGather;
     });
     return api;
@@ -341,6 +345,13 @@ static int model_alloc(b2_model* m, void** p, size_t bytes) {
         if (rc_ != B2_OK) { b2_model_destroy(m); return rc_; }           \
     } while (0)
 
+// Text of the last error a C-ABI call of this thread recorded (NCCL
+// messages, for instance); empty when none.
+static thread_local std::string g_last_error;
+static void set_last_error(const char* msg) { g_last_error = msg ? msg : ""; }
+
+extern "C" const char* b2_last_error(void) { return g_last_error.c_str(); }
+
 extern "C" int b2_nccl_unique_id(void* out128) {
     B2_REQUIRE(out128);
     ncclUniqueId id;
@@ -404,7 +415,20 @@ extern "C" int b2_model_create(const b2_model_config* cfg, int tp_rank, int tp_s
     if (tp_size > 1) {
         ncclUniqueId id;
         memcpy(&id, nccl_id, sizeof(id));
-        if (!nccl().ok || nccl().CommInitRank(&m->comm, tp_size, id, tp_rank) != ncclSuccess) {
+        if (!nccl().ok) {
+            set_last_error("NCCL could not be loaded (libnccl.so.2 / B2_NCCL_LIB)");
+            b2_model_destroy(m);
+            return B2_ERR_NCCL;
+        }
+        const ncclResult_t r = nccl().CommInitRank(&m->comm, tp_size, id, tp_rank);
+        if (r != ncclSuccess) {
+            std::string msg = "ncclCommInitRank: ";
+            msg += nccl().GetErrorString ? nccl().GetErrorString(r) : "error";
+            if (nccl().GetLastError) {
+                msg += ": ";
+                msg += nccl().GetLastError(nullptr);
+            }
+            set_last_error(msg.c_str());
             m->comm = nullptr;
             b2_model_destroy(m);
             return B2_ERR_NCCL;
