@@ -213,6 +213,7 @@ def config_dict(args, world):
             "global_batch": args.batch, "prompt_len": args.prompt,
             "ctx_range": [args.prompt + args.warmup, args.prompt + args.warmup + args.steps],
             "parallelism": f"tp{world}",
+            "tp_exchange": (args.exchange if world > 1 else None),
             "l2": "inputs larger than L2: every step streams ~15 GB of weights (L2 126 MB)"}
 
 
@@ -241,6 +242,12 @@ def run_b2(args, rank, world, local):
                  theta=c["theta"], tied=False, max_batch=B, max_seq=max_seq, tp_rank=rank, tp_size=world,
                  nccl_id=nccl_id)
     m.init_random(SEED_W, 0.02)
+    if world > 1 and args.exchange == "p2p":
+        # decode-step partial sums over NVLink peer memory (fused into the
+        # GEMVs) instead of NCCL all-reduces
+        handles = [None] * world
+        dist.all_gather_object(handles, m.p2p_handle())
+        m.p2p_open(handles)
     prompt = np.random.default_rng(SEED_P).integers(0, c["vocab"], (B, args.prompt))
     m.prefill(prompt, want_logits=False)  # first call: workspace allocation, module load
     m.reset()
@@ -357,6 +364,8 @@ def main():
     ap.add_argument("--batch", type=int, default=1)
     ap.add_argument("--impl", default="b2", choices=["b2", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--exchange", default="p2p", choices=["p2p", "nccl"],
+                    help="tensor-parallel decode reduction: fused peer-memory exchange or NCCL all-reduce")
     ap.add_argument("--prompt", type=int, default=PROMPT, help="prompt length (512 for the metric)")
     ap.add_argument("--layers", type=int, default=LLAMA8B["layers"],
                     help="decoder depth (reduced only for small profiler captures; the metric uses 32)")

@@ -249,6 +249,20 @@ int b2_model_create(const b2_model_config* cfg, int tp_rank, int tp_size, const 
                     b2_model** out);
 int b2_model_destroy(b2_model* m);
 
+/* Tensor-parallel exchange over peer memory (one node, tp_size > 1).  Each
+ * rank exports the 64-byte CUDA IPC handle of its exchange buffer; the
+ * caller all-gathers the tp handles (rank order) with its own launcher and
+ * passes them to b2_model_p2p_open on every rank.  From then on the decode
+ * step runs without NCCL: the o and down GEMVs store their fp32 partial rows
+ * into every rank's receive slots over NVLink as 8-byte words tagged with
+ * the exchange's epoch, and the next GEMV's RMSNorm prologue polls (bounded,
+ * about a second) until the words it needs carry the epoch, then sums the
+ * slots in rank order; the lm_head's argmax is exchanged with one flag per
+ * rank.  Without b2_model_p2p_open the step uses NCCL
+ * all-reduces.  New API (the reference has no parallelism). */
+int b2_model_p2p_handle(b2_model* m, void* out64);
+int b2_model_p2p_open(b2_model* m, const void* handles);
+
 /* Fills every weight from the seeded generator (identical global tensors at
  * any tp_size; norm weights 1.0).  Synchronises. */
 int b2_model_init_random(b2_model* m, uint64_t seed, float stddev);
@@ -322,6 +336,17 @@ double b2_model_kernel_bytes(const b2_model* m, int kind, int batch, int ctx);
 
 /* Number of kernel launches one decode step issues (for reporting). */
 int b2_model_step_launches(const b2_model* m, int batch);
+
+/* Runs one decode step (not from its captured graph) with every kernel
+ * recording, in %globaltimer nanoseconds, when its first CTA passed its
+ * programmatic-launch wait and when its last CTA finished: host_ns receives
+ * (start, end) pairs in launch order, *n_slots the number of launches.
+ * Advances the sequences like b2_model_decode_step (tokens and positions
+ * from the device state).  Allocates its buffer on first use; synchronises.
+ * Under tensor parallelism every rank calls it together.  No reference
+ * counterpart beyond its per-launch CudaTimer records
+ * (src/model/forward_gpu.cu:542-551). */
+int b2_model_trace_step(b2_model* m, int batch, unsigned long long* host_ns, int max_slots, int* n_slots);
 
 #ifdef __cplusplus
 }

@@ -77,6 +77,9 @@ _SIGS = {
     "b2_model_create": (i32, [C.POINTER(ModelConfig), i32, i32, vp, C.POINTER(vp)]),
     "b2_model_destroy": (i32, [vp]),
     "b2_model_init_random": (i32, [vp, u64, f32]),
+    "b2_model_p2p_handle": (i32, [vp, vp]),
+    "b2_model_p2p_open": (i32, [vp, vp]),
+    "b2_model_trace_step": (i32, [vp, i32, vp, i32, C.POINTER(i32)]),
     "b2_model_set_tensor": (i32, [vp, C.c_char_p, vp, i64, i64]),
     "b2_model_reset": (i32, [vp]),
     "b2_model_prefill": (i32, [vp, vp, i32, i32, vp]),
@@ -236,6 +239,29 @@ class Model:
 
     def init_random(self, seed: int, std: float = 0.02):
         call("b2_model_init_random", self.h, seed, std)
+
+    def trace_step(self, batch: int):
+        """One decode step with per-launch device timestamps: an array of
+        (start_ns, end_ns) rows in launch order, relative to the first start."""
+        import numpy as np
+        n = self.step_launches(batch)
+        buf = np.zeros(2 * n, np.uint64)
+        got = i32(0)
+        call("b2_model_trace_step", self.h, batch, buf.ctypes.data, n, C.byref(got))
+        t = buf[: 2 * got.value].astype(np.int64).reshape(-1, 2)
+        return t - t[0, 0]
+
+    def p2p_handle(self) -> bytes:
+        """64-byte CUDA IPC handle of this rank's tensor-parallel exchange buffer."""
+        buf = C.create_string_buffer(64)
+        call("b2_model_p2p_handle", self.h, buf)
+        return buf.raw
+
+    def p2p_open(self, handles) -> None:
+        """Map every rank's exchange buffer (handles in rank order); the decode
+        step then exchanges partial sums over NVLink instead of NCCL."""
+        blob = C.create_string_buffer(b"".join(handles), 64 * len(handles))
+        call("b2_model_p2p_open", self.h, blob)
 
     def set_tensor(self, name: str, arr16):
         import numpy as np

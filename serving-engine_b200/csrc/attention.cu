@@ -60,6 +60,7 @@ struct AttnParams {
     // at least two kernels earlier, so they may be read before the
     // programmatic-launch wait.
     int early_kv;
+    TraceSlot trace;
 };
 
 constexpr int kAttnWarps = 4;
@@ -96,6 +97,7 @@ __global__ void __launch_bounds__(kAttnThreads) attn_decode_kernel(const AttnPar
     if (!p.early_kv) {
         griddep_wait();
         griddep_launch_dependents();
+        trace_begin(p.trace);
     }
 
     const int L = p.causal_base >= 0 ? p.causal_base + b + 1 : (p.seq_lens ? p.seq_lens[b] : p.len_const);
@@ -129,6 +131,7 @@ __global__ void __launch_bounds__(kAttnThreads) attn_decode_kernel(const AttnPar
     if (p.early_kv) {
         griddep_wait();
         griddep_launch_dependents();
+        trace_begin(p.trace);
 #pragma unroll
         for (int u = 0; u < UNR; ++u) {
             const int pos = base + u * PPW + pidx;
@@ -261,7 +264,11 @@ __global__ void __launch_bounds__(kAttnThreads) attn_decode_kernel(const AttnPar
             if (d == 0) p.ml[r] = make_float2(M, Ls);
         }
     }
-    if (direct) return;
+    if (direct) {
+        __syncthreads();
+        trace_end(p.trace);
+        return;
+    }
 
     // ---- last CTA of this (sequence, kv head, head group) merges the splits
     __shared__ int s_last;
@@ -270,7 +277,10 @@ __global__ void __launch_bounds__(kAttnThreads) attn_decode_kernel(const AttnPar
     int* ctr = p.counters + ((int64_t)b * p.nkv + kvh) * p.hg + hgi;
     if (threadIdx.x == 0) s_last = atomicAdd(ctr, 1) == n_used - 1;
     __syncthreads();
-    if (!s_last) return;
+    if (!s_last) {
+        trace_end(p.trace);
+        return;
+    }
     __threadfence();
     // per head: normalised weight of every split, exp2(m_s - M) / sum, in shared memory
     for (int g = warp; g < nh; g += kAttnWarps) {
@@ -308,6 +318,8 @@ __global__ void __launch_bounds__(kAttnThreads) attn_decode_kernel(const AttnPar
         p.out[(int64_t)b * p.o_sb + (int64_t)(h0 + g) * D + d] = __float2half_rn(A);
     }
     if (threadIdx.x == 0) *ctr = 0;
+    __syncthreads();
+    trace_end(p.trace);
 }
 
 template <int D>
@@ -531,7 +543,7 @@ int attn_decode_launch_model(const __half* q, const __half* kbase, const __half*
 // more than the newest row).
 int attn_decode_launch_step(const __half* q, const __half* kbase, const __half* vbase, int64_t sb, int64_t sh,
                             int64_t ss, const int* seq_lens, __half* out, float* part, int splits, int B, int nq,
-                            int nkv, int D, cudaStream_t s) {
+                            int nkv, int D, cudaStream_t s, TraceSlot trace) {
     AttnParams p = {};
     p.q = q;
     p.q_sb = (int64_t)nq * D;
@@ -550,6 +562,7 @@ int attn_decode_launch_step(const __half* q, const __half* kbase, const __half* 
     p.part = part;
     p.splits = splits;
     p.early_kv = 1;
+    p.trace = trace;
     return attn_decode_launch(p, B, D, s, true);
 }
 }  // namespace b2

@@ -81,6 +81,28 @@ __device__ __forceinline__ void griddep_launch_dependents() {
     asm volatile("griddepcontrol.launch_dependents;" :::);
 }
 
+// Step trace: one (start, end) pair of %globaltimer nanoseconds per launch
+// slot; start = the first CTA past its programmatic-launch wait, end = the
+// last CTA to finish.  buf == nullptr: tracing off.
+struct TraceSlot {
+    unsigned long long* buf;
+    int slot;
+};
+
+__device__ __forceinline__ unsigned long long globaltimer_ns() {
+    unsigned long long t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+}
+
+__device__ __forceinline__ void trace_begin(const TraceSlot& tr) {
+    if (tr.buf && threadIdx.x == 0) atomicMin(tr.buf + 2 * tr.slot, globaltimer_ns());
+}
+
+__device__ __forceinline__ void trace_end(const TraceSlot& tr) {
+    if (tr.buf && threadIdx.x == 0) atomicMax(tr.buf + 2 * tr.slot + 1, globaltimer_ns());
+}
+
 // 16-byte streaming load that bypasses L1 allocation (weights are read once).
 __device__ __forceinline__ uint4 ldg_stream(const void* p) {
     uint4 r;

@@ -81,35 +81,146 @@ __device__ __forceinline__ void task_rows(const GemvParams& p, int t, const uint
     }
 }
 
+template <int OM>
+constexpr bool kBlockRowsSmem() { return OM == OUT_PUSH; }
+
 template <int R, int BT, int XM, int OM, int U>
 __global__ void __launch_bounds__(kGemvThreads, 2) gemv_vec_kernel(const GemvParams p) {
     extern __shared__ __align__(16) uint4 xs[];  // [BT][K8] packed half
     __shared__ float s_rs[BT];
     __shared__ float s_ss[BT][kGemvWarps];
     __shared__ unsigned long long s_best[kGemvWarps][BT];
+    __shared__ __align__(16) float s_push[kBlockRowsSmem<OM>() ? BT : 1][kBlockRowsSmem<OM>() ? kPushRows : 1];
 
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const int K8 = p.K >> 3;
     const int NB = (K8 + 32 * U - 1) / (32 * U);
+    // Tasks are dealt round-robin over all warps of the grid, except for
+    // OUT_PUSH, where each CTA owns a contiguous block of rows so that it can
+    // push them to the other ranks as 16-byte stores once its stream is done.
+    constexpr bool kBlockRows = OM == OUT_PUSH;
     const int total_warps = gridDim.x * kGemvWarps;
-    int t = blockIdx.x * kGemvWarps + warp;
+    const int row0 = kBlockRows ? blockIdx.x * p.rows_per_cta : 0;
+    const int t_step = kBlockRows ? kGemvWarps : total_warps;
+    const int t_end = kBlockRows ? min(p.tasks, row0 + p.rows_per_cta) : p.tasks;
+    int t = kBlockRows ? row0 + warp : blockIdx.x * kGemvWarps + warp;
 
     // Weights do not depend on the previous kernel: start streaming them now.
     uint4 wn[R][U];
-    if (t < p.tasks) {
+    if (t < t_end) {
         const uint4* rp[R];
         task_rows<R, OM>(p, t, rp);
         load_rows<R, U>(wn, rp, 0, K8, lane);
     }
 
-    griddep_wait();
+    // X_SUM reads the previous kernel's output only through the tagged
+    // exchange words it polls, and everything else it reads or overwrites was
+    // last touched two or more kernels back (whose completion the previous
+    // kernel's own wait implied), so it skips the programmatic-launch wait
+    // and starts polling as soon as it is resident.
+    if constexpr (XM != X_SUM) griddep_wait();
     griddep_launch_dependents();
+    trace_begin(p.trace);
 
     // ---- stage x in shared memory --------------------------------------
-    if constexpr (XM == X_NORM) {
+    if constexpr (XM == X_SUM) {
+        // h = hid_in + every rank's tagged partial words, summed in rank
+        // order; staged as half in xs, then normalised in place once the
+        // CTA has the sum of squares.  Loads for two ranks at a time are
+        // issued together (one L2 round trip per pair of ranks per chunk).
+        const unsigned tag = (unsigned)(*p.tpx.step) * (unsigned)p.nslots + (unsigned)p.slot + 1u;
+        const unsigned par = tag & 1u;
+        float ss[BT];
+#pragma unroll
+        for (int b = 0; b < BT; ++b) ss[b] = 0.f;
+        for (int i = threadIdx.x; i < BT * K8; i += kGemvThreads) {
+            const int b = i / K8, c = i - b * K8;
+            uint4 o = make_uint4(0, 0, 0, 0);
+            if (b < p.B) {
+                float h[8];
+                {
+                    const float4* hr = reinterpret_cast<const float4*>(p.hid_in + (size_t)b * p.ldx) + 2 * c;
+                    const float4 a0 = __ldcg(hr), a1 = __ldcg(hr + 1);
+                    h[0] = a0.x; h[1] = a0.y; h[2] = a0.z; h[3] = a0.w;
+                    h[4] = a1.x; h[5] = a1.y; h[6] = a1.z; h[7] = a1.w;
+                }
+                for (int r0 = 0; r0 < p.tpx.tp; r0 += 2) {
+                    unsigned long long w[2][8];
+#pragma unroll
+                    for (int q = 0; q < 2; ++q) {
+                        if (r0 + q < p.tpx.tp) {
+                            const unsigned long long* src =
+                                p.tpx.recv + (((size_t)par * p.tpx.tp + r0 + q) * p.tpx.Bmax + b) * p.tpx.H + 8 * (size_t)c;
+#pragma unroll
+                            for (int k = 0; k < 8; k += 2)
+                                asm volatile("ld.volatile.global.v2.u64 {%0, %1}, [%2];"
+                                             : "=l"(w[q][k]), "=l"(w[q][k + 1])
+                                             : "l"(src + k)
+                                             : "memory");
+                        }
+                    }
+#pragma unroll
+                    for (int q = 0; q < 2; ++q) {
+                        if (r0 + q < p.tpx.tp) {
+                            const unsigned long long* src =
+                                p.tpx.recv + (((size_t)par * p.tpx.tp + r0 + q) * p.tpx.Bmax + b) * p.tpx.H + 8 * (size_t)c;
+#pragma unroll
+                            for (int k = 0; k < 8; k += 2) {
+                                float2 v;
+                                if ((unsigned)(w[q][k] >> 32) == tag && (unsigned)(w[q][k + 1] >> 32) == tag)
+                                    v = make_float2(__uint_as_float((unsigned)w[q][k]), __uint_as_float((unsigned)w[q][k + 1]));
+                                else
+                                    ll_load2(src + k, tag, v, p.tpx.err, 100 + p.slot);
+                                h[k] += v.x;
+                                h[k + 1] += v.y;
+                            }
+                        }
+                    }
+                }
+                if (blockIdx.x == 0) {  // the residual stream after the exchange
+                    float4* ho = reinterpret_cast<float4*>(p.hid_out + (size_t)b * p.ldx) + 2 * c;
+                    ho[0] = make_float4(h[0], h[1], h[2], h[3]);
+                    ho[1] = make_float4(h[4], h[5], h[6], h[7]);
+                }
+#pragma unroll
+                for (int k = 0; k < 8; ++k) {
+#pragma unroll
+                    for (int bb = 0; bb < BT; ++bb)
+                        if (bb == b) ss[bb] = fmaf(h[k], h[k], ss[bb]);
+                }
+                o = pack8(h);
+            }
+            xs[i] = o;
+        }
+#pragma unroll
+        for (int b = 0; b < BT; ++b) {
+            const float v = warp_sum(ss[b]);
+            if (lane == 0) s_ss[b][warp] = v;
+        }
+        __syncthreads();
+        if (threadIdx.x < BT) {
+            float tot = 0.f;
+#pragma unroll
+            for (int w = 0; w < kGemvWarps; ++w) tot += s_ss[threadIdx.x][w];
+            s_rs[threadIdx.x] = rsqrtf(tot / (float)p.K + p.eps);
+        }
+        __syncthreads();
+        for (int i = threadIdx.x; i < BT * K8; i += kGemvThreads) {
+            const int b = i / K8, c = i - b * K8;
+            if (b < p.B) {
+                float f[8], wv[8];
+                unpack8(xs[i], f);
+                unpack8(ldg16(reinterpret_cast<const uint4*>(p.norm_w) + c), wv);
+                const float r = s_rs[b];
+#pragma unroll
+                for (int k = 0; k < 8; ++k) f[k] = f[k] * r * wv[k];
+                xs[i] = pack8(f);
+            }
+        }
+    } else if constexpr (XM == X_NORM) {
+        const float* hrow = static_cast<const float*>(p.x);
         // Sum of squares of each sequence's fp32 residual row, spread over the
         // whole CTA so the loads are independent (one L2 round trip, not K/128).
-        const float* h = static_cast<const float*>(p.x);
         float ss[BT];
 #pragma unroll
         for (int b = 0; b < BT; ++b) ss[b] = 0.f;
@@ -118,7 +229,7 @@ __global__ void __launch_bounds__(kGemvThreads, 2) gemv_vec_kernel(const GemvPar
 #pragma unroll
             for (int b = 0; b < BT; ++b) {
                 if (b < p.B) {
-                    const float4 v = reinterpret_cast<const float4*>(h + (size_t)b * p.ldx)[i];
+                    const float4 v = reinterpret_cast<const float4*>(hrow + (size_t)b * p.ldx)[i];
                     ss[b] = fmaf(v.x, v.x, ss[b]); ss[b] = fmaf(v.y, v.y, ss[b]);
                     ss[b] = fmaf(v.z, v.z, ss[b]); ss[b] = fmaf(v.w, v.w, ss[b]);
                 }
@@ -141,7 +252,7 @@ __global__ void __launch_bounds__(kGemvThreads, 2) gemv_vec_kernel(const GemvPar
             const int b = i / K8, c = i - b * K8;
             uint4 o = make_uint4(0, 0, 0, 0);
             if (b < p.B) {
-                const float4* hr = reinterpret_cast<const float4*>(h + (size_t)b * p.ldx) + 2 * c;
+                const float4* hr = reinterpret_cast<const float4*>(hrow + (size_t)b * p.ldx) + 2 * c;
                 const float4 a0 = hr[0], a1 = hr[1];
                 float wv[8];
                 unpack8(ldg16(reinterpret_cast<const uint4*>(p.norm_w) + c), wv);
@@ -165,9 +276,14 @@ __global__ void __launch_bounds__(kGemvThreads, 2) gemv_vec_kernel(const GemvPar
     unsigned long long best[BT];
 #pragma unroll
     for (int b = 0; b < BT; ++b) best[b] = 0ull;
+    unsigned push_epoch = 0, push_par = 0;
+    if constexpr (OM == OUT_PUSH) {
+        push_epoch = (unsigned)(*p.tpx.step) * (unsigned)p.nslots + (unsigned)p.slot + 1u;
+        push_par = push_epoch & 1u;
+    }
 
     // ---- stream the warp's tasks ---------------------------------------
-    for (; t < p.tasks; t += total_warps) {
+    for (; t < t_end; t += t_step) {
         float acc[R][BT];
 #pragma unroll
         for (int r = 0; r < R; ++r)
@@ -183,8 +299,8 @@ __global__ void __launch_bounds__(kGemvThreads, 2) gemv_vec_kernel(const GemvPar
             // issue the next batch (this task's next chunk batch, or the next task's first)
             {
                 int nt = t, ncb = cb + 1;
-                if (ncb == NB) { nt = t + total_warps; ncb = 0; }
-                if (nt < p.tasks) {
+                if (ncb == NB) { nt = t + t_step; ncb = 0; }
+                if (nt < t_end) {
                     const uint4* rp[R];
                     task_rows<R, OM>(p, nt, rp);
                     load_rows<R, U>(wn, rp, ncb * 32 * U, K8, lane);
@@ -235,6 +351,8 @@ __global__ void __launch_bounds__(kGemvThreads, 2) gemv_vec_kernel(const GemvPar
             } else if constexpr (OM == OUT_RESID) {
                 float* y = static_cast<float*>(p.y) + (size_t)b * p.ldy + t;
                 *y = p.resid_add ? *y + acc[0][b] : acc[0][b];
+            } else if constexpr (OM == OUT_PUSH) {
+                s_push[b][t - row0] = acc[0][b];
             } else if constexpr (OM == OUT_LOGITS) {
                 static_cast<float*>(p.y)[(size_t)b * p.ldy + t] = acc[0][b];
             } else if constexpr (OM == OUT_SWIGLU) {
@@ -271,6 +389,22 @@ __global__ void __launch_bounds__(kGemvThreads, 2) gemv_vec_kernel(const GemvPar
         }
     }
 
+    if constexpr (OM == OUT_PUSH) {
+        // this CTA's block of partial rows, as tagged 8-byte words (two per
+        // 16-byte store) into slot [parity][rank] of every rank
+        __syncthreads();
+        const int n2 = (t_end - row0) >> 1;  // rows_per_cta and H are even
+        const int per_rank = p.B * n2;
+        for (int i = threadIdx.x; i < p.tpx.tp * per_rank; i += kGemvThreads) {
+            const int r = i / per_rank, rem = i - r * per_rank;
+            const int b = rem / n2, c2 = rem - b * n2;
+            unsigned long long* dst = p.tpx.peer_recv[r] +
+                                      (((size_t)push_par * p.tpx.tp + p.tpx.rank) * p.tpx.Bmax + b) * p.tpx.H + row0 +
+                                      2 * c2;
+            ll_store2(dst, ll_word(s_push[b][2 * c2], push_epoch), ll_word(s_push[b][2 * c2 + 1], push_epoch));
+        }
+    }
+
     if constexpr (OM == OUT_LOGITS) {
         if (lane == 0) {
 #pragma unroll
@@ -282,7 +416,28 @@ __global__ void __launch_bounds__(kGemvThreads, 2) gemv_vec_kernel(const GemvPar
             for (int w = 0; w < kGemvWarps; ++w) m = s_best[w][threadIdx.x] > m ? s_best[w][threadIdx.x] : m;
             if (m) atomicMax(p.argmax + threadIdx.x, m);
         }
+        if (p.tp_on) {
+            // the last CTA hands this vocabulary shard's argmax to every rank
+            __syncthreads();
+            if (threadIdx.x == 0) {
+                __threadfence();
+                if (atomicAdd(p.tpx.ctr, 1) == (int)gridDim.x - 1) {
+                    __threadfence();
+                    const unsigned tag = (unsigned)(*p.tpx.step) + 1u;
+                    for (int b = 0; b < p.B; ++b) {
+                        const unsigned long long v = atomicAdd(p.argmax + b, 0ull);
+                        for (int r = 0; r < p.tpx.tp; ++r)
+                            p.tpx.peer_am_recv[r][(size_t)p.tpx.rank * p.tpx.Bmax + b] = v;
+                    }
+                    *p.tpx.ctr = 0;
+                    fence_acq_rel_sys();
+                    for (int r = 0; r < p.tpx.tp; ++r) store_release_sys(p.tpx.peer_am_flags[r] + p.tpx.rank, tag);
+                }
+            }
+        }
     }
+    __syncthreads();
+    trace_end(p.trace);
 }
 
 // ---------------------------------------------------------------------------
@@ -310,8 +465,14 @@ static int launch_vec(const GemvParams& p, cudaStream_t s, bool pdl) {
     const int max_warps = sm_count() * last_occ * kGemvWarps;
     const int rounds = (p.tasks + max_warps - 1) / max_warps;
     const int warps = (p.tasks + rounds - 1) / rounds;
-    const int ctas = (warps + kGemvWarps - 1) / kGemvWarps;
-    B2_TRY(launch(kern, dim3(ctas), dim3(kGemvThreads), smem, s, pdl, p));
+    int ctas = (warps + kGemvWarps - 1) / kGemvWarps;
+    GemvParams q = p;
+    if (OM == OUT_PUSH) {
+        q.rows_per_cta = kGemvWarps * rounds;
+        if (q.rows_per_cta > kPushRows || (p.tasks & 7)) return B2_ERR_UNSUPPORTED;
+        ctas = (p.tasks + q.rows_per_cta - 1) / q.rows_per_cta;
+    }
+    B2_TRY(launch(kern, dim3(ctas), dim3(kGemvThreads), smem, s, pdl, q));
     return B2_OK;
 }
 
@@ -336,14 +497,22 @@ int gemv_launch(const GemvParams& p, XMode xm, OutMode om, cudaStream_t s, bool 
     if (p.K <= 0 || (p.K & 7) || !aligned16(p.W) || !aligned16(p.x) || (p.ldx & 7)) return B2_ERR_UNSUPPORTED;
     if (p.B > 8 || p.B > gemv_batch_tile(p.K)) return B2_ERR_UNSUPPORTED;
     if (om == OUT_SWIGLU && !aligned16(p.W2)) return B2_ERR_UNSUPPORTED;
-    if (xm == X_NORM && (!p.norm_w || !aligned16(p.norm_w))) return B2_ERR_UNSUPPORTED;
+    if ((xm == X_NORM || xm == X_SUM) && (!p.norm_w || !aligned16(p.norm_w))) return B2_ERR_UNSUPPORTED;
+    if ((xm == X_SUM || om == OUT_PUSH) && (!p.tp_on || p.tpx.tp < 1 || p.tpx.tp > kMaxTp)) return B2_ERR_INVALID;
     switch (om) {
         case OUT_HALF: return dispatch_bt<1, X_HALF, OUT_HALF, 8>(p, s, pdl);
         case OUT_F32:  return dispatch_bt<1, X_HALF, OUT_F32, 8>(p, s, pdl);
         case OUT_RESID: return dispatch_bt<1, X_HALF, OUT_RESID, 8>(p, s, pdl);
-        case OUT_QKV:  return xm == X_NORM ? dispatch_bt<2, X_NORM, OUT_QKV, 4>(p, s, pdl) : B2_ERR_UNSUPPORTED;
-        case OUT_SWIGLU: return xm == X_NORM ? dispatch_bt<2, X_NORM, OUT_SWIGLU, 4>(p, s, pdl) : B2_ERR_UNSUPPORTED;
-        case OUT_LOGITS: return xm == X_NORM ? dispatch_bt<1, X_NORM, OUT_LOGITS, 8>(p, s, pdl) : B2_ERR_UNSUPPORTED;
+        case OUT_PUSH: return p.tp_on ? dispatch_bt<1, X_HALF, OUT_PUSH, 8>(p, s, pdl) : B2_ERR_INVALID;
+        case OUT_QKV:
+            if (xm == X_SUM) return dispatch_bt<2, X_SUM, OUT_QKV, 4>(p, s, pdl);
+            return xm == X_NORM ? dispatch_bt<2, X_NORM, OUT_QKV, 4>(p, s, pdl) : B2_ERR_UNSUPPORTED;
+        case OUT_SWIGLU:
+            if (xm == X_SUM) return dispatch_bt<2, X_SUM, OUT_SWIGLU, 4>(p, s, pdl);
+            return xm == X_NORM ? dispatch_bt<2, X_NORM, OUT_SWIGLU, 4>(p, s, pdl) : B2_ERR_UNSUPPORTED;
+        case OUT_LOGITS:
+            if (xm == X_SUM) return dispatch_bt<1, X_SUM, OUT_LOGITS, 8>(p, s, pdl);
+            return xm == X_NORM ? dispatch_bt<1, X_NORM, OUT_LOGITS, 8>(p, s, pdl) : B2_ERR_UNSUPPORTED;
     }
     return B2_ERR_UNSUPPORTED;
 }

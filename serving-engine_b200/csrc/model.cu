@@ -43,7 +43,7 @@ size_t attn_scratch_floats(int batch, int nq, int nkv, int D, int splits);
 bool attn_head_dim_supported(int D);
 int attn_decode_launch_step(const __half* q, const __half* kbase, const __half* vbase, int64_t sb, int64_t sh,
                             int64_t ss, const int* seq_lens, __half* out, float* part, int splits, int B, int nq,
-                            int nkv, int D, cudaStream_t s);
+                            int nkv, int D, cudaStream_t s, TraceSlot trace);
 
 struct FlashArgs {
     const void* q;
@@ -61,6 +61,7 @@ int causal_attention_rows_ld(const __half* q, int64_t ldq, const __half* k, cons
                              __half* out, int64_t ldo, int64_t S, int nq, int nkv, int D, int batch, cudaStream_t s);
 enum TcEpi : int { TC_HALF = 0, TC_F32 = 1, TC_F32_ADD = 2 };
 int gemm_tc(const __half* A, const __half* B, void* C, int M, int N, int K, int epi, cudaStream_t s);
+int* wait_error_word();
 
 // ---------------------------------------------------------------------------
 // seeded initialisation (bit-identical to oracle/b2oracle.c ora_init_value)
@@ -98,9 +99,11 @@ __global__ void fill_half_kernel(__half* dst, int64_t n, float v) {
 __global__ void step_begin_kernel(const int64_t* __restrict__ tokens, const int* __restrict__ positions,
                                   const __half* __restrict__ embed, float* __restrict__ hidden, int H,
                                   int* __restrict__ seq_lens, unsigned long long* __restrict__ argmax,
-                                  int64_t* __restrict__ hist, const int* __restrict__ hist_count, int hist_cap) {
+                                  int64_t* __restrict__ hist, const int* __restrict__ hist_count, int hist_cap,
+                                  TraceSlot trace) {
     griddep_wait();
     griddep_launch_dependents();
+    trace_begin(trace);
     const int b = blockIdx.x;
     const int64_t id = tokens[b];
     const uint4* src = reinterpret_cast<const uint4*>(embed + id * H);
@@ -118,14 +121,36 @@ __global__ void step_begin_kernel(const int64_t* __restrict__ tokens, const int*
         const int c = *hist_count;
         if (c < hist_cap) hist[(int64_t)c * gridDim.x + b] = id;
     }
+    __syncthreads();
+    trace_end(trace);
 }
 
-// token[b] = argmax id, pos[b] += 1, history counter += 1.
+// token[b] = argmax id, pos[b] += 1, history counter += 1.  With the peer
+// exchange on, the argmax is the max over every rank's vocabulary shard
+// (bounded wait for their flags) and the step counter advances.
 __global__ void step_end_kernel(const unsigned long long* __restrict__ argmax, int64_t* __restrict__ tokens,
-                                int* __restrict__ positions, int B, int* __restrict__ hist_count, int hist_cap) {
+                                int* __restrict__ positions, int B, int* __restrict__ hist_count, int hist_cap,
+                                int tp_on, const unsigned long long* am_recv, const unsigned* am_flags, int tp,
+                                int Bmax, int* step, int* err, TraceSlot trace) {
     griddep_wait();
+    trace_begin(trace);
     const int b = threadIdx.x;
-    if (b < B) {
+    if (tp_on) {
+        const unsigned tag = (unsigned)(*step) + 1u;
+        if (b < tp) wait_flag_geq(am_flags + b, tag, err, 99);
+        __syncthreads();
+        if (b < B) {
+            unsigned long long best = 0ull;
+            for (int r = 0; r < tp; ++r) {
+                const unsigned long long v = __ldcg(am_recv + (size_t)r * Bmax + b);
+                best = v > best ? v : best;
+            }
+            tokens[b] = (int64_t)argmax_key_id(best);
+            positions[b] += 1;
+        }
+        __syncthreads();
+        if (b == 0) *step += 1;
+    } else if (b < B) {
         tokens[b] = (int64_t)argmax_key_id(argmax[b]);
         positions[b] += 1;
     }
@@ -133,6 +158,8 @@ __global__ void step_end_kernel(const unsigned long long* __restrict__ argmax, i
         const int c = *hist_count;
         if (c < hist_cap) *hist_count = c + 1;
     }
+    __syncthreads();
+    trace_end(trace);
 }
 
 // ---------------------------------------------------------------------------
@@ -327,6 +354,20 @@ struct b2_model {
     __half* pf_up = nullptr;     // [T, inter]
     int64_t* pf_ids = nullptr;   // [T]
 
+    // tensor-parallel exchange over peer memory (see TpExchange)
+    void* p2p_base = nullptr;           // this rank's exchange region (IPC-exported)
+    size_t p2p_bytes = 0;
+    size_t off_recv = 0, off_am_recv = 0, off_am_flags = 0;
+    std::vector<void*> peer_bases;      // opened IPC mappings (index = rank; own = p2p_base)
+    float* hidden2 = nullptr;           // second residual-stream buffer
+    int* step_ctr = nullptr;            // decode steps completed
+    int* push_ctr = nullptr;            // arrival counter of pushing kernels
+    bool p2p_on = false;
+    TpExchange tpx{};
+    unsigned long long* trace_buf = nullptr;  // step trace [slots][start, end]
+    unsigned long long* trace_cur = nullptr;  // non-null while a traced step is enqueued
+    int trace_next = 0;
+
     std::vector<cudaGraphExec_t> graphs;  // per batch size
     int splits = 1;
     int last_B = 0;  // batch of the most recent prefill / decode step
@@ -368,7 +409,10 @@ extern "C" int b2_model_destroy(b2_model* m) {
         if (g) cudaGraphExecDestroy(g);
     m->graphs.clear();
     if (m->comm) nccl().CommDestroy(m->comm);
+    for (size_t r = 0; r < m->peer_bases.size(); ++r)
+        if (m->peer_bases[r] && m->peer_bases[r] != m->p2p_base) cudaIpcCloseMemHandle(m->peer_bases[r]);
     for (void* p : m->allocs) cudaFree(p);
+    cudaFree(m->trace_buf);
     for (void* p : {(void*)m->pf_hidden, (void*)m->pf_xn, (void*)m->pf_qkv, (void*)m->pf_attn, (void*)m->pf_gate,
                     (void*)m->pf_up, (void*)m->pf_ids})
         cudaFree(p);
@@ -497,6 +541,24 @@ extern "C" int b2_model_create(const b2_model_config* cfg, int tp_rank, int tp_s
     M_ALLOC(m->tokens, (size_t)B * sizeof(int64_t));
     M_ALLOC(m->positions, (size_t)B * sizeof(int));
     M_ALLOC(m->seq_lens, (size_t)B * sizeof(int));
+    M_ALLOC(m->hidden2, (size_t)B * H * sizeof(float));
+    M_ALLOC(m->step_ctr, 256);
+    M_ALLOC(m->push_ctr, 256);
+    if (tp_size > 1) {
+        auto up = [](size_t x) { return (x + 255) & ~size_t(255); };
+        m->off_recv = 0;
+        m->off_am_recv = up((size_t)2 * tp_size * B * H * sizeof(unsigned long long));
+        m->off_am_flags = m->off_am_recv + up((size_t)tp_size * B * sizeof(unsigned long long));
+        m->p2p_bytes = m->off_am_flags + up((size_t)tp_size * sizeof(unsigned));
+        M_ALLOC(m->p2p_base, m->p2p_bytes);
+        cudaError_t e = cudaMemset(m->p2p_base, 0, m->p2p_bytes);
+        if (e != cudaSuccess) { b2_model_destroy(m); return (int)e; }
+    }
+    {
+        cudaError_t e = cudaMemset(m->step_ctr, 0, 256);
+        if (e == cudaSuccess) e = cudaMemset(m->push_ctr, 0, 256);
+        if (e != cudaSuccess) { b2_model_destroy(m); return (int)e; }
+    }
     m->hist_cap = 4096;
     M_ALLOC(m->hist, (size_t)m->hist_cap * B * sizeof(int64_t));
     M_ALLOC(m->hist_count, sizeof(int));
@@ -512,6 +574,74 @@ extern "C" int b2_model_create(const b2_model_config* cfg, int tp_rank, int tp_s
     }
     m->graphs.assign(B + 1, nullptr);
     *out = m;
+    return B2_OK;
+}
+
+// ---------------------------------------------------------------------------
+// tensor-parallel exchange over peer memory
+// ---------------------------------------------------------------------------
+static void invalidate_graphs(b2_model* m) {
+    for (auto& g : m->graphs)
+        if (g) {
+            cudaGraphExecDestroy(g);
+            g = nullptr;
+        }
+}
+
+extern "C" int b2_model_p2p_handle(b2_model* m, void* out64) {
+    B2_REQUIRE(m && out64);
+    if (m->tp < 2 || !m->p2p_base) return B2_ERR_STATE;
+    cudaIpcMemHandle_t h;
+    static_assert(sizeof(cudaIpcMemHandle_t) == 64, "IPC handle size");
+    B2_TRY(cudaIpcGetMemHandle(&h, m->p2p_base));
+    memcpy(out64, &h, sizeof(h));
+    return B2_OK;
+}
+
+extern "C" int b2_model_p2p_open(b2_model* m, const void* handles) {
+    B2_REQUIRE(m && handles);
+    if (m->tp < 2 || !m->p2p_base || m->tp > kMaxTp) return B2_ERR_STATE;
+    if (m->p2p_on) return B2_OK;
+    B2_TRY(cudaStreamSynchronize(m->stream));
+    std::vector<void*> bases(m->tp, nullptr);
+    for (int r = 0; r < m->tp; ++r) {
+        if (r == m->rank) {
+            bases[r] = m->p2p_base;
+            continue;
+        }
+        cudaIpcMemHandle_t h;
+        memcpy(&h, static_cast<const char*>(handles) + 64 * (size_t)r, sizeof(h));
+        const cudaError_t e = cudaIpcOpenMemHandle(&bases[r], h, cudaIpcMemLazyEnablePeerAccess);
+        if (e != cudaSuccess) {
+            for (int q = 0; q < r; ++q)
+                if (bases[q] && q != m->rank) cudaIpcCloseMemHandle(bases[q]);
+            set_last_error("cudaIpcOpenMemHandle failed for a peer's exchange buffer");
+            return (int)e;
+        }
+    }
+    m->peer_bases = bases;
+    TpExchange& x = m->tpx;
+    x = TpExchange{};
+    x.tp = m->tp;
+    x.rank = m->rank;
+    x.Bmax = m->cfg.max_batch;
+    x.H = m->cfg.hidden_size;
+    char* own = static_cast<char*>(m->p2p_base);
+    x.recv = reinterpret_cast<unsigned long long*>(own + m->off_recv);
+    x.am_recv = reinterpret_cast<unsigned long long*>(own + m->off_am_recv);
+    x.am_flags = reinterpret_cast<unsigned*>(own + m->off_am_flags);
+    for (int r = 0; r < m->tp; ++r) {
+        char* pb = static_cast<char*>(bases[r]);
+        x.peer_recv[r] = reinterpret_cast<unsigned long long*>(pb + m->off_recv);
+        x.peer_am_recv[r] = reinterpret_cast<unsigned long long*>(pb + m->off_am_recv);
+        x.peer_am_flags[r] = reinterpret_cast<unsigned*>(pb + m->off_am_flags);
+    }
+    x.step = m->step_ctr;
+    x.ctr = m->push_ctr;
+    x.err = wait_error_word();
+    if (!x.err) return B2_ERR_STATE;
+    m->p2p_on = true;
+    invalidate_graphs(m);  // recapture the step with the exchange in place of NCCL
     return B2_OK;
 }
 
@@ -646,11 +776,32 @@ static int nccl_sum_hidden(b2_model* m, int B) {
     return B2_OK;
 }
 
-static int launch_qkv(b2_model* m, int l, int B, bool pdl) {
+// With the peer exchange on (xch), the step keeps its residual stream in two
+// buffers: exchange 2l (after o of layer l) is consumed by that layer's
+// gate/up GEMV, hidden -> hidden2; exchange 2l+1 (after down) by the next
+// layer's q|k|v GEMV or the lm_head, hidden2 -> hidden.
+// Launch slot of the next kernel of a traced step (tracing off: buf null).
+static TraceSlot next_trace(b2_model* m) {
+    TraceSlot t = {m->trace_cur, 0};
+    if (m->trace_cur) t.slot = m->trace_next++;
+    return t;
+}
+
+static void set_exchange(b2_model* m, GemvParams& p, int slot, const float* hin, float* hout) {
+    p.tp_on = 1;
+    p.tpx = m->tpx;
+    p.slot = slot;
+    p.nslots = 2 * m->cfg.num_layers;
+    p.hid_in = hin;
+    p.hid_out = hout;
+}
+
+static int launch_qkv(b2_model* m, int l, int B, bool pdl, bool xch = false) {
     const b2_model_config& c = m->cfg;
     LayerW& w = m->layers[l];
     __half* kbase = m->kv + (int64_t)l * m->kv_s_layer;
     GemvParams p = {};
+    p.trace = next_trace(m);
     p.W = w.wqkv;
     p.K = c.hidden_size;
     p.tasks = m->qkv_rows / 2;
@@ -671,6 +822,11 @@ static int launch_qkv(b2_model* m, int l, int B, bool pdl) {
     p.vcache = kbase + m->kv_s_kv;
     p.kv_sb = m->kv_s_batch;
     p.kv_sh = m->kv_s_head;
+    if (xch && l > 0) {
+        set_exchange(m, p, 2 * (l - 1) + 1, m->hidden2, m->hidden);
+        p.x = m->hidden2;
+        return gemv_launch(p, X_SUM, OUT_QKV, m->stream, pdl);
+    }
     return gemv_launch(p, X_NORM, OUT_QKV, m->stream, pdl);
 }
 
@@ -679,12 +835,13 @@ static int launch_attn(b2_model* m, int l, int B, bool pdl) {
     const int D = m->cfg.head_dim;
     __half* kbase = m->kv + (int64_t)l * m->kv_s_layer;
     return attn_decode_launch_step(m->q, kbase, kbase + m->kv_s_kv, m->kv_s_batch, m->kv_s_head, D, m->seq_lens,
-                                   m->attn, m->part, m->splits, B, m->nq, m->nkv, D, m->stream);
+                                   m->attn, m->part, m->splits, B, m->nq, m->nkv, D, m->stream, next_trace(m));
 }
 
-static int launch_o(b2_model* m, int l, int B, bool pdl) {
+static int launch_o(b2_model* m, int l, int B, bool pdl, bool xch = false) {
     const b2_model_config& c = m->cfg;
     GemvParams p = {};
+    p.trace = next_trace(m);
     p.W = m->layers[l].wo;
     p.K = m->nq * c.head_dim;
     p.tasks = c.hidden_size;
@@ -694,13 +851,18 @@ static int launch_o(b2_model* m, int l, int B, bool pdl) {
     p.resid_add = m->rank == 0 ? 1 : 0;
     p.y = m->hidden;
     p.ldy = c.hidden_size;
+    if (xch) {
+        set_exchange(m, p, 2 * l, nullptr, nullptr);
+        return gemv_launch(p, X_HALF, OUT_PUSH, m->stream, pdl);
+    }
     return gemv_launch(p, X_HALF, OUT_RESID, m->stream, pdl);
 }
 
-static int launch_gateup(b2_model* m, int l, int B, bool pdl) {
+static int launch_gateup(b2_model* m, int l, int B, bool pdl, bool xch = false) {
     const b2_model_config& c = m->cfg;
     LayerW& w = m->layers[l];
     GemvParams p = {};
+    p.trace = next_trace(m);
     p.W = w.wg;
     p.W2 = w.wu;
     p.K = c.hidden_size;
@@ -712,12 +874,17 @@ static int launch_gateup(b2_model* m, int l, int B, bool pdl) {
     p.eps = c.rms_norm_eps;
     p.y = m->act;
     p.ldy = m->inter;
+    if (xch) {
+        set_exchange(m, p, 2 * l, m->hidden, m->hidden2);
+        return gemv_launch(p, X_SUM, OUT_SWIGLU, m->stream, pdl);
+    }
     return gemv_launch(p, X_NORM, OUT_SWIGLU, m->stream, pdl);
 }
 
-static int launch_down(b2_model* m, int l, int B, bool pdl) {
+static int launch_down(b2_model* m, int l, int B, bool pdl, bool xch = false) {
     const b2_model_config& c = m->cfg;
     GemvParams p = {};
+    p.trace = next_trace(m);
     p.W = m->layers[l].wd;
     p.K = m->inter;
     p.tasks = c.hidden_size;
@@ -727,12 +894,17 @@ static int launch_down(b2_model* m, int l, int B, bool pdl) {
     p.resid_add = m->rank == 0 ? 1 : 0;
     p.y = m->hidden;
     p.ldy = c.hidden_size;
+    if (xch) {
+        set_exchange(m, p, 2 * l + 1, nullptr, nullptr);
+        return gemv_launch(p, X_HALF, OUT_PUSH, m->stream, pdl);
+    }
     return gemv_launch(p, X_HALF, OUT_RESID, m->stream, pdl);
 }
 
-static int launch_lm_head(b2_model* m, int B, bool pdl) {
+static int launch_lm_head(b2_model* m, int B, bool pdl, bool xch = false) {
     const b2_model_config& c = m->cfg;
     GemvParams p = {};
+    p.trace = next_trace(m);
     p.W = m->lm_head;
     p.K = c.hidden_size;
     p.tasks = m->vocab_l;
@@ -746,6 +918,11 @@ static int launch_lm_head(b2_model* m, int B, bool pdl) {
     p.argmax = m->argmax;
     p.row_offset = m->vocab_off;
     p.argmax_limit = c.vocab_size > 151665 ? 151665 : c.vocab_size;
+    if (xch) {
+        set_exchange(m, p, 2 * c.num_layers - 1, m->hidden2, m->hidden);
+        p.x = m->hidden2;
+        return gemv_launch(p, X_SUM, OUT_LOGITS, m->stream, pdl);
+    }
     return gemv_launch(p, X_NORM, OUT_LOGITS, m->stream, pdl);
 }
 
@@ -754,25 +931,31 @@ static int enqueue_step(b2_model* m, int B) {
     const b2_model_config& c = m->cfg;
     cudaStream_t s = m->stream;
     const bool pdl = true;
+    const bool xch = m->p2p_on;
     B2_TRY(launch(step_begin_kernel, dim3(B), dim3(256), 0, s, pdl, (const int64_t*)m->tokens,
                   (const int*)m->positions, (const __half*)m->embed, m->hidden, c.hidden_size, m->seq_lens, m->argmax,
-                  m->hist, (const int*)m->hist_count, m->hist_cap));
+                  m->hist, (const int*)m->hist_count, m->hist_cap, next_trace(m)));
     for (int l = 0; l < c.num_layers; ++l) {
-        M_TRY(launch_qkv(m, l, B, pdl));
+        M_TRY(launch_qkv(m, l, B, pdl, xch));
         M_TRY(launch_attn(m, l, B, pdl));
-        M_TRY(launch_o(m, l, B, pdl));
-        M_TRY(nccl_sum_hidden(m, B));
-        M_TRY(launch_gateup(m, l, B, pdl));
-        M_TRY(launch_down(m, l, B, pdl));
-        M_TRY(nccl_sum_hidden(m, B));
+        M_TRY(launch_o(m, l, B, pdl, xch));
+        if (!xch) M_TRY(nccl_sum_hidden(m, B));
+        M_TRY(launch_gateup(m, l, B, pdl, xch));
+        M_TRY(launch_down(m, l, B, pdl, xch));
+        if (!xch) M_TRY(nccl_sum_hidden(m, B));
     }
-    M_TRY(launch_lm_head(m, B, pdl));
-    if (m->tp > 1) {
+    M_TRY(launch_lm_head(m, B, pdl, xch));
+    if (m->tp > 1 && !xch) {
         if (nccl().AllReduce(m->argmax, m->argmax, (size_t)B, ncclUint64, ncclMax, m->comm, s) != ncclSuccess)
             return B2_ERR_NCCL;
     }
+    const unsigned long long* am_recv =
+        xch ? reinterpret_cast<const unsigned long long*>(static_cast<char*>(m->p2p_base) + m->off_am_recv) : nullptr;
+    const unsigned* am_flags =
+        xch ? reinterpret_cast<const unsigned*>(static_cast<char*>(m->p2p_base) + m->off_am_flags) : nullptr;
     B2_TRY(launch(step_end_kernel, dim3(1), dim3(32), 0, s, pdl, (const unsigned long long*)m->argmax, m->tokens,
-                  m->positions, B, m->hist_count, m->hist_cap));
+                  m->positions, B, m->hist_count, m->hist_cap, xch ? 1 : 0, am_recv, am_flags, m->tp,
+                  c.max_batch, m->step_ctr, m->tpx.err, next_trace(m)));
     return B2_OK;
 }
 
@@ -1081,6 +1264,32 @@ extern "C" double b2_model_kernel_bytes(const b2_model* m, int kind, int B, int 
         case 4: return 2.0 * H * m->inter + 2.0 * B * m->inter + 8.0 * B * H;
         default: return 2.0 * m->vocab_l * H + 4.0 * B * H + 2.0 * H + 4.0 * B * m->vocab_l;
     }
+}
+
+extern "C" int b2_model_trace_step(b2_model* m, int B, unsigned long long* host_ns, int max_slots, int* n_slots) {
+    B2_REQUIRE(m && host_ns && n_slots && B >= 1 && B <= m->cfg.max_batch && max_slots > 0);
+    const int need = b2_model_step_launches(m, B);
+    if (!m->trace_buf) B2_TRY(cudaMalloc(&m->trace_buf, (size_t)2 * need * sizeof(unsigned long long)));
+    std::vector<unsigned long long> init(2 * (size_t)need);
+    for (int i = 0; i < need; ++i) {
+        init[2 * i] = ~0ull;
+        init[2 * i + 1] = 0ull;
+    }
+    B2_TRY(cudaMemcpyAsync(m->trace_buf, init.data(), init.size() * sizeof(unsigned long long), cudaMemcpyHostToDevice,
+                           m->stream));
+    m->trace_cur = m->trace_buf;
+    m->trace_next = 0;
+    const int rc = enqueue_step(m, B);
+    m->trace_cur = nullptr;
+    if (rc != B2_OK) return rc;
+    m->last_B = B;
+    B2_TRY(cudaMemcpyAsync(init.data(), m->trace_buf, init.size() * sizeof(unsigned long long), cudaMemcpyDeviceToHost,
+                           m->stream));
+    B2_TRY(cudaStreamSynchronize(m->stream));
+    const int n = m->trace_next < max_slots ? m->trace_next : max_slots;
+    for (int i = 0; i < 2 * n; ++i) host_ns[i] = init[i];
+    *n_slots = m->trace_next;
+    return B2_OK;
 }
 
 extern "C" int b2_model_step_launches(const b2_model* m, int B) {

@@ -37,12 +37,17 @@ def main():
         ("llama8b-width", O.Config(vocab=128256, hidden=4096, inter=14336, layers=2, nq=32, nkv=8, head_dim=128,
                                    theta=5e5), 16, 6),
     ]
-    for name, cfg, S0, n_dec in cases:
+    cases = [(n, c, s0, nd, x) for (n, c, s0, nd) in cases for x in ("nccl", "p2p")]
+    for name, cfg, S0, n_dec, xch in cases:
         obj = [b2.nccl_unique_id() if rank == 0 else None]  # one id per communicator
         dist.broadcast_object_list(obj, src=0)
         m = b2.Model(cfg.vocab, cfg.hidden, cfg.inter, cfg.layers, cfg.nq, cfg.nkv, cfg.head_dim, eps=cfg.eps,
                      theta=cfg.theta, max_batch=1, max_seq=128, tp_rank=rank, tp_size=world, nccl_id=obj[0])
         m.init_random(77, 0.02)
+        if xch == "p2p":  # partial sums over NVLink peer memory instead of NCCL
+            handles = [None] * world
+            dist.all_gather_object(handles, m.p2p_handle())
+            m.p2p_open(handles)
         rng = np.random.default_rng(5)
         prompt = rng.integers(0, cfg.vocab, S0)
         lg0 = m.prefill(prompt[None, :])
@@ -53,7 +58,9 @@ def main():
         for i in range(3):
             lg, _ = m.decode_step([gen[i]], [S0 + i])
             dec.append(lg[0])
+        status = b2.device_status()
         m.close()
+        verdict["ok"] &= status == 0
         if rank == 0:
             W = O.seeded_weights(cfg, 77)
             ref = O.forward(cfg, W, np.concatenate([prompt, gen[:-1]]).astype(np.int64), logit_row0=S0 - 1)
@@ -72,7 +79,8 @@ def main():
                     greedy_ok &= bool(s[0] - s[1] < 0.05)
             ok = worst_d <= 2e-2 and worst_cos >= 0.9999 and greedy_ok
             verdict["ok"] &= ok
-            verdict["cases"].append({"name": name, "max_abs": worst_d, "cos": worst_cos, "greedy_ok": greedy_ok})
+            verdict["cases"].append({"name": name, "exchange": xch, "max_abs": worst_d, "cos": worst_cos,
+                                     "greedy_ok": greedy_ok, "device_status": status})
     dist.barrier()
     if rank == 0:
         with open(out_path, "w") as f:
