@@ -37,7 +37,8 @@ def main():
         ("llama8b-width", O.Config(vocab=128256, hidden=4096, inter=14336, layers=2, nq=32, nkv=8, head_dim=128,
                                    theta=5e5), 16, 6),
     ]
-    cases = [(n, c, s0, nd, x) for (n, c, s0, nd) in cases for x in ("nccl", "p2p")]
+    cases = [(n, c, s0, nd, x) for (n, c, s0, nd) in cases for x in ("nccl", "p2p")
+             if c.nkv % world == 0 and c.inter % world == 0 and c.vocab % world == 0]
     for name, cfg, S0, n_dec, xch in cases:
         obj = [b2.nccl_unique_id() if rank == 0 else None]  # one id per communicator
         dist.broadcast_object_list(obj, src=0)
