@@ -317,6 +317,26 @@ def run_b2(args, rank, world, local):
     ms_e2e = max_over_ranks(e2.elapsed_time(e3))
     ck = clocks.stop()
 
+    trace = None
+    if args.trace:
+        # per-launch device timestamps of a few live steps (b2_model_trace_step)
+        names = ["step_begin"] + ["qkv", "attention", "o_proj", "gate_up", "down"] * c["layers"] + ["lm_head",
+                                                                                                   "step_end"]
+        runs = np.stack([m.trace_step(B) for _ in range(5)])
+        t = np.median(runs, axis=0)
+        agg, prev = {}, 0
+        for i, (a, e) in enumerate(t):
+            g = agg.setdefault(names[i] if i < len(names) else f"k{i}", [0, 0.0, 0.0])
+            g[0] += 1
+            g[1] += (e - a) / 1e3
+            g[2] += (a - prev) / 1e3
+            prev = e
+        trace = {"step_span_us": float(t[-1, 1] - t[0, 0]) / 1e3,
+                 "per_kernel": {k: {"launches": n, "mean_us": d / n, "mean_gap_before_us": gp / n}
+                                for k, (n, d, gp) in agg.items()},
+                 "how": "b2_model_trace_step: %globaltimer at the first CTA past its programmatic-launch wait and "
+                        "at the last CTA's end, median of 5 steps, rank 0"}
+
     if rank == 0:
         peak, peak_src = measured_peak()
         dom = max(ktimes, key=lambda k: ktimes[k] * (c["layers"] if k != "lm_head" else 1))
@@ -347,6 +367,8 @@ def run_b2(args, rank, world, local):
                                "synchronised), second call"},
             "clocks": ck,
         }
+        if trace:
+            out["trace"] = trace
         if world == 1 and not args.no_cpu_baseline:
             try:
                 out["cpu_baseline"] = cpu_baseline_single()
@@ -364,6 +386,7 @@ def main():
     ap.add_argument("--batch", type=int, default=1)
     ap.add_argument("--impl", default="b2", choices=["b2", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--trace", action="store_true", help="add a per-kernel device trace of a few steps")
     ap.add_argument("--exchange", default="p2p", choices=["p2p", "nccl"],
                     help="tensor-parallel decode reduction: fused peer-memory exchange or NCCL all-reduce")
     ap.add_argument("--prompt", type=int, default=PROMPT, help="prompt length (512 for the metric)")
