@@ -378,6 +378,131 @@ def run_b2(args, rank, world, local):
     m.close()
 
 
+# ---------------------------------------------------------------------------
+# kernel microbenchmarks (BASELINE configs 2 and 3, prefill projections)
+# ---------------------------------------------------------------------------
+
+def _events_time(fn, iters, flush=None):
+    """Median per-call milliseconds over `iters` calls timed with CUDA events on
+    the current stream; `flush` (if given) runs before each call, outside the
+    timed interval."""
+    import torch
+    times = []
+    for _ in range(iters):
+        if flush is not None:
+            flush()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        fn()
+        e1.record()
+        e1.synchronize()
+        times.append(e0.elapsed_time(e1))
+    return statistics.median(times)
+
+
+def run_op(args):
+    import numpy as np  # noqa: F401
+    import torch
+
+    import b2engine as b2
+    torch.cuda.set_device(0)
+    peak_hbm, hbm_src = measured_peak()
+    peaks = {}
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            peaks = json.load(f)
+    except Exception:
+        pass
+    peak_tf = float(peaks.get("bf16_tflops", 1590.0))
+    flush_buf = torch.empty(512 << 20, dtype=torch.uint8, device="cuda")  # 512 MB > 4x L2
+
+    def flush():
+        flush_buf.zero_()
+
+    st = b2.stream_ptr()
+    warm, iters = max(args.warmup, 3), max(args.steps, 1)
+    out = {"metric": None, "n_gpus": 1, "steps": iters, "warmup": warm, "data": "synthetic ~N(0,1)"}
+    if args.op == "attention":
+        # split-KV decode attention: fp16 q [B,32,128], K/V [B,ctx,8,128] token-major, GQA 4:1
+        nq, nkv, D = 32, 8, 128
+        cases = []
+        for B in (1, 8, 32):
+            for ctx in (512, 4096, 32768):
+                g = torch.Generator(device="cuda").manual_seed(B * 100003 + ctx)
+                q = torch.randn(B, nq, D, generator=g, device="cuda").half()
+                k = torch.randn(B, ctx, nkv, D, generator=g, device="cuda").half()
+                v = torch.randn(B, ctx, nkv, D, generator=g, device="cuda").half()
+                lens = torch.full((B,), ctx, dtype=torch.int32, device="cuda")
+                o = torch.empty_like(q)
+                split = torch.empty(B * nq * 132 * (D + 2) + 4096, dtype=torch.float32, device="cuda")
+                kv = b2.KVView(k.data_ptr(), ctx * nkv * D, D, nkv * D, 1)
+                vv = b2.KVView(v.data_ptr(), ctx * nkv * D, D, nkv * D, 1)
+
+                def fn():
+                    b2.call("b2_decode_gqa_split", q.data_ptr(), kv, vv, lens.data_ptr(), o.data_ptr(), B, nq, nkv, D,
+                            ctx, split.data_ptr(), split.numel(), st)
+                for _ in range(warm):
+                    fn()
+                ms = _events_time(fn, iters, flush)
+                nbytes = 4.0 * B * ctx * nkv * D + 4.0 * B * nq * D
+                gbs = nbytes / (ms * 1e-3) / 1e9
+                cases.append({"B": B, "ctx": ctx, "us": ms * 1e3, "bytes": nbytes, "GBs": gbs, "frac": gbs / peak_hbm})
+                del q, k, v, o, split
+        out.update({"metric": "split-KV decode attention achieved HBM GB/s (fp16, Hq 32 / Hkv 8, D 128)",
+                    "value": max(c["GBs"] for c in cases), "unit": "GB/s", "higher_is_better": True,
+                    "dtype": "f16", "config": {"workload": "BASELINE split-KV decode attention microbench",
+                                               "l2": "512 MB buffer written between timed calls"},
+                    "cases": cases, "peak": peak_hbm, "peak_source": hbm_src})
+    elif args.op == "flash_prefill":
+        nq, nkv, D = 32, 8, 128
+        cases = []
+        for S in ([args.seq] if args.seq else [2048, 8192]):
+            g = torch.Generator(device="cuda").manual_seed(S)
+            q = torch.randn(S, nq, D, generator=g, device="cuda").bfloat16()
+            k = torch.randn(S, nkv, D, generator=g, device="cuda").bfloat16()
+            v = torch.randn(S, nkv, D, generator=g, device="cuda").bfloat16()
+            o = torch.empty_like(q)
+            for rope in (500000.0, 0.0):
+                def fn():
+                    b2.call("b2_flash_prefill_gqa_ex", q.data_ptr(), k.data_ptr(), v.data_ptr(), o.data_ptr(), S, nq,
+                            nkv, D, 1, 1, rope, 0, st)
+                for _ in range(warm):
+                    fn()
+                ms = _events_time(fn, iters)
+                flop = 2.0 * S * S * D * nq
+                tf = flop / (ms * 1e-3) / 1e12
+                cases.append({"S": S, "rope_theta": rope, "us": ms * 1e3, "flop": flop, "TFLOPs": tf,
+                              "frac": tf / peak_tf})
+            assert b2.device_status() == 0
+        out.update({"metric": "causal flash prefill TFLOP/s (bf16, tcgen05, Hq 32 / Hkv 8, D 128)",
+                    "value": max(c["TFLOPs"] for c in cases), "unit": "TFLOP/s", "higher_is_better": True,
+                    "dtype": "bf16", "config": {"workload": "BASELINE causal flash prefill, batch 1",
+                                                "flop": "2*S^2*D*Hq (causal half of 4*S^2*D*Hq)"},
+                    "cases": cases, "peak": peak_tf, "peak_source": "measured (MEASURED_PEAKS.json bf16_tflops)"})
+    elif args.op == "gemm":
+        cases = []
+        for (M, K, N) in [(512, 4096, 6144), (2048, 4096, 6144), (2048, 4096, 28672), (2048, 14336, 4096),
+                          (8192, 4096, 6144)]:
+            A = torch.randn(M, K, device="cuda").half()
+            Bw = torch.randn(N, K, device="cuda").half()
+            C = torch.empty(M, N, device="cuda").half()
+
+            def fn():
+                b2.call("b2_matmul_transB", A.data_ptr(), Bw.data_ptr(), C.data_ptr(), M, K, N, st)
+            for _ in range(warm):
+                fn()
+            ms = _events_time(fn, iters)
+            tf = 2.0 * M * N * K / (ms * 1e-3) / 1e12
+            cases.append({"M": M, "K": K, "N": N, "us": ms * 1e3, "TFLOPs": tf, "frac": tf / peak_tf})
+            del A, Bw, C
+        assert b2.device_status() == 0
+        out.update({"metric": "prefill projection GEMM TFLOP/s (fp16 in, fp32 accumulate, tcgen05)",
+                    "value": max(c["TFLOPs"] for c in cases), "unit": "TFLOP/s", "higher_is_better": True,
+                    "dtype": "f16", "config": {"workload": "Llama-3-8B prefill projection shapes"},
+                    "cases": cases, "peak": peak_tf, "peak_source": "measured (MEASURED_PEAKS.json bf16_tflops)"})
+    print(json.dumps(out), flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -387,6 +512,9 @@ def main():
     ap.add_argument("--impl", default="b2", choices=["b2", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--trace", action="store_true", help="add a per-kernel device trace of a few steps")
+    ap.add_argument("--op", default=None, choices=["attention", "flash_prefill", "gemm"],
+                    help="kernel microbenchmark instead of the decode metric (1 GPU)")
+    ap.add_argument("--seq", type=int, default=0, help="--op flash_prefill: one sequence length")
     ap.add_argument("--exchange", default="p2p", choices=["p2p", "nccl"],
                     help="tensor-parallel decode reduction: fused peer-memory exchange or NCCL all-reduce")
     ap.add_argument("--prompt", type=int, default=PROMPT, help="prompt length (512 for the metric)")
@@ -399,6 +527,10 @@ def main():
     local = int(os.environ.get("LOCAL_RANK", "0"))
     if args.impl == "reference":
         run_reference(args, rank, world)
+        return
+    if args.op:
+        if rank == 0:
+            run_op(args)
         return
     if world > 1:
         # one node: NCCL's bootstrap goes over loopback (its default pick, the

@@ -119,7 +119,7 @@ struct GemvParams {
     int slot, nslots;            // this exchange's index in the step
     const float* hid_in;         // X_SUM: residual stream before the exchange
     float* hid_out;              // X_SUM: residual stream after it
-    int rows_per_cta;            // OUT_PUSH: each CTA owns a contiguous block of rows (set at launch)
+    int rows_per_cta;            // OUT_PUSH: contiguous block of rows per CTA (set at launch)
     TraceSlot trace;             // step trace (buf null: off)
 };
 
