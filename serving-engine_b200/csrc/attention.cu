@@ -67,6 +67,19 @@ constexpr int kAttnWarps = 4;
 constexpr int kAttnThreads = kAttnWarps * 32;
 constexpr int kMaxSplits = 128;
 
+// 16-byte asynchronous global->shared copy (zero-filled when !valid);
+// completion tracked per thread with commit / wait groups.
+__device__ __forceinline__ void cp_async16(void* smem, const void* gmem, bool valid) {
+    const unsigned sa = static_cast<unsigned>(__cvta_generic_to_shared(smem));
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(sa), "l"(gmem), "r"(valid ? 16 : 0)
+                 : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
+
+constexpr int kAttnStages = 3;  // K/V tiles each lane keeps in flight (cp.async ring)
+
 template <int C8>
 struct LaneMap {
     static constexpr int LP = C8 <= 2 ? 2 : (C8 <= 4 ? 4 : (C8 <= 8 ? 8 : (C8 <= 16 ? 16 : 32)));
@@ -114,32 +127,39 @@ __global__ void __launch_bounds__(kAttnThreads) attn_decode_kernel(const AttnPar
     const __half* kb = p.k + (int64_t)b * p.sb + (int64_t)kvh * p.sh + c * 8;
     const __half* vb = p.v + (int64_t)b * p.sb + (int64_t)kvh * p.sh + c * 8;
 
-    // first tile of this warp; in the decode-step form the rows older than
-    // the newest are requested before waiting on the previous kernel
-    uint4 kr[UNR], vr[UNR];
-    int base = start + warp * WT;
+    // K/V tiles stream through a per-lane cp.async ring (each lane copies and
+    // later reads only its own 16-byte slots), kAttnStages - 1 tiles ahead of
+    // the one being computed.  In the decode-step form the first tiles are
+    // requested before waiting on the previous kernel, without the newest row
+    // (written by that kernel), which is read directly once the wait is over.
+    extern __shared__ __align__(16) uint4 kv_ring[];  // [warp][stage][UNR][K,V][lane]
+    uint4* ring = kv_ring + (size_t)warp * kAttnStages * UNR * 2 * 32;
+    const int tile0 = start + warp * WT;
+    const int nt = tile0 < end ? (end - tile0 + kAttnWarps * WT - 1) / (kAttnWarps * WT) : 0;
+    auto issue = [&](int i, int lim) {
+        if (i < nt) {
+            const int tb = tile0 + i * kAttnWarps * WT;
+            uint4* st = ring + (size_t)(i % kAttnStages) * UNR * 2 * 32;
+#pragma unroll
+            for (int u = 0; u < UNR; ++u) {
+                const int pos = tb + u * PPW + pidx;
+                const bool ok = cact && pos < lim;
+                const int64_t off = ok ? (int64_t)pos * p.ss : 0;
+                cp_async16(st + (u * 2 + 0) * 32 + lane, kb + off, ok);
+                cp_async16(st + (u * 2 + 1) * 32 + lane, vb + off, ok);
+            }
+        }
+        cp_async_commit();
+    };
     {
         const int lim = p.early_kv ? min(end, L - 1) : end;
 #pragma unroll
-        for (int u = 0; u < UNR; ++u) {
-            const int pos = base + u * PPW + pidx;
-            const bool ok = cact && pos < lim;
-            kr[u] = ok ? ldg16(kb + (int64_t)pos * p.ss) : make_uint4(0, 0, 0, 0);
-            vr[u] = ok ? ldg16(vb + (int64_t)pos * p.ss) : make_uint4(0, 0, 0, 0);
-        }
+        for (int i = 0; i < kAttnStages - 1; ++i) issue(i, lim);
     }
     if (p.early_kv) {
         griddep_wait();
         griddep_launch_dependents();
         trace_begin(p.trace);
-#pragma unroll
-        for (int u = 0; u < UNR; ++u) {
-            const int pos = base + u * PPW + pidx;
-            if (cact && pos == L - 1 && pos < end) {
-                kr[u] = ldg16(kb + (int64_t)pos * p.ss);
-                vr[u] = ldg16(vb + (int64_t)pos * p.ss);
-            }
-        }
     }
 
     float qf[G][8];
@@ -165,14 +185,27 @@ __global__ void __launch_bounds__(kAttnThreads) attn_decode_kernel(const AttnPar
         for (int j = 0; j < 8; ++j) acc[g][j] = 0.f;
     }
 
-    for (bool first = true; base < end; base += kAttnWarps * WT, first = false) {
-        if (!first) {
+    for (int i = 0; i < nt; ++i) {
+        const int base = tile0 + i * kAttnWarps * WT;
+        issue(i + kAttnStages - 1, end);
+        cp_async_wait<kAttnStages - 1>();
+        uint4 kr[UNR], vr[UNR];
+        {
+            const uint4* st = ring + (size_t)(i % kAttnStages) * UNR * 2 * 32;
+#pragma unroll
+            for (int u = 0; u < UNR; ++u) {
+                kr[u] = st[(u * 2 + 0) * 32 + lane];
+                vr[u] = st[(u * 2 + 1) * 32 + lane];
+            }
+        }
+        if (p.early_kv && i < kAttnStages - 1) {
 #pragma unroll
             for (int u = 0; u < UNR; ++u) {
                 const int pos = base + u * PPW + pidx;
-                const bool ok = cact && pos < end;
-                kr[u] = ok ? ldg16(kb + (int64_t)pos * p.ss) : make_uint4(0, 0, 0, 0);
-                vr[u] = ok ? ldg16(vb + (int64_t)pos * p.ss) : make_uint4(0, 0, 0, 0);
+                if (cact && pos == L - 1 && pos < end) {
+                    kr[u] = ldg16(kb + (int64_t)pos * p.ss);
+                    vr[u] = ldg16(vb + (int64_t)pos * p.ss);
+                }
             }
         }
         float s[UNR][G];
@@ -214,6 +247,8 @@ __global__ void __launch_bounds__(kAttnThreads) attn_decode_kernel(const AttnPar
             m_run[g] = m_new;
         }
     }
+
+    cp_async_wait<0>();
 
     // merge the PPW position groups of the warp (same running max: it is warp-uniform)
 #pragma unroll
@@ -322,13 +357,33 @@ __global__ void __launch_bounds__(kAttnThreads) attn_decode_kernel(const AttnPar
     trace_end(p.trace);
 }
 
+template <int G>
+constexpr size_t attn_ring_bytes() {
+    return (size_t)kAttnWarps * kAttnStages * (G <= 4 ? 4 : 2) * 2 * 32 * sizeof(uint4);
+}
+
+template <int D, int G>
+static cudaError_t launch_decode_dg(const AttnParams& p, dim3 grid, cudaStream_t s, bool pdl) {
+    auto kern = attn_decode_kernel<D, G>;
+    constexpr size_t smem = attn_ring_bytes<G>();
+    static thread_local int set_dev = -1;
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (dev != set_dev) {
+        const cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        if (e != cudaSuccess) return e;
+        set_dev = dev;
+    }
+    return launch(kern, grid, dim3(kAttnThreads), smem, s, pdl, p);
+}
+
 template <int D>
 static cudaError_t launch_decode_d(const AttnParams& p, dim3 grid, int G, cudaStream_t s, bool pdl) {
     switch (G) {
-        case 1: return launch(attn_decode_kernel<D, 1>, grid, dim3(kAttnThreads), 0, s, pdl, p);
-        case 2: return launch(attn_decode_kernel<D, 2>, grid, dim3(kAttnThreads), 0, s, pdl, p);
-        case 4: return launch(attn_decode_kernel<D, 4>, grid, dim3(kAttnThreads), 0, s, pdl, p);
-        default: return launch(attn_decode_kernel<D, 8>, grid, dim3(kAttnThreads), 0, s, pdl, p);
+        case 1: return launch_decode_dg<D, 1>(p, grid, s, pdl);
+        case 2: return launch_decode_dg<D, 2>(p, grid, s, pdl);
+        case 4: return launch_decode_dg<D, 4>(p, grid, s, pdl);
+        default: return launch_decode_dg<D, 8>(p, grid, s, pdl);
     }
 }
 
