@@ -8,8 +8,9 @@
  * Each entry point names the reference interface it replaces
  * (XVX-016/serving-engine, paths relative to that project).  The reference's
  * C++ signatures (namespace engine::cuda, void returns, exceptions on error)
- * are kept as inline wrappers over this layer in
- * serving-engine_b200/compat/src/... so that its callers build unchanged.
+ * are kept as inline wrappers over this layer in serving-engine_b200/compat
+ * (src/cuda/kernels.h, src/cuda/kv_view.h, src/runtime/sampler.h,
+ * src/runtime/kv_cache.h) so that its callers build unchanged.
  *
  * Element types: "half" is IEEE fp16, "bf16" is bfloat16, "float" is fp32.
  */
