@@ -592,6 +592,32 @@ int attn_decode_launch_model(const __half* q, const __half* kbase, const __half*
     return attn_decode_launch(p, B, D, s, pdl);
 }
 
+// Decode-step launch with q rows `q_sb` elements apart (the batched step
+// reads q in place from the fused q|k|v rows).
+int attn_decode_launch_step_q(const __half* q, int64_t q_sb, const __half* kbase, const __half* vbase, int64_t sb,
+                              int64_t sh, int64_t ss, const int* seq_lens, __half* out, float* part, int splits,
+                              int B, int nq, int nkv, int D, cudaStream_t s) {
+    AttnParams p = {};
+    p.q = q;
+    p.q_sb = q_sb;
+    p.k = kbase;
+    p.v = vbase;
+    p.sb = sb;
+    p.sh = sh;
+    p.ss = ss;
+    p.seq_lens = seq_lens;
+    p.causal_base = -1;
+    p.out = out;
+    p.o_sb = (int64_t)nq * D;
+    p.nq = nq;
+    p.nkv = nkv;
+    p.scale_log2 = 1.4426950408889634f / sqrtf((float)D);
+    p.part = part;
+    p.splits = splits;
+    p.early_kv = 1;
+    return attn_decode_launch(p, B, D, s, true);
+}
+
 // Decode-step launch: as attn_decode_launch_model, and in addition the K/V
 // rows older than seq_lens[b] - 1 and seq_lens itself are read before the
 // programmatic-launch wait (valid only when the preceding kernel writes no

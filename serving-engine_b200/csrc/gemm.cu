@@ -39,7 +39,7 @@ enum TcEpi : int { TC_HALF = 0, TC_F32 = 1, TC_F32_ADD = 2 };
 template <int BN, int EPI>
 __global__ void __launch_bounds__(192, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
-                   void* __restrict__ C, int M, int N, int K, int* err) {
+                   void* __restrict__ C, int M, int N, int K, int kb_per_split, int* err) {
     using Cfg = TcGemmCfg<BN>;
     constexpr int STAGES = Cfg::STAGES;
     extern __shared__ uint8_t smem_raw[];
@@ -68,7 +68,12 @@ __global__ void __launch_bounds__(192, 1)
     griddep_launch_dependents();
 
     const int m0 = blockIdx.y * kTcBM, n0 = blockIdx.x * BN;
-    const int nk = (K + kTcBK - 1) / kTcBK;
+    // split-K: this CTA's k blocks [kb0, kb1); split z writes slab z of C
+    const int nk_all = (K + kTcBK - 1) / kTcBK;
+    const int kb0 = blockIdx.z * kb_per_split;
+    const int kb1 = min(nk_all, kb0 + kb_per_split);
+    const int nk = kb1 - kb0;
+    if (gridDim.z > 1) C = static_cast<float*>(C) + (size_t)blockIdx.z * M * N;
 
     if (warp == 4) {
         if (lane == 0) {
@@ -78,8 +83,8 @@ __global__ void __launch_bounds__(192, 1)
                 if (kb >= STAGES && !tc::mbar_wait(&empty[s], ph ^ 1u, err, 1)) break;
                 uint8_t* st = smem + s * Cfg::STAGE_BYTES;
                 tc::mbar_arrive_expect_tx(&full[s], Cfg::STAGE_BYTES);
-                tc::tma_load_2d(st, &tmA, &full[s], kb * kTcBK, m0);
-                tc::tma_load_2d(st + Cfg::A_BYTES, &tmB, &full[s], kb * kTcBK, n0);
+                tc::tma_load_2d(st, &tmA, &full[s], (kb0 + kb) * kTcBK, m0);
+                tc::tma_load_2d(st + Cfg::A_BYTES, &tmB, &full[s], (kb0 + kb) * kTcBK, n0);
             }
         }
     } else if (warp == 5) {
@@ -167,30 +172,52 @@ __global__ void __launch_bounds__(192, 1)
 }
 
 template <int BN, int EPI>
-static int launch_tc(const CUtensorMap& ta, const CUtensorMap& tb, void* C, int M, int N, int K, int* err,
-                     cudaStream_t s) {
+static int launch_tc(const CUtensorMap& ta, const CUtensorMap& tb, void* C, int M, int N, int K, int ksplit,
+                     int* err, cudaStream_t s) {
     auto kern = gemm_tc_kernel<BN, EPI>;
     const size_t smem = TcGemmCfg<BN>::SMEM;
     B2_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-    dim3 grid((unsigned)((N + BN - 1) / BN), (unsigned)((M + kTcBM - 1) / kTcBM));
-    B2_TRY(launch(kern, grid, dim3(192), smem, s, true, ta, tb, C, M, N, K, err));
+    const int nk = (K + kTcBK - 1) / kTcBK;
+    const int kbps = (nk + ksplit - 1) / ksplit;
+    ksplit = (nk + kbps - 1) / kbps;  // no empty split
+    dim3 grid((unsigned)((N + BN - 1) / BN), (unsigned)((M + kTcBM - 1) / kTcBM), (unsigned)ksplit);
+    B2_TRY(launch(kern, grid, dim3(192), smem, s, true, ta, tb, C, M, N, K, kbps, err));
     return B2_OK;
 }
 
 template <int BN>
 static int launch_tc_epi(const CUtensorMap& ta, const CUtensorMap& tb, void* C, int M, int N, int K, int epi,
-                         int* err, cudaStream_t s) {
+                         int ksplit, int* err, cudaStream_t s) {
     switch (epi) {
-        case TC_HALF: return launch_tc<BN, TC_HALF>(ta, tb, C, M, N, K, err, s);
-        case TC_F32: return launch_tc<BN, TC_F32>(ta, tb, C, M, N, K, err, s);
-        default: return launch_tc<BN, TC_F32_ADD>(ta, tb, C, M, N, K, err, s);
+        case TC_HALF: return launch_tc<BN, TC_HALF>(ta, tb, C, M, N, K, 1, err, s);
+        case TC_F32: return launch_tc<BN, TC_F32>(ta, tb, C, M, N, K, ksplit, err, s);
+        default: return launch_tc<BN, TC_F32_ADD>(ta, tb, C, M, N, K, 1, err, s);
     }
 }
 
 // C[M,N] (=, or += for TC_F32_ADD) A[M,K] * B[N,K]^T on the tensor cores.
 // Requires 16-byte aligned A, B, C and K % 8 == 0 (TMA row strides are
-// multiples of 16 bytes); B2_ERR_UNSUPPORTED otherwise.
+// multiples of 16 bytes); B2_ERR_UNSUPPORTED otherwise.  ksplit > 1 (TC_F32
+// only): the K range is cut into that many parts (at most; whole 64-deep
+// blocks each) and part z writes fp32 slab z of C ([ksplit][M][N]) for the
+// caller to reduce; the number of slabs written is returned through
+// *slabs when it is not null.
+int gemm_tc_split(const __half* A, const __half* B, void* C, int M, int N, int K, int epi, int ksplit, int* slabs,
+                  cudaStream_t s);
+
 int gemm_tc(const __half* A, const __half* B, void* C, int M, int N, int K, int epi, cudaStream_t s) {
+    return gemm_tc_split(A, B, C, M, N, K, epi, 1, nullptr, s);
+}
+
+int gemm_tc_split(const __half* A, const __half* B, void* C, int M, int N, int K, int epi, int ksplit, int* slabs,
+                  cudaStream_t s) {
+    if (ksplit > 1 && epi != TC_F32) return B2_ERR_INVALID;
+    if (ksplit < 1) ksplit = 1;
+    {
+        const int nk = (K + kTcBK - 1) / kTcBK;
+        const int kbps = (nk + ksplit - 1) / ksplit;
+        if (slabs) *slabs = (nk + kbps - 1) / kbps;
+    }
     if (M <= 0 || N <= 0 || K <= 0) return B2_ERR_UNSUPPORTED;
     if ((K & 7) || !aligned16(A) || !aligned16(B) || !aligned16(C)) return B2_ERR_UNSUPPORTED;
     int* err = wait_error_word();
@@ -206,8 +233,8 @@ int gemm_tc(const __half* A, const __half* B, void* C, int M, int N, int K, int 
     if (rc != B2_OK) return rc;
     rc = make_tensor_map(&tb, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, B, db, sb, bb);
     if (rc != B2_OK) return rc;
-    return BN == 256 ? launch_tc_epi<256>(ta, tb, C, M, N, K, epi, err, s)
-                     : launch_tc_epi<128>(ta, tb, C, M, N, K, epi, err, s);
+    return BN == 256 ? launch_tc_epi<256>(ta, tb, C, M, N, K, epi, ksplit, err, s)
+                     : launch_tc_epi<128>(ta, tb, C, M, N, K, epi, ksplit, err, s);
 }
 
 // ---------------------------------------------------------------------------

@@ -37,6 +37,13 @@
 
 namespace b2 {
 
+// Batches up to kGemvMaxBatch decode with the fused GEMVs; larger batches
+// run the projections on the tensor cores (split-K GEMM, weights streamed
+// once per step for the whole batch).
+constexpr int kGemvMaxBatch = 8;
+constexpr int kMaxBatch = 256;
+constexpr int kMaxSplitK = 8;
+
 struct AttnParams;
 int attn_pick_splits(int batch, int nq, int nkv, int D, int max_len, size_t cap_floats);
 size_t attn_scratch_floats(int batch, int nq, int nkv, int D, int splits);
@@ -61,6 +68,11 @@ int causal_attention_rows_ld(const __half* q, int64_t ldq, const __half* k, cons
                              __half* out, int64_t ldo, int64_t S, int nq, int nkv, int D, int batch, cudaStream_t s);
 enum TcEpi : int { TC_HALF = 0, TC_F32 = 1, TC_F32_ADD = 2 };
 int gemm_tc(const __half* A, const __half* B, void* C, int M, int N, int K, int epi, cudaStream_t s);
+int gemm_tc_split(const __half* A, const __half* B, void* C, int M, int N, int K, int epi, int ksplit, int* slabs,
+                  cudaStream_t s);
+int attn_decode_launch_step_q(const __half* q, int64_t q_sb, const __half* kbase, const __half* vbase, int64_t sb,
+                              int64_t sh, int64_t ss, const int* seq_lens, __half* out, float* part, int splits,
+                              int B, int nq, int nkv, int D, cudaStream_t s);
 int* wait_error_word();
 
 // ---------------------------------------------------------------------------
@@ -209,9 +221,13 @@ __global__ void rmsnorm_rows_kernel(const float* __restrict__ hidden, const __ha
 // grid (T, nq + 2 nkv), D/2 threads.
 __global__ void rope_append_kernel(__half* __restrict__ qkv, int64_t ld, const float2* __restrict__ rope, int S,
                                    int nq, int nkv, int D, __half* __restrict__ kcache, __half* __restrict__ vcache,
-                                   int64_t kv_sb, int64_t kv_sh) {
+                                   int64_t kv_sb, int64_t kv_sh, const int* __restrict__ positions) {
+    griddep_wait();
     const int64_t t = blockIdx.x;
-    const int b = (int)(t / S), pos = (int)(t - (int64_t)b * S);
+    // prefill: row t is position t % S of sequence t / S; decode (positions
+    // given): row t is sequence t at positions[t]
+    const int b = positions ? (int)t : (int)(t / S);
+    const int pos = positions ? positions[t] : (int)(t - (int64_t)b * S);
     const int head = blockIdx.y, half = D >> 1, i = threadIdx.x;
     __half* row = qkv + t * ld + (int64_t)head * D;
     float x1 = __half2float(row[i]), x2 = __half2float(row[i + half]);
@@ -248,6 +264,100 @@ __global__ void prefill_end_kernel(const unsigned long long* __restrict__ argmax
     if (b < B) {
         tokens[b] = (int64_t)argmax_key_id(argmax[b]);
         positions[b] = S;
+    }
+}
+
+// ---------------------------------------------------------------------------
+// batched decode step (B > 8): tensor-core projections with split-K; each
+// GEMM writes fp32 partial slabs [slabs][B][N] that these kernels reduce in
+// slab order (deterministic) fused with the operation that follows.
+// ---------------------------------------------------------------------------
+__global__ void reduce_half_kernel(const float* __restrict__ ws, int slabs, int64_t MN, int N,
+                                   const __half* __restrict__ bias, __half* __restrict__ out) {
+    griddep_wait();
+    for (int64_t i = (blockIdx.x * (int64_t)blockDim.x + threadIdx.x) * 4; i < MN;
+         i += (int64_t)gridDim.x * blockDim.x * 4) {
+        float4 a = *reinterpret_cast<const float4*>(ws + i);
+        for (int z = 1; z < slabs; ++z) {
+            const float4 v = *reinterpret_cast<const float4*>(ws + (int64_t)z * MN + i);
+            a.x += v.x; a.y += v.y; a.z += v.z; a.w += v.w;
+        }
+        if (bias) {
+            const int n = (int)(i % N);
+            a.x += __half2float(bias[n]); a.y += __half2float(bias[n + 1]);
+            a.z += __half2float(bias[n + 2]); a.w += __half2float(bias[n + 3]);
+        }
+        __half2* o = reinterpret_cast<__half2*>(out + i);
+        o[0] = __floats2half2_rn(a.x, a.y);
+        o[1] = __floats2half2_rn(a.z, a.w);
+    }
+}
+
+// hidden = (add ? hidden : 0) + sum of the slabs
+__global__ void reduce_add_kernel(const float* __restrict__ ws, int slabs, int64_t MN, float* __restrict__ hidden,
+                                  int add) {
+    griddep_wait();
+    for (int64_t i = (blockIdx.x * (int64_t)blockDim.x + threadIdx.x) * 4; i < MN;
+         i += (int64_t)gridDim.x * blockDim.x * 4) {
+        float4 a = *reinterpret_cast<const float4*>(ws + i);
+        for (int z = 1; z < slabs; ++z) {
+            const float4 v = *reinterpret_cast<const float4*>(ws + (int64_t)z * MN + i);
+            a.x += v.x; a.y += v.y; a.z += v.z; a.w += v.w;
+        }
+        float4* h = reinterpret_cast<float4*>(hidden + i);
+        if (add) {
+            const float4 o = *h;
+            a.x += o.x; a.y += o.y; a.z += o.z; a.w += o.w;
+        }
+        *h = a;
+    }
+}
+
+// act = half(silu(gate) * up) from the two GEMMs' slabs
+__global__ void reduce_swiglu_kernel(const float* __restrict__ wg, int sg, const float* __restrict__ wu, int su,
+                                     int64_t MN, __half* __restrict__ act) {
+    griddep_wait();
+    for (int64_t i = (blockIdx.x * (int64_t)blockDim.x + threadIdx.x) * 4; i < MN;
+         i += (int64_t)gridDim.x * blockDim.x * 4) {
+        float4 g = *reinterpret_cast<const float4*>(wg + i);
+        for (int z = 1; z < sg; ++z) {
+            const float4 v = *reinterpret_cast<const float4*>(wg + (int64_t)z * MN + i);
+            g.x += v.x; g.y += v.y; g.z += v.z; g.w += v.w;
+        }
+        float4 u = *reinterpret_cast<const float4*>(wu + i);
+        for (int z = 1; z < su; ++z) {
+            const float4 v = *reinterpret_cast<const float4*>(wu + (int64_t)z * MN + i);
+            u.x += v.x; u.y += v.y; u.z += v.z; u.w += v.w;
+        }
+        __half2* o = reinterpret_cast<__half2*>(act + i);
+        o[0] = __floats2half2_rn(g.x / (1.0f + expf(-g.x)) * u.x, g.y / (1.0f + expf(-g.y)) * u.y);
+        o[1] = __floats2half2_rn(g.z / (1.0f + expf(-g.z)) * u.z, g.w / (1.0f + expf(-g.w)) * u.w);
+    }
+}
+
+// packed (value, id) argmax of each logits row, ties to the lower id;
+// ids >= limit are not candidates.  grid (chunks, B); argmax zeroed before.
+__global__ void rows_argmax_kernel(const float* __restrict__ logits, int V, int row_offset, int limit,
+                                   unsigned long long* __restrict__ argmax) {
+    griddep_wait();
+    __shared__ unsigned long long red[32];
+    const int b = blockIdx.y;
+    unsigned long long best = 0ull;
+    for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < V; i += gridDim.x * blockDim.x) {
+        const int gid = row_offset + i;
+        if (gid >= limit) break;
+        const unsigned long long k = argmax_key(logits[(int64_t)b * V + i], (uint32_t)gid);
+        best = k > best ? k : best;
+    }
+    for (int o = 16; o > 0; o >>= 1) {
+        const unsigned long long x = __shfl_xor_sync(0xffffffffu, best, o);
+        best = x > best ? x : best;
+    }
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = best;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        for (int w = 1; w < (int)(blockDim.x >> 5); ++w) best = red[w] > best ? red[w] : best;
+        if (best) atomicMax(argmax + b, best);
     }
 }
 
@@ -364,6 +474,14 @@ struct b2_model {
     int* push_ctr = nullptr;            // arrival counter of pushing kernels
     bool p2p_on = false;
     TpExchange tpx{};
+    // batched decode step (B > kGemvMaxBatch): split-K GEMM partial slabs and
+    // the fused q|k|v rows / normed activations of the step
+    float* bws_a = nullptr;
+    float* bws_b = nullptr;
+    size_t bws_floats = 0;
+    __half* bqkv = nullptr;  // [max_batch, qkv_rows]
+    __half* bxn = nullptr;   // [max_batch, H]
+
     unsigned long long* trace_buf = nullptr;  // step trace [slots][start, end]
     unsigned long long* trace_cur = nullptr;  // non-null while a traced step is enqueued
     int trace_next = 0;
@@ -372,6 +490,18 @@ struct b2_model {
     int splits = 1;
     int last_B = 0;  // batch of the most recent prefill / decode step
 };
+
+// Whether a decode step of B sequences runs the fused GEMVs: B within
+// kGemvMaxBatch and within the batch tile every projection's width allows
+// (the activation rows are staged in shared memory).  Otherwise the batched
+// tensor-core step runs.
+static bool gemv_step(const b2_model* m, int B) {
+    if (B > kGemvMaxBatch) return false;
+    const int Ks[3] = {m->cfg.hidden_size, m->nq * m->cfg.head_dim, m->inter};
+    for (int K : Ks)
+        if (B > gemv_batch_tile(K)) return false;
+    return true;
+}
 
 static int model_alloc(b2_model* m, void** p, size_t bytes) {
     cudaError_t e = cudaMalloc(p, bytes > 0 ? bytes : 16);
@@ -432,7 +562,7 @@ extern "C" int b2_model_create(const b2_model_config* cfg, int tp_rank, int tp_s
     const b2_model_config& c = *cfg;
     B2_REQUIRE(c.vocab_size > 0 && c.hidden_size > 0 && c.intermediate_size > 0 && c.num_layers > 0);
     B2_REQUIRE(c.num_q_heads > 0 && c.num_kv_heads > 0 && c.num_q_heads % c.num_kv_heads == 0);
-    B2_REQUIRE(c.max_batch >= 1 && c.max_batch <= 8 && c.max_seq >= 1);
+    B2_REQUIRE(c.max_batch >= 1 && c.max_batch <= kMaxBatch && c.max_seq >= 1);
     if (c.num_kv_heads % tp_size || c.intermediate_size % tp_size || c.vocab_size % tp_size) return B2_ERR_UNSUPPORTED;
     if (!attn_head_dim_supported(c.head_dim) || c.hidden_size % 8 || (c.intermediate_size / tp_size) % 8 ||
         (c.num_q_heads / tp_size * c.head_dim) % 8)
@@ -542,6 +672,16 @@ extern "C" int b2_model_create(const b2_model_config* cfg, int tp_rank, int tp_s
     M_ALLOC(m->positions, (size_t)B * sizeof(int));
     M_ALLOC(m->seq_lens, (size_t)B * sizeof(int));
     M_ALLOC(m->hidden2, (size_t)B * H * sizeof(float));
+    if (!gemv_step(m, B)) {  // batched decode step: split-K slabs, q|k|v rows, normed rows
+        size_t nmax = (size_t)m->qkv_rows;
+        if ((size_t)m->inter > nmax) nmax = m->inter;
+        if ((size_t)H > nmax) nmax = H;
+        m->bws_floats = (size_t)kMaxSplitK * B * nmax;
+        M_ALLOC(m->bws_a, m->bws_floats * sizeof(float));
+        M_ALLOC(m->bws_b, m->bws_floats * sizeof(float));
+        M_ALLOC(m->bqkv, (size_t)B * m->qkv_rows * hs);
+        M_ALLOC(m->bxn, (size_t)B * H * hs);
+    }
     M_ALLOC(m->step_ctr, 256);
     M_ALLOC(m->push_ctr, 256);
     if (tp_size > 1) {
@@ -926,8 +1066,100 @@ static int launch_lm_head(b2_model* m, int B, bool pdl, bool xch = false) {
     return gemv_launch(p, X_NORM, OUT_LOGITS, m->stream, pdl);
 }
 
+// split-K parts that give the GEMM about one CTA per SM
+static int split_for(int M, int N) {
+    const int tiles = ((N + 127) / 128) * ((M + 127) / 128);
+    int ks = (sm_count() + tiles - 1) / tiles;
+    return ks < 1 ? 1 : (ks > kMaxSplitK ? kMaxSplitK : ks);
+}
+
+static unsigned elem_blocks(int64_t n) {
+    int64_t blocks = (n / 4 + 255) / 256;
+    const int64_t cap = (int64_t)sm_count() * 8;
+    if (blocks > cap) blocks = cap;
+    return (unsigned)(blocks > 0 ? blocks : 1);
+}
+
+// Decode step for B > kGemvMaxBatch sequences: every projection is a
+// tensor-core GEMM with M = B (weights streamed once for the whole batch),
+// split along K so the grid covers the SMs; the partial slabs are reduced in
+// order by kernels fused with bias, RoPE + KV append, SwiGLU or the residual
+// add.  Attention, step begin / end are those of the GEMV step.
+// Final norm, lm_head GEMM (M = B) and the packed argmax of each row, on
+// m->hidden; argmax must be zero before.
+static int lm_head_rows(b2_model* m, int B) {
+    const b2_model_config& c = m->cfg;
+    cudaStream_t s = m->stream;
+    rmsnorm_rows_kernel<<<B, 256, 0, s>>>(m->hidden, m->final_norm, m->bxn, c.hidden_size, c.rms_norm_eps);
+    B2_CHECK_LAUNCH();
+    M_TRY(gemm_tc(m->bxn, m->lm_head, m->logits, B, m->vocab_l, c.hidden_size, TC_F32, s));
+    const int limit = c.vocab_size > 151665 ? 151665 : c.vocab_size;
+    const unsigned chunks = (unsigned)((m->vocab_l + 4095) / 4096);
+    rows_argmax_kernel<<<dim3(chunks, (unsigned)B), 256, 0, s>>>(m->logits, m->vocab_l, m->vocab_off, limit,
+                                                                m->argmax);
+    B2_CHECK_LAUNCH();
+    return B2_OK;
+}
+
+// one thread per sequence for the step / prefill end kernels
+static unsigned end_threads(int B) { return (unsigned)(((B + 31) / 32) * 32); }
+
+static int enqueue_step_batched(b2_model* m, int B) {
+    const b2_model_config& c = m->cfg;
+    cudaStream_t s = m->stream;
+    const int H = c.hidden_size, D = c.head_dim, I = m->inter, qd = m->nq * D, R = m->qkv_rows;
+    const float eps = c.rms_norm_eps;
+    int sl = 1, sg = 1, su = 1;
+    B2_TRY(launch(step_begin_kernel, dim3(B), dim3(256), 0, s, true, (const int64_t*)m->tokens,
+                  (const int*)m->positions, (const __half*)m->embed, m->hidden, H, m->seq_lens, m->argmax, m->hist,
+                  (const int*)m->hist_count, m->hist_cap, TraceSlot{nullptr, 0}));
+    for (int l = 0; l < c.num_layers; ++l) {
+        LayerW& w = m->layers[l];
+        __half* kbase = m->kv + (int64_t)l * m->kv_s_layer;
+        rmsnorm_rows_kernel<<<B, 256, 0, s>>>(m->hidden, w.ln1, m->bxn, H, eps);
+        B2_CHECK_LAUNCH();
+        M_TRY(gemm_tc_split(m->bxn, w.wqkv, m->bws_a, B, R, H, TC_F32, split_for(B, R), &sl, s));
+        reduce_half_kernel<<<elem_blocks((int64_t)B * R), 256, 0, s>>>(m->bws_a, sl, (int64_t)B * R, R, w.bqkv,
+                                                                       m->bqkv);
+        B2_CHECK_LAUNCH();
+        rope_append_kernel<<<dim3((unsigned)B, (unsigned)(m->nq + 2 * m->nkv)), D / 2, 0, s>>>(
+            m->bqkv, R, m->rope, 1, m->nq, m->nkv, D, kbase, kbase + m->kv_s_kv, m->kv_s_batch, m->kv_s_head,
+            m->positions);
+        B2_CHECK_LAUNCH();
+        M_TRY(attn_decode_launch_step_q(m->bqkv, R, kbase, kbase + m->kv_s_kv, m->kv_s_batch, m->kv_s_head, D,
+                                        m->seq_lens, m->attn, m->part, m->splits, B, m->nq, m->nkv, D, s));
+        M_TRY(gemm_tc_split(m->attn, w.wo, m->bws_a, B, H, qd, TC_F32, split_for(B, H), &sl, s));
+        reduce_add_kernel<<<elem_blocks((int64_t)B * H), 256, 0, s>>>(m->bws_a, sl, (int64_t)B * H, m->hidden,
+                                                                      m->rank == 0 ? 1 : 0);
+        B2_CHECK_LAUNCH();
+        M_TRY(nccl_sum_hidden(m, B));
+        rmsnorm_rows_kernel<<<B, 256, 0, s>>>(m->hidden, w.ln2, m->bxn, H, eps);
+        B2_CHECK_LAUNCH();
+        M_TRY(gemm_tc_split(m->bxn, w.wg, m->bws_a, B, I, H, TC_F32, split_for(B, I), &sg, s));
+        M_TRY(gemm_tc_split(m->bxn, w.wu, m->bws_b, B, I, H, TC_F32, split_for(B, I), &su, s));
+        reduce_swiglu_kernel<<<elem_blocks((int64_t)B * I), 256, 0, s>>>(m->bws_a, sg, m->bws_b, su,
+                                                                         (int64_t)B * I, m->act);
+        B2_CHECK_LAUNCH();
+        M_TRY(gemm_tc_split(m->act, w.wd, m->bws_a, B, H, I, TC_F32, split_for(B, H), &sl, s));
+        reduce_add_kernel<<<elem_blocks((int64_t)B * H), 256, 0, s>>>(m->bws_a, sl, (int64_t)B * H, m->hidden,
+                                                                      m->rank == 0 ? 1 : 0);
+        B2_CHECK_LAUNCH();
+        M_TRY(nccl_sum_hidden(m, B));
+    }
+    M_TRY(lm_head_rows(m, B));
+    if (m->tp > 1) {
+        if (nccl().AllReduce(m->argmax, m->argmax, (size_t)B, ncclUint64, ncclMax, m->comm, s) != ncclSuccess)
+            return B2_ERR_NCCL;
+    }
+    B2_TRY(launch(step_end_kernel, dim3(1), dim3(end_threads(B)), 0, s, false, (const unsigned long long*)m->argmax, m->tokens,
+                  m->positions, B, m->hist_count, m->hist_cap, 0, (const unsigned long long*)nullptr,
+                  (const unsigned*)nullptr, m->tp, c.max_batch, m->step_ctr, (int*)nullptr, TraceSlot{nullptr, 0}));
+    return B2_OK;
+}
+
 // Issue every launch of one decode step for B sequences on m->stream.
 static int enqueue_step(b2_model* m, int B) {
+    if (!gemv_step(m, B)) return enqueue_step_batched(m, B);
     const b2_model_config& c = m->cfg;
     cudaStream_t s = m->stream;
     const bool pdl = true;
@@ -953,7 +1185,7 @@ static int enqueue_step(b2_model* m, int B) {
         xch ? reinterpret_cast<const unsigned long long*>(static_cast<char*>(m->p2p_base) + m->off_am_recv) : nullptr;
     const unsigned* am_flags =
         xch ? reinterpret_cast<const unsigned*>(static_cast<char*>(m->p2p_base) + m->off_am_flags) : nullptr;
-    B2_TRY(launch(step_end_kernel, dim3(1), dim3(32), 0, s, pdl, (const unsigned long long*)m->argmax, m->tokens,
+    B2_TRY(launch(step_end_kernel, dim3(1), dim3(end_threads(B)), 0, s, pdl, (const unsigned long long*)m->argmax, m->tokens,
                   m->positions, B, m->hist_count, m->hist_cap, xch ? 1 : 0, am_recv, am_flags, m->tp,
                   c.max_batch, m->step_ctr, m->tpx.err, next_trace(m)));
     return B2_OK;
@@ -1093,7 +1325,7 @@ static int prefill_batched(b2_model* m, int B, int S) {
         if (w.bqkv) M_TRY(b2_bias_add(m->pf_qkv, w.bqkv, m->pf_qkv, T, m->qkv_rows, st));
         rope_append_kernel<<<dim3((unsigned)T, (unsigned)(m->nq + 2 * m->nkv)), D / 2, 0, st>>>(
             m->pf_qkv, m->qkv_rows, m->rope, S, m->nq, m->nkv, D, kbase, kbase + m->kv_s_kv, m->kv_s_batch,
-            m->kv_s_head);
+            m->kv_s_head, nullptr);
         B2_CHECK_LAUNCH();
         FlashArgs fa = {};
         fa.q = m->pf_qkv;
@@ -1125,12 +1357,13 @@ static int prefill_batched(b2_model* m, int B, int S) {
     gather_last_kernel<<<B, 256, 0, st>>>(m->pf_hidden, m->hidden, S, H);
     B2_CHECK_LAUNCH();
     B2_TRY(cudaMemsetAsync(m->argmax, 0, (size_t)B * sizeof(unsigned long long), st));
-    M_TRY(launch_lm_head(m, B, false));
+    if (gemv_step(m, B)) M_TRY(launch_lm_head(m, B, false));
+    else M_TRY(lm_head_rows(m, B));
     if (m->tp > 1) {
         if (nccl().AllReduce(m->argmax, m->argmax, (size_t)B, ncclUint64, ncclMax, m->comm, st) != ncclSuccess)
             return B2_ERR_NCCL;
     }
-    prefill_end_kernel<<<1, 32, 0, st>>>(m->argmax, m->tokens, m->positions, B, S);
+    prefill_end_kernel<<<1, end_threads(B), 0, st>>>(m->argmax, m->tokens, m->positions, B, S);
     B2_CHECK_LAUNCH();
     return B2_OK;
 }
@@ -1222,6 +1455,7 @@ extern "C" double b2_model_step_bytes(const b2_model* m, int B, int ctx) {
 
 extern "C" int b2_model_time_kernel(b2_model* m, int kind, int B, int reps, float* avg_ms) {
     B2_REQUIRE(m && avg_ms && B >= 1 && B <= m->cfg.max_batch && reps >= 1 && kind >= 0 && kind <= 5);
+    if (!gemv_step(m, B)) return B2_ERR_UNSUPPORTED;  // the batched step has no single fused kernel per kind
     const int L = m->cfg.num_layers;
     auto one = [&](int l) -> int {
         switch (kind) {
@@ -1294,6 +1528,8 @@ extern "C" int b2_model_trace_step(b2_model* m, int B, unsigned long long* host_
 
 extern "C" int b2_model_step_launches(const b2_model* m, int B) {
     if (!m) return 0;
+    if (!gemv_step(m, B))  // batched step: 13 launches per layer, final norm + lm_head GEMM + argmax
+        return 5 + m->cfg.num_layers * 13;
     // step_begin, per layer {qkv, attention (merges its own splits), o, gateup, down}, lm_head, step_end
     return 3 + m->cfg.num_layers * 5;
 }

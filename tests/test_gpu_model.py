@@ -224,3 +224,39 @@ def test_batched_prefill_matches_token_by_token(cuda):
         check_logits(lg_a[bb], lg_b[bb], f"b{bb}")
     a.close()
     b.close()
+
+
+def _batched_teacher_forced(cfg, seed, B, S0, n_dec, max_seq=64):
+    rng = np.random.default_rng(seed)
+    prompts = rng.integers(0, cfg.vocab, (B, S0))
+    conts = rng.integers(0, cfg.vocab, (B, n_dec))
+    m = make_model(cfg, seed, max_batch=B, max_seq=max_seq)
+    W = O.seeded_weights(cfg, seed)
+    lg = m.prefill(prompts)
+    refs = [O.forward(cfg, W, np.concatenate([prompts[b], conts[b]]), logit_row0=S0 - 1) for b in range(B)]
+    for b in range(B):
+        check_logits(lg[b], refs[b][0], f"prefill b{b}")
+    for i in range(n_dec):
+        lg, nxt = m.decode_step(conts[:, i], [S0 + i] * B, want_next=True)
+        for b in range(B):
+            check_logits(lg[b], refs[b][i + 1], f"decode {i} b{b}")
+            row = refs[b][i + 1]
+            top = int(np.argmax(row))
+            if int(nxt[b]) != top:
+                srt = np.sort(row)[::-1]
+                assert srt[0] - srt[1] < TIE_MARGIN, (i, b)
+    m.close()
+
+
+def test_batched_tensor_core_step_matches_oracle(cuda):
+    """B = 12 > the GEMV step's batch limit: every projection is a split-K
+    tcgen05 GEMM with M = B, partial slabs reduced with bias / RoPE / SwiGLU /
+    residual, lm_head GEMM + row argmax."""
+    _batched_teacher_forced(SMALL, 404, B=12, S0=8, n_dec=4)
+
+
+def test_batched_tensor_core_step_llama8b_width(cuda):
+    """Llama-3-8B widths at 2 layers, B = 4: the down projection's width
+    (14336) caps the GEMV batch tile at 2, so the tensor-core step runs."""
+    cfg = O.Config(vocab=128256, hidden=4096, inter=14336, layers=2, nq=32, nkv=8, head_dim=128, theta=500000.0)
+    _batched_teacher_forced(cfg, 405, B=4, S0=6, n_dec=3)
