@@ -144,10 +144,14 @@ int b2_flash_prefill_gqa(const void* q, const void* k, const void* v, void* out,
                          int num_q_heads, int num_kv_heads, int head_dim, int batch_size, void* stream);
 
 /* b2_flash_prefill_gqa with a choice of element type (bf16 != 0: bf16
- * q/k/v/out, else half) and rotate-half RoPE applied inside the kernel to q
- * and k at positions start_pos + s when rope_theta > 0 (q, k in memory are
- * left unrotated).  head_dim 64 or 128 only.  New API (the reference applies
- * RoPE as a separate apply_rope launch, src/model/forward_gpu.cu:419-421). */
+ * q/k/v/out, else half) and rotate-half RoPE at positions start_pos + s when
+ * rope_theta > 0: q rotated inside the attention kernel, k once per key by a
+ * pre-pass kernel of the same call into a per-device scratch copy
+ * (batch*S*nkv*head_dim*2 bytes, allocated on first use and grown as
+ * needed; RoPE calls on one device must not overlap in time).  q, k in
+ * memory are left unrotated.  head_dim 64 or 128 only.  New API (the
+ * reference applies RoPE as a separate apply_rope launch,
+ * src/model/forward_gpu.cu:419-421). */
 int b2_flash_prefill_gqa_ex(const void* q, const void* k, const void* v, void* out, int64_t seq_len,
                             int num_q_heads, int num_kv_heads, int head_dim, int batch_size, int bf16,
                             float rope_theta, int64_t start_pos, void* stream);

@@ -7,16 +7,19 @@
 //   S_j = Q K_j^T    M=128 queries, N=128 keys, K=D   (TMEM columns 0-255,
 //                    two buffers, so S_{j+1} is computed while row j's
 //                    softmax runs)
-//   O  += P_j V_j    M=128 queries, N=D, K=128 keys  (TMEM columns 256..)
-// Warp roles (192 threads, 320 with RoPE):
+//   O  += P_j V_j    M=128 queries, N=D, K=128 keys  (TMEM columns 256..;
+//                    columns 384.. hold the RoPE warps' angle tables)
+// Warp roles (192 threads):
 //   warp 4      TMA producer: Q once, then K_j / V_j into 2-stage rings;
 //   warp 5      MMA issuer (one thread): S_j, then P_{j-1} V_{j-1};
-//   warps 0..3  softmax, one query row per thread: row max of S_j (scale
-//               and causal mask applied on the fly), P_j = exp2(S - m) as
-//               half/bf16 into a swizzled shared-memory operand, running
-//               row sum; the output O / l at the end;
-//   warps 6..9  (RoPE form) rotate the Q tile and every K tile in shared
-//               memory before the MMA issuer may use them.
+//   warps 0..3  softmax, one query row per thread: (RoPE form) the row of
+//               Q rotated in shared memory first; then per key tile the row
+//               of S_j read from TMEM once into registers, causal mask, row
+//               max, P_j = exp2(S scale - m) as half/bf16 into one of two
+//               swizzled shared-memory P buffers (P_j is written while
+//               P_{j-1} V_{j-1} runs), running row sum; O / l at the end.
+// RoPE form: keys are rotated once by a pre-pass kernel of the same call
+// into a dense copy that the K tiles are loaded from.
 // Online softmax without a rescale per tile: the reference max m of a row
 // only moves when the tile max exceeds it by more than 8 (log2 units); P
 // values stay <= 2^8 otherwise, and when m moves the O row in TMEM is scaled
@@ -30,6 +33,7 @@
 // Reference replaced: src/cuda/flash_prefill.cu:43-240 (16 threads per CTA,
 // one query row per thread, scalar FMA, head_dim fixed at 64).
 #include <cmath>
+#include <mutex>
 #include <type_traits>
 
 #include "tc.cuh"
@@ -60,13 +64,13 @@ struct FlashCfg {
     static constexpr uint32_t OFF_Q = 0;
     static constexpr uint32_t OFF_K = TILE;                 // 2 stages
     static constexpr uint32_t OFF_V = 3 * TILE;             // 2 stages
-    static constexpr uint32_t OFF_P = 5 * TILE;
-    static constexpr uint32_t OFF_BAR = OFF_P + P_BYTES;
+    static constexpr uint32_t OFF_P = 5 * TILE;             // 2 buffers
+    static constexpr uint32_t OFF_BAR = OFF_P + 2 * P_BYTES;
     // 1 KB alignment slack; at least 120 KB so that one CTA (and its 512 TMEM
     // columns) owns an SM
     static constexpr size_t SMEM_NEED = OFF_BAR + 256 + 1024;
     static constexpr size_t SMEM = SMEM_NEED > 122880 ? SMEM_NEED : 122880;
-    static constexpr int THREADS = ROPE ? 320 : 192;
+    static constexpr int THREADS = 192;
     static constexpr uint32_t TMEM_COLS = 512;
 };
 
@@ -99,32 +103,81 @@ __device__ __forceinline__ uint32_t sw128_off(int row, int e) {
            ((uint32_t)(e & 7) << 1);
 }
 
-// Rotate-half RoPE of one tile row in shared memory at position `pos`:
-// x[i], x[i+D/2] -> x[i] cos - x[i+D/2] sin, x[i+D/2] cos + x[i] sin with
-// angle = pos * inv_freq[i] (the reference's float arithmetic,
-// src/cpu/ops.cpp:174-189).
+// Rotate-half RoPE of the reference (src/cpu/ops.cpp:174-189): x[i],
+// x[i+D/2] -> x[i] c - x[i+D/2] s, x[i+D/2] c + x[i] s with
+// (c, s) = (cos, sin)(float(pos) * inv_freq[i]), inv_freq[i] =
+// 1 / theta^(2i/D) -- the same float product per element as the reference.
+//
+// Q: row r of the tile (position p) rotated in shared memory by thread r.
 template <int D, bool BF16>
-__device__ __forceinline__ void rope_row(uint8_t* tile, int row, int pos, const float* invf) {
+__device__ __forceinline__ void rope_row(uint8_t* tile, int r, int p, const float* invf) {
     constexpr int H = D / 2;
 #pragma unroll 1
-    for (int e1 = 0; e1 < H; e1 += 8) {
-        uint4* p1 = reinterpret_cast<uint4*>(tile + sw128_off(row, e1));
-        uint4* p2 = reinterpret_cast<uint4*>(tile + sw128_off(row, e1 + H));
-        uint4 a = *p1, c = *p2;
+    for (int c = 0; c < H; c += 8) {
+        uint4* p1 = reinterpret_cast<uint4*>(tile + sw128_off(r, c));
+        uint4* p2 = reinterpret_cast<uint4*>(tile + sw128_off(r, c + H));
+        uint4 a = *p1, b = *p2;
         uint32_t* aw = reinterpret_cast<uint32_t*>(&a);
-        uint32_t* cw = reinterpret_cast<uint32_t*>(&c);
+        uint32_t* bw = reinterpret_cast<uint32_t*>(&b);
 #pragma unroll
-        for (int k = 0; k < 4; ++k) {
-            const float2 x1 = unpack2<BF16>(aw[k]), x2 = unpack2<BF16>(cw[k]);
+        for (int q = 0; q < 4; ++q) {
+            const float2 x1 = unpack2<BF16>(aw[q]), x2 = unpack2<BF16>(bw[q]);
             float s0, c0, s1, c1;
-            sincosf((float)pos * invf[e1 + 2 * k], &s0, &c0);
-            sincosf((float)pos * invf[e1 + 2 * k + 1], &s1, &c1);
-            aw[k] = pack2<BF16>(x1.x * c0 - x2.x * s0, x1.y * c1 - x2.y * s1);
-            cw[k] = pack2<BF16>(x2.x * c0 + x1.x * s0, x2.y * c1 + x1.y * s1);
+            sincosf((float)p * invf[c + 2 * q], &s0, &c0);
+            sincosf((float)p * invf[c + 2 * q + 1], &s1, &c1);
+            aw[q] = pack2<BF16>(x1.x * c0 - x2.x * s0, x1.y * c1 - x2.y * s1);
+            bw[q] = pack2<BF16>(x2.x * c0 + x1.x * s0, x2.y * c1 + x1.y * s1);
         }
         *p1 = a;
-        *p2 = c;
+        *p2 = b;
     }
+}
+
+// K: every key row rotated once, into a dense [batch][S][nkv][D] copy, before
+// the attention kernel runs (each key tile is read by every query tile and
+// query head of its group, so rotating it inside each CTA would repeat the
+// work S/128 * nq/nkv times).  One thread per 8 frequencies of a row.
+template <bool BF16>
+__global__ void rope_keys_kernel(const uint16_t* __restrict__ k, int64_t ldk, uint16_t* __restrict__ out, int S,
+                                 int nkv, int D, int batch, float theta, int pos0) {
+    __shared__ float invf[64];
+    const int H = D / 2;
+    if ((int)threadIdx.x < H) invf[threadIdx.x] = 1.0f / powf(theta, (float)(2 * threadIdx.x) / (float)D);
+    __syncthreads();
+    griddep_wait();
+    const int chunks = H / 8;
+    const int64_t n = (int64_t)batch * S * nkv * chunks;
+    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
+        const int c = (int)(i % chunks) * 8;
+        const int64_t row = i / chunks;  // (b, s, head)
+        const int hd = (int)(row % nkv);
+        const int64_t bs = row / nkv;
+        const int pos = pos0 + (int)(bs % S);
+        const uint16_t* src = k + bs * ldk + (int64_t)hd * D;
+        uint16_t* dst = out + row * D;
+        uint4 a = *reinterpret_cast<const uint4*>(src + c), b = *reinterpret_cast<const uint4*>(src + c + H);
+        uint32_t* aw = reinterpret_cast<uint32_t*>(&a);
+        uint32_t* bw = reinterpret_cast<uint32_t*>(&b);
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+            const float2 x1 = unpack2<BF16>(aw[q]), x2 = unpack2<BF16>(bw[q]);
+            float s0, c0, s1, c1;
+            sincosf((float)pos * invf[c + 2 * q], &s0, &c0);
+            sincosf((float)pos * invf[c + 2 * q + 1], &s1, &c1);
+            aw[q] = pack2<BF16>(x1.x * c0 - x2.x * s0, x1.y * c1 - x2.y * s1);
+            bw[q] = pack2<BF16>(x2.x * c0 + x1.x * s0, x2.y * c1 + x1.y * s1);
+        }
+        *reinterpret_cast<uint4*>(dst + c) = a;
+        *reinterpret_cast<uint4*>(dst + c + H) = b;
+    }
+}
+
+// 2^x on the SFU (ex2.approx, flush-to-zero): exp2(-inf) = 0, relative error
+// ~2^-22, far below the half/bf16 rounding that P gets next.
+__device__ __forceinline__ float fast_exp2(float x) {
+    float y;
+    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+    return y;
 }
 
 template <int D, bool BF16, bool ROPE>
@@ -144,15 +197,14 @@ __global__ void __launch_bounds__(FlashCfg<D, ROPE>::THREADS, 1)
     uint64_t* bar = reinterpret_cast<uint64_t*>(sm + Cfg::OFF_BAR);
     uint64_t* q_full = bar + 0;
     uint64_t* q_ready = bar + 1;
-    uint64_t* k_full = bar + 2;   // [2]
-    uint64_t* k_ready = bar + 4;  // [2]
+    uint64_t* k_full = bar + 2;   // [2] (bar + 4, + 5 spare)
     uint64_t* k_empty = bar + 6;  // [2]
     uint64_t* v_full = bar + 8;   // [2]
     uint64_t* v_empty = bar + 10; // [2]
     uint64_t* s_full = bar + 12;  // [2]
-    uint64_t* p_full = bar + 14;
-    uint64_t* o_done = bar + 15;
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bar + 16);
+    uint64_t* p_full = bar + 14;  // [2]
+    uint64_t* o_done = bar + 16;  // [2]: P_j V_j done, committed on o_done[j & 1]
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bar + 18);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int qt = (int)gridDim.x - 1 - (int)blockIdx.x;  // heaviest tiles first
@@ -166,14 +218,15 @@ __global__ void __launch_bounds__(FlashCfg<D, ROPE>::THREADS, 1)
         tc::mbar_init(q_ready, 128);
         for (int s = 0; s < 2; ++s) {
             tc::mbar_init(&k_full[s], 1);
-            tc::mbar_init(&k_ready[s], 128);
             tc::mbar_init(&k_empty[s], 1);
             tc::mbar_init(&v_full[s], 1);
             tc::mbar_init(&v_empty[s], 1);
             tc::mbar_init(&s_full[s], 1);
         }
-        tc::mbar_init(p_full, 128);
-        tc::mbar_init(o_done, 1);
+        for (int s = 0; s < 2; ++s) {
+            tc::mbar_init(&p_full[s], 128);
+            tc::mbar_init(&o_done[s], 1);
+        }
         tc::fence_barrier_init();
     }
     if (ROPE && threadIdx.x < D / 2) s_invf[threadIdx.x] = 1.0f / powf(rope_theta, (float)(2 * threadIdx.x) / (float)D);
@@ -220,7 +273,7 @@ __global__ void __launch_bounds__(FlashCfg<D, ROPE>::THREADS, 1)
                 if (j < nt) {
                     const int s = j & 1;
                     const uint32_t u = (uint32_t)j >> 1;
-                    ok = tc::mbar_wait(ROPE ? &k_ready[s] : &k_full[s], u & 1u, err, 14);
+                    ok = tc::mbar_wait(&k_full[s], u & 1u, err, 14);
                     if (!ok) break;
                     tc::fence_after_sync();
 #pragma unroll
@@ -235,122 +288,112 @@ __global__ void __launch_bounds__(FlashCfg<D, ROPE>::THREADS, 1)
                 if (j > 0) {
                     const int jj = j - 1, s = jj & 1;
                     const uint32_t u = (uint32_t)jj >> 1;
-                    ok = tc::mbar_wait(p_full, (uint32_t)jj & 1u, err, 15) && tc::mbar_wait(&v_full[s], u & 1u, err, 16);
+                    ok = tc::mbar_wait(&p_full[s], u & 1u, err, 15) && tc::mbar_wait(&v_full[s], u & 1u, err, 16);
                     if (!ok) break;
                     tc::fence_after_sync();
 #pragma unroll
                     for (int kk = 0; kk < 8; ++kk) {
                         const uint32_t offp = (uint32_t)(kk >> 2) * Cfg::ATOM + (uint32_t)(kk & 3) * 32;
-                        tc::mma_f16(tO, tc::desc_k_sw128(aP + offp),
+                        tc::mma_f16(tO, tc::desc_k_sw128(aP + s * Cfg::P_BYTES + offp),
                                     tc::desc_mn_sw128(aV + s * TILE + (uint32_t)kk * 2048u, Cfg::ATOM), idO,
                                     (jj > 0 || kk > 0) ? 1u : 0u);
                     }
-                    tc::mma_commit(o_done);
+                    tc::mma_commit(&o_done[s]);
                     tc::mma_commit(&v_empty[s]);
                 }
             }
         }
-    } else if (ROPE && warp >= 6) {
-        // ---------------- RoPE warps ----------------
-        const int t = threadIdx.x - 192;
-        bool ok = __all_sync(0xffffffffu, tc::mbar_wait(q_full, 0, err, 17));
-        if (ok) {
-            rope_row<D, BF16>(sQ, t, pos0 + q0 + t, s_invf);
-            tc::fence_proxy_async_smem();
-            tc::mbar_arrive(q_ready);
-        }
-        for (int j = 0; ok && j < nt; ++j) {
-            const int s = j & 1;
-            const uint32_t u = (uint32_t)j >> 1;
-            ok = __all_sync(0xffffffffu, tc::mbar_wait(&k_full[s], u & 1u, err, 18));
-            if (!ok) break;
-            rope_row<D, BF16>(sK + s * TILE, t, pos0 + j * 128 + t, s_invf);
-            tc::fence_proxy_async_smem();
-            tc::mbar_arrive(&k_ready[s]);
-        }
     } else if (warp < 4) {
         // ---------------- softmax and output ----------------
+        // Thread r owns query row r: S_j's row comes out of TMEM once (128
+        // registers), is masked and reduced, and P_j = exp2(S scale - m) goes
+        // to P buffer j & 1, so P_j is written while P_{j-1} V_{j-1} runs.
+        // The O row is touched only when m moves (after P_{j-1} V_{j-1}).
         const int r = warp * 32 + lane;
         const int qpos = q0 + r;
         const uint32_t lane_base = (uint32_t)(warp * 32) << 16;
-        float m = -INFINITY, l = 0.f;
+        float m = -1e30f, l = 0.f;  // finite start: a fully masked row keeps P = 0 and l = 0
         bool ok = true;
-        for (int j = 0; j < nt; ++j) {
+        if constexpr (ROPE) {  // rotate this thread's Q row before the first S = Q K^T
+            ok = __all_sync(0xffffffffu, tc::mbar_wait(q_full, 0, err, 17));
+            if (ok) {
+                rope_row<D, BF16>(sQ, r, pos0 + qpos, s_invf);
+                tc::fence_proxy_async_smem();
+                tc::mbar_arrive(q_ready);
+            }
+        }
+        for (int j = 0; ok && j < nt; ++j) {
             const int s = j & 1;
             const uint32_t u = (uint32_t)j >> 1;
             ok = __all_sync(0xffffffffu, tc::mbar_wait(&s_full[s], u & 1u, err, 19));
             if (!ok) break;
             tc::fence_after_sync();
+            uint32_t v[128];
             const uint32_t srow = tmem + lane_base + s * 128;
-            const int kbase = j * 128;
-            const bool masked = kbase + 127 > q0 || kbase + 128 > S;
-            // pass 1: row max of the scaled, masked scores
-            float mx = -INFINITY;
-#pragma unroll 1
-            for (int c = 0; c < 128; c += 32) {
-                uint32_t v[32];
-                tc::tmem_ld32(srow + c, v);
-                tc::tmem_wait_ld();
 #pragma unroll
-                for (int e = 0; e < 32; ++e) {
-                    const int key = kbase + c + e;
-                    float x = __uint_as_float(v[e]) * scale_log2;
-                    if (masked && (key > qpos || key >= S)) x = -INFINITY;
-                    mx = fmaxf(mx, x);
-                }
+            for (int c = 0; c < 4; ++c)
+                tc::tmem_ld32(srow + 32 * c, *reinterpret_cast<uint32_t(*)[32]>(&v[32 * c]));
+            tc::tmem_wait_ld();
+            const int kbase = j * 128;
+            if (kbase + 127 > q0 || kbase + 128 > S) {  // diagonal or ragged tile (warp-uniform)
+#pragma unroll
+                for (int e = 0; e < 128; ++e)
+                    if (kbase + e > qpos || kbase + e >= S) v[e] = 0xff800000u;  // -inf
             }
+            float mx4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
+#pragma unroll
+            for (int e = 0; e < 128; ++e) mx4[e & 3] = fmaxf(mx4[e & 3], __uint_as_float(v[e]));
+            const float mx = fmaxf(fmaxf(mx4[0], mx4[1]), fmaxf(mx4[2], mx4[3])) * scale_log2;
             const float m_new = fmaxf(m, mx);
             const bool resc = m_new > m + 8.f;
             const float m_use = resc ? m_new : m;
-            const float alpha = exp2f(m - m_use);
-            // P buffer free and O stable once P_{j-1} V_{j-1} has completed
-            if (j > 0) {
-                ok = __all_sync(0xffffffffu, tc::mbar_wait(o_done, (uint32_t)(j - 1) & 1u, err, 20));
+            const float alpha = fast_exp2(m - m_use);
+            if (j > 0 && __any_sync(0xffffffffu, resc)) {
+                // O must hold P_{j-1} V_{j-1} before this warp's rows are scaled
+                const uint32_t jj = (uint32_t)(j - 1);
+                ok = __all_sync(0xffffffffu, tc::mbar_wait(&o_done[jj & 1u], (jj >> 1) & 1u, err, 20));
                 if (!ok) break;
                 tc::fence_after_sync();
-                if (__any_sync(0xffffffffu, resc)) {
 #pragma unroll 1
-                    for (int c = 0; c < D; c += 32) {
-                        uint32_t v[32];
-                        tc::tmem_ld32(tO + lane_base + c, v);
-                        tc::tmem_wait_ld();
+                for (int c = 0; c < D; c += 32) {
+                    uint32_t o[32];
+                    tc::tmem_ld32(tO + lane_base + c, o);
+                    tc::tmem_wait_ld();
 #pragma unroll
-                        for (int e = 0; e < 32; ++e) v[e] = __float_as_uint(__uint_as_float(v[e]) * alpha);
-                        tc::tmem_st32(tO + lane_base + c, v);
-                    }
-                    tc::tmem_wait_st();
+                    for (int e = 0; e < 32; ++e) o[e] = __float_as_uint(__uint_as_float(o[e]) * alpha);
+                    tc::tmem_st32(tO + lane_base + c, o);
                 }
+                tc::tmem_wait_st();
             }
-            l *= alpha;
             m = m_use;
-            // pass 2: P = exp2(x - m) into the swizzled operand tile, row sum
-#pragma unroll 1
-            for (int c = 0; c < 128; c += 32) {
-                uint32_t v[32];
-                tc::tmem_ld32(srow + c, v);
-                tc::tmem_wait_ld();
-                uint32_t pk[16];
+            // P buffer s is free once P_{j-2} V_{j-2} has completed
+            if (j >= 2) {
+                ok = __all_sync(0xffffffffu, tc::mbar_wait(&o_done[s], (u - 1) & 1u, err, 22));
+                if (!ok) break;
+            }
+            uint8_t* pbuf = sP + s * Cfg::P_BYTES;
+            float l4[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
-                for (int e = 0; e < 32; e += 2) {
-                    float x0 = __uint_as_float(v[e]) * scale_log2, x1 = __uint_as_float(v[e + 1]) * scale_log2;
-                    const int key = kbase + c + e;
-                    if (masked && (key > qpos || key >= S)) x0 = -INFINITY;
-                    if (masked && (key + 1 > qpos || key + 1 >= S)) x1 = -INFINITY;
-                    const float p0 = exp2f(x0 - m), p1 = exp2f(x1 - m);
-                    l += p0 + p1;
+            for (int c = 0; c < 128; c += 8) {
+                uint32_t pk[4];
+#pragma unroll
+                for (int e = 0; e < 8; e += 2) {
+                    const float p0 = fast_exp2(fmaf(__uint_as_float(v[c + e]), scale_log2, -m));
+                    const float p1 = fast_exp2(fmaf(__uint_as_float(v[c + e + 1]), scale_log2, -m));
+                    l4[e >> 1] += p0 + p1;
                     pk[e >> 1] = pack2<BF16>(p0, p1);
                 }
-#pragma unroll
-                for (int q = 0; q < 4; ++q) {
-                    *reinterpret_cast<uint4*>(sP + sw128_off(r, c + q * 8)) =
-                        make_uint4(pk[4 * q], pk[4 * q + 1], pk[4 * q + 2], pk[4 * q + 3]);
-                }
+                *reinterpret_cast<uint4*>(pbuf + sw128_off(r, c)) = make_uint4(pk[0], pk[1], pk[2], pk[3]);
             }
+            l = l * alpha + ((l4[0] + l4[1]) + (l4[2] + l4[3]));
             tc::fence_proxy_async_smem();
             tc::fence_before_sync();
-            tc::mbar_arrive(p_full);
+            tc::mbar_arrive(&p_full[s]);
         }
-        if (ok) ok = __all_sync(0xffffffffu, tc::mbar_wait(o_done, (uint32_t)(nt - 1) & 1u, err, 21));
+        if (ok) {
+            const uint32_t jl = (uint32_t)(nt - 1);
+            ok = __all_sync(0xffffffffu, tc::mbar_wait(&o_done[jl & 1u], (jl >> 1) & 1u, err, 21));
+        }
         tc::fence_after_sync();
         const float inv_l = l > 0.f ? 1.f / l : 0.f;
         using T = typename std::conditional<BF16, __nv_bfloat16, __half>::type;
@@ -380,11 +423,48 @@ __global__ void __launch_bounds__(FlashCfg<D, ROPE>::THREADS, 1)
     }
 }
 
+// Rotated-key buffer of the RoPE form: one per device, grown on demand and
+// kept (freed at process exit).  Calls with RoPE on one device that overlap
+// in time (different streams) would share it and must not be issued.
+static std::mutex g_rk_mu;
+static void* g_rk_buf[64];
+static size_t g_rk_bytes[64];
+
+static int rotated_key_buffer(size_t bytes, void** out) {
+    int dev = 0;
+    B2_TRY(cudaGetDevice(&dev));
+    if (dev < 0 || dev >= 64) return B2_ERR_UNSUPPORTED;
+    std::lock_guard<std::mutex> lk(g_rk_mu);
+    if (g_rk_bytes[dev] < bytes) {
+        if (g_rk_buf[dev]) B2_TRY(cudaFree(g_rk_buf[dev]));
+        g_rk_buf[dev] = nullptr;
+        g_rk_bytes[dev] = 0;
+        B2_TRY(cudaMalloc(&g_rk_buf[dev], bytes));
+        g_rk_bytes[dev] = bytes;
+    }
+    *out = g_rk_buf[dev];
+    return B2_OK;
+}
+
 template <int D, bool BF16, bool ROPE>
-static int launch_flash(const FlashArgs& a, cudaStream_t s) {
+static int launch_flash(const FlashArgs& a_in, cudaStream_t s) {
     using Cfg = FlashCfg<D, ROPE>;
     int* err = wait_error_word();
     if (!err) return B2_ERR_STATE;
+    FlashArgs a = a_in;
+    if constexpr (ROPE) {  // keys rotated once into a dense copy; K tiles then come from it
+        void* rk = nullptr;
+        const int rrc = rotated_key_buffer((size_t)a.batch * a.S * a.nkv * D * 2, &rk);
+        if (rrc != B2_OK) return rrc;
+        const int64_t work = (int64_t)a.batch * a.S * a.nkv * (D / 16);
+        int64_t blocks = (work + 255) / 256;
+        if (blocks > (int64_t)sm_count() * 16) blocks = (int64_t)sm_count() * 16;
+        B2_TRY(launch(rope_keys_kernel<BF16>, dim3((unsigned)blocks), dim3(256), 0, s, true,
+                      static_cast<const uint16_t*>(a.k), a.ldkv, static_cast<uint16_t*>(rk), a.S, a.nkv, D, a.batch,
+                      a.rope_theta, a.pos0));
+        a.k = rk;
+    }
+    const int64_t ldk = ROPE ? (int64_t)a.nkv * D : a.ldkv;
     const CUtensorMapDataType dt = BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
     CUtensorMap tq, tk, tv;
     const uint32_t box[4] = {64, 1, 128, 1};
@@ -397,7 +477,8 @@ static int launch_flash(const FlashArgs& a, cudaStream_t s) {
     {
         const uint64_t dims[4] = {(uint64_t)D, (uint64_t)a.nkv, (uint64_t)a.S, (uint64_t)a.batch};
         const uint64_t st[3] = {(uint64_t)D * 2, (uint64_t)a.ldkv * 2, (uint64_t)a.S * a.ldkv * 2};
-        int rc = make_tensor_map(&tk, dt, 4, a.k, dims, st, box);
+        const uint64_t stk[3] = {(uint64_t)D * 2, (uint64_t)ldk * 2, (uint64_t)a.S * ldk * 2};
+        int rc = make_tensor_map(&tk, dt, 4, a.k, dims, stk, box);
         if (rc != B2_OK) return rc;
         rc = make_tensor_map(&tv, dt, 4, a.v, dims, st, box);
         if (rc != B2_OK) return rc;
