@@ -39,6 +39,27 @@ sys.path.insert(0, os.path.join(ROOT, "oracle"))
 METRIC = "decode tok/s (Llama-8B shape, bs1) at 1/2/4/8 B200; GEMV % of HBM peak"
 LLAMA8B = dict(vocab=128256, hidden=4096, inter=14336, layers=32, nq=32, nkv=8, head_dim=128, eps=1e-5,
                theta=500000.0)
+# BASELINE's model shapes (random-init; the metric's default is llama3-8b)
+MODELS = {
+    "llama3-8b": LLAMA8B,
+    "llama3-70b": dict(vocab=128256, hidden=8192, inter=28672, layers=80, nq=64, nkv=8, head_dim=128, eps=1e-5,
+                       theta=500000.0),
+    "tinyllama-1.1b": dict(vocab=32000, hidden=2048, inter=5632, layers=22, nq=32, nkv=4, head_dim=64, eps=1e-5,
+                           theta=10000.0),
+}
+
+
+def weight_gb(c):
+    lin = c["layers"] * ((c["nq"] + 2 * c["nkv"]) * c["head_dim"] * c["hidden"] + c["hidden"] * c["nq"] *
+                         c["head_dim"] + 3 * c["inter"] * c["hidden"]) + 2 * c["vocab"] * c["hidden"]
+    return 2.0 * lin / 1e9
+
+
+def model_cfg(args):
+    c = dict(MODELS[args.model])
+    if args.layers:
+        c["layers"] = args.layers
+    return c
 PROMPT = 512
 SEED_W, SEED_P = 1234, 42
 FALLBACK_HBM = 6650.0
@@ -206,15 +227,17 @@ def run_reference(args, rank, world):
 
 
 def config_dict(args, world):
-    return {"workload": f"Llama-3-8B-shaped decode, batch {args.batch}, {args.prompt}-token prompt then "
+    c = model_cfg(args)
+    return {"workload": f"{args.model}-shaped decode, batch {args.batch}, {args.prompt}-token prompt then "
                         f"{args.warmup}+{args.steps} decode steps",
-            "model": f"llama3-8b-shape random-init (H4096 L{args.layers} 32/8 heads D128 FFN14336 V128256, "
-                     "theta 5e5)",
+            "model": f"{args.model}-shape random-init (H{c['hidden']} L{c['layers']} {c['nq']}/{c['nkv']} heads "
+                     f"D{c['head_dim']} FFN{c['inter']} V{c['vocab']}, theta {c['theta']:g})",
             "global_batch": args.batch, "prompt_len": args.prompt,
             "ctx_range": [args.prompt + args.warmup, args.prompt + args.warmup + args.steps],
             "parallelism": f"tp{world}",
             "tp_exchange": (args.exchange if world > 1 else None),
-            "l2": "inputs larger than L2: every step streams ~15 GB of weights (L2 126 MB)"}
+            "l2": f"inputs larger than L2: every step streams the model's {weight_gb(c):.1f} GB of fp16 weights "
+                  f"(divided over the tensor-parallel ranks; L2 126 MB)"}
 
 
 # ---------------------------------------------------------------------------
@@ -237,7 +260,7 @@ def run_b2(args, rank, world, local):
         nccl_id = obj[0]
     B, K, W = args.batch, args.steps, args.warmup
     max_seq = max(4096, args.prompt + 2 * (W + K) + 8)
-    c = dict(LLAMA8B, layers=args.layers)
+    c = model_cfg(args)
     m = b2.Model(c["vocab"], c["hidden"], c["inter"], c["layers"], c["nq"], c["nkv"], c["head_dim"], eps=c["eps"],
                  theta=c["theta"], tied=False, max_batch=B, max_seq=max_seq, tp_rank=rank, tp_size=world,
                  nccl_id=nccl_id)
@@ -297,7 +320,10 @@ def run_b2(args, rank, world, local):
 
     # per-kernel launch durations (dominant kernel for the roofline)
     ctx_mid = pos0 + K // 2
-    ktimes = {k: m.time_kernel(k, B, reps=2) for k in b2.Model.KERNELS}
+    try:  # the fused-GEMV step; the batched tensor-core step has no per-kind kernel
+        ktimes = {k: m.time_kernel(k, B, reps=2) for k in b2.Model.KERNELS}
+    except b2.B2Error:
+        ktimes = {}
     kbytes = {k: m.kernel_bytes(k, B, ctx_mid) for k in b2.Model.KERNELS}
 
     # e2e: public step API with host buffers, same contexts as the timed loop
@@ -318,7 +344,7 @@ def run_b2(args, rank, world, local):
     ck = clocks.stop()
 
     trace = None
-    if args.trace:
+    if args.trace and ktimes:  # the fused-GEMV step carries trace points
         # per-launch device timestamps of a few live steps (b2_model_trace_step)
         names = ["step_begin"] + ["qkv", "attention", "o_proj", "gate_up", "down"] * c["layers"] + ["lm_head",
                                                                                                    "step_end"]
@@ -339,12 +365,15 @@ def run_b2(args, rank, world, local):
 
     if rank == 0:
         peak, peak_src = measured_peak()
-        dom = max(ktimes, key=lambda k: ktimes[k] * (c["layers"] if k != "lm_head" else 1))
-        dom = "gate_up" if "gate_up" in ktimes else dom
-        achieved = kbytes[dom] / (ktimes[dom] * 1e-3) / 1e9
         step_ms = ms / K
         step_bytes = m.step_bytes(B, ctx_mid)
         step_gbs = step_bytes / (step_ms * 1e-3) / 1e9
+        if ktimes:
+            dom = "gate_up"
+            achieved, dom_bytes, dom_ms, dom_name = (kbytes[dom] / (ktimes[dom] * 1e-3) / 1e9, kbytes[dom],
+                                                     ktimes[dom], f"gemv {dom}")
+        else:
+            achieved, dom_bytes, dom_ms, dom_name = step_gbs, step_bytes, step_ms, "whole decode step (batched)"
         launches = m.step_launches(B)
         out = {
             "metric": METRIC, "value": B * K / (ms * 1e-3), "unit": "tok/s", "n_gpus": world, "steps": K,
@@ -356,8 +385,9 @@ def run_b2(args, rank, world, local):
                     "d2h_bytes_per_step": 4 * B * c["vocab"] + 8 * B, "ms_per_step": ms_e2e / K,
                     "api": "b2_model_decode_step (host token + position in, fp32 logits + next id out)"},
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
-                         "frac": achieved / peak, "traffic": ncu_traffic(dom), "kernel": f"gemv {dom}",
-                         "bytes_per_launch": kbytes[dom], "launch_ms": ktimes[dom], "peak_source": peak_src},
+                         "frac": achieved / peak, "traffic": ncu_traffic("gate_up") if ktimes else None,
+                         "kernel": dom_name, "bytes_per_launch": dom_bytes, "launch_ms": dom_ms,
+                         "peak_source": peak_src},
             "step_roofline": {"bytes_per_step": step_bytes, "achieved": step_gbs, "peak": peak, "unit": "GB/s",
                               "frac": step_gbs / peak},
             "kernels_ms_per_launch": {k: round(v, 5) for k, v in ktimes.items()},
@@ -369,7 +399,7 @@ def run_b2(args, rank, world, local):
         }
         if trace:
             out["trace"] = trace
-        if world == 1 and not args.no_cpu_baseline:
+        if world == 1 and not args.no_cpu_baseline and args.model == "llama3-8b":
             try:
                 out["cpu_baseline"] = cpu_baseline_single()
             except Exception as ex:  # reported, never fatal
@@ -518,8 +548,10 @@ def main():
     ap.add_argument("--exchange", default="p2p", choices=["p2p", "nccl"],
                     help="tensor-parallel decode reduction: fused peer-memory exchange or NCCL all-reduce")
     ap.add_argument("--prompt", type=int, default=PROMPT, help="prompt length (512 for the metric)")
-    ap.add_argument("--layers", type=int, default=LLAMA8B["layers"],
-                    help="decoder depth (reduced only for small profiler captures; the metric uses 32)")
+    ap.add_argument("--layers", type=int, default=0,
+                    help="decoder depth override (reduced only for small profiler captures; 0 = the model's)")
+    ap.add_argument("--model", default="llama3-8b", choices=sorted(MODELS),
+                    help="model shape (the metric is quoted on llama3-8b)")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     rank = int(os.environ.get("RANK", "0"))

@@ -36,6 +36,9 @@ def main():
         ("small", O.Config(vocab=1000, hidden=256, inter=704, layers=2, nq=8, nkv=4, head_dim=32, theta=1e4), 12, 8),
         ("llama8b-width", O.Config(vocab=128256, hidden=4096, inter=14336, layers=2, nq=32, nkv=8, head_dim=128,
                                    theta=5e5), 16, 6),
+        # Llama-3-70B widths at reduced depth (full depth needs 278 GB of fp32 weights on the host)
+        ("llama70b-width", O.Config(vocab=128256, hidden=8192, inter=28672, layers=1, nq=64, nkv=8, head_dim=128,
+                                    theta=5e5), 12, 4),
     ]
     cases = [(n, c, s0, nd, x) for (n, c, s0, nd) in cases for x in ("nccl", "p2p")
              if c.nkv % world == 0 and c.inter % world == 0 and c.vocab % world == 0]
