@@ -25,6 +25,7 @@
 #include <dlfcn.h>
 #include <nccl.h>
 
+#include <algorithm>
 #include <cmath>
 #include <mutex>
 #include <cstdio>
@@ -34,6 +35,10 @@
 #include <vector>
 
 #include "gemv.cuh"
+#include "skinny.cuh"
+
+#include <cooperative_groups.h>
+namespace cg = cooperative_groups;
 
 namespace b2 {
 
@@ -42,7 +47,6 @@ namespace b2 {
 // once per step for the whole batch).
 constexpr int kGemvMaxBatch = 8;
 constexpr int kMaxBatch = 256;
-constexpr int kMaxSplitK = 8;
 
 struct AttnParams;
 int attn_pick_splits(int batch, int nq, int nkv, int D, int max_len, size_t cap_floats);
@@ -68,8 +72,6 @@ int causal_attention_rows_ld(const __half* q, int64_t ldq, const __half* k, cons
                              __half* out, int64_t ldo, int64_t S, int nq, int nkv, int D, int batch, cudaStream_t s);
 enum TcEpi : int { TC_HALF = 0, TC_F32 = 1, TC_F32_ADD = 2 };
 int gemm_tc(const __half* A, const __half* B, void* C, int M, int N, int K, int epi, cudaStream_t s);
-int gemm_tc_split(const __half* A, const __half* B, void* C, int M, int N, int K, int epi, int ksplit, int* slabs,
-                  cudaStream_t s);
 int attn_decode_launch_step_q(const __half* q, int64_t q_sb, const __half* kbase, const __half* vbase, int64_t sb,
                               int64_t sh, int64_t ss, const int* seq_lens, __half* out, float* part, int splits,
                               int B, int nq, int nkv, int D, cudaStream_t s);
@@ -268,86 +270,192 @@ __global__ void prefill_end_kernel(const unsigned long long* __restrict__ argmax
 }
 
 // ---------------------------------------------------------------------------
-// batched decode step (B > 8): tensor-core projections with split-K; each
-// GEMM writes fp32 partial slabs [slabs][B][N] that these kernels reduce in
-// slab order (deterministic) fused with the operation that follows.
+// consumers of the skinny (decode-batch) projections: each sums the fp32
+// partial slabs of its columns in slab order (skinny.cu) and fuses the
+// operation that follows the projection.
 // ---------------------------------------------------------------------------
-__global__ void reduce_half_kernel(const float* __restrict__ ws, int slabs, int64_t MN, int N,
-                                   const __half* __restrict__ bias, __half* __restrict__ out) {
+struct SkSlabs {
+    const float* ws;  // [slab][B][N]
+    int N, nk, per;
+    int col0;  // column of element 0 of this operand inside N
+};
+
+// columns n .. n+3 (n % 4 == 0, so one tile and one partial count)
+__device__ __forceinline__ float4 sk_sum4(const SkSlabs& a, int B, int b, int n) {
+    n += a.col0;
+    const int ns = sk_nseg(n, a.nk, a.per);
+    const size_t step = (size_t)B * a.N;
+    const float* p = a.ws + (size_t)b * a.N + n;
+    float4 x = *reinterpret_cast<const float4*>(p);
+#pragma unroll 4
+    for (int z = 1; z < ns; ++z) {
+        const float4 v = *reinterpret_cast<const float4*>(p + z * step);
+        x.x += v.x; x.y += v.y; x.z += v.z; x.w += v.w;
+    }
+    return x;
+}
+
+__device__ __forceinline__ float sk_sum(const SkSlabs& a, int B, int b, int n) {
+    n += a.col0;
+    const int ns = sk_nseg(n, a.nk, a.per);
+    const size_t step = (size_t)B * a.N;
+    const float* p = a.ws + (size_t)b * a.N + n;
+    float x = p[0];
+    for (int z = 1; z < ns; ++z) x += p[z * step];
+    return x;
+}
+
+// q|k|v of sequence b: sum + bias, rounded to half (the projection's output
+// type), RoPE (model table) on q and k, q into qkv row b, k and v appended
+// to the cache at positions[b].  Thread = (head, 4 rotation pairs i..i+3 and
+// i+D/2..); grid (B, ceil((nq + 2 nkv) D/8 / 256)), 256 threads.
+__global__ void sk_qkv_rope_kernel(SkSlabs a, int B, const __half* __restrict__ bias, __half* __restrict__ qkv,
+                                   int64_t ld, const float2* __restrict__ rope, int nq, int nkv, int D,
+                                   __half* __restrict__ kcache, __half* __restrict__ vcache, int64_t kv_sb,
+                                   int64_t kv_sh, const int* __restrict__ positions) {
     griddep_wait();
-    for (int64_t i = (blockIdx.x * (int64_t)blockDim.x + threadIdx.x) * 4; i < MN;
-         i += (int64_t)gridDim.x * blockDim.x * 4) {
-        float4 a = *reinterpret_cast<const float4*>(ws + i);
-        for (int z = 1; z < slabs; ++z) {
-            const float4 v = *reinterpret_cast<const float4*>(ws + (int64_t)z * MN + i);
-            a.x += v.x; a.y += v.y; a.z += v.z; a.w += v.w;
-        }
+    griddep_launch_dependents();
+    const int b = blockIdx.x, half = D >> 1, per_head = D >> 3;
+    const int t = blockIdx.y * blockDim.x + threadIdx.x;
+    const int head = t / per_head, i = (t - head * per_head) * 4;
+    if (head >= nq + 2 * nkv) return;
+    const int n1 = head * D + i, n2 = n1 + half;
+    const float4 s1 = sk_sum4(a, B, b, n1), s2 = sk_sum4(a, B, b, n2);
+    float x1[4] = {s1.x, s1.y, s1.z, s1.w}, x2[4] = {s2.x, s2.y, s2.z, s2.w};
+    __half o1[4], o2[4];
+    const int pos = positions[b];
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
         if (bias) {
-            const int n = (int)(i % N);
-            a.x += __half2float(bias[n]); a.y += __half2float(bias[n + 1]);
-            a.z += __half2float(bias[n + 2]); a.w += __half2float(bias[n + 3]);
+            x1[e] += __half2float(bias[n1 + e]);
+            x2[e] += __half2float(bias[n2 + e]);
         }
-        __half2* o = reinterpret_cast<__half2*>(out + i);
-        o[0] = __floats2half2_rn(a.x, a.y);
-        o[1] = __floats2half2_rn(a.z, a.w);
+        x1[e] = __half2float(__float2half_rn(x1[e]));
+        x2[e] = __half2float(__float2half_rn(x2[e]));
+        if (head < nq + nkv) {
+            const float2 cs = rope[(int64_t)pos * half + i + e];
+            o1[e] = __float2half_rn(x1[e] * cs.x - x2[e] * cs.y);
+            o2[e] = __float2half_rn(x2[e] * cs.x + x1[e] * cs.y);
+        } else {
+            o1[e] = __float2half_rn(x1[e]);
+            o2[e] = __float2half_rn(x2[e]);
+        }
+    }
+    __half* dst;
+    if (head < nq) dst = qkv + (int64_t)b * ld + (int64_t)head * D;
+    else if (head < nq + nkv) dst = kcache + b * kv_sb + (int64_t)(head - nq) * kv_sh + (int64_t)pos * D;
+    else dst = vcache + b * kv_sb + (int64_t)(head - nq - nkv) * kv_sh + (int64_t)pos * D;
+    __half2 p0 = __halves2half2(o1[0], o1[1]), p1 = __halves2half2(o1[2], o1[3]);
+    __half2 q0 = __halves2half2(o2[0], o2[1]), q1 = __halves2half2(o2[2], o2[3]);
+    uint2 w1, w2;
+    w1.x = *reinterpret_cast<uint32_t*>(&p0);
+    w1.y = *reinterpret_cast<uint32_t*>(&p1);
+    w2.x = *reinterpret_cast<uint32_t*>(&q0);
+    w2.y = *reinterpret_cast<uint32_t*>(&q1);
+    *reinterpret_cast<uint2*>(dst + i) = w1;
+    *reinterpret_cast<uint2*>(dst + i + half) = w2;
+}
+
+// hidden[b] = (add ? hidden[b] : 0) + projection; then, when norm_w is set,
+// xn[b] = half(hidden[b] * rsqrt(mean(hidden[b]^2) + eps) * norm_w).  A
+// cluster of kAddNormCtas CTAs per row (grid (kAddNormCtas, B)), each over
+// H / kAddNormCtas columns, 4 per thread; the row's sum of squares is the
+// sum of the CTAs' partials read through distributed shared memory in rank
+// order (the same order in every CTA, so deterministic).
+constexpr int kAddNormCtas = 8;
+
+__global__ void __launch_bounds__(128) sk_add_norm_kernel(SkSlabs a, int B, float* __restrict__ hidden, int add,
+                                                          int H, const __half* __restrict__ norm_w,
+                                                          __half* __restrict__ xn, float eps) {
+    __shared__ float red[4];
+    __shared__ float part;
+    griddep_wait();
+    griddep_launch_dependents();
+    const int b = blockIdx.y;
+    const int cols = H / kAddNormCtas;
+    const int c0 = blockIdx.x * cols;
+    constexpr int kMaxV = 4;  // float4 groups per thread (H <= 16384)
+    float4 hv[kMaxV];
+    float ss = 0.f;
+#pragma unroll
+    for (int k = 0; k < kMaxV; ++k) {
+        const int n = c0 + 4 * ((int)threadIdx.x + k * (int)blockDim.x);
+        if (n < c0 + cols) {
+            float4 v = sk_sum4(a, B, b, n);
+            float4* h = reinterpret_cast<float4*>(hidden + (int64_t)b * H + n);
+            if (add) {
+                const float4 o = *h;
+                v.x = o.x + v.x; v.y = o.y + v.y; v.z = o.z + v.z; v.w = o.w + v.w;
+            }
+            *h = v;
+            hv[k] = v;
+            ss = fmaf(v.x, v.x, ss); ss = fmaf(v.y, v.y, ss); ss = fmaf(v.z, v.z, ss); ss = fmaf(v.w, v.w, ss);
+        }
+    }
+    if (!norm_w) return;  // uniform over the grid
+    for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = ss;
+    __syncthreads();
+    if (threadIdx.x == 0) part = (red[0] + red[1]) + (red[2] + red[3]);
+    cg::cluster_group cl = cg::this_cluster();
+    cl.sync();
+    float tot = 0.f;
+    for (int r = 0; r < kAddNormCtas; ++r) tot += *cl.map_shared_rank(&part, r);
+    cl.sync();  // no CTA leaves while another still reads its partial
+    const float rs = rsqrtf(tot / (float)H + eps);
+#pragma unroll
+    for (int k = 0; k < kMaxV; ++k) {
+        const int n = c0 + 4 * ((int)threadIdx.x + k * (int)blockDim.x);
+        if (n < c0 + cols) {
+            const float4 v = hv[k];
+            const uint2 wv = *reinterpret_cast<const uint2*>(norm_w + n);
+            const float2 w01 = __half22float2(*reinterpret_cast<const __half2*>(&wv.x));
+            const float2 w23 = __half22float2(*reinterpret_cast<const __half2*>(&wv.y));
+            __half2 o0 = __floats2half2_rn(v.x * rs * w01.x, v.y * rs * w01.y);
+            __half2 o1 = __floats2half2_rn(v.z * rs * w23.x, v.w * rs * w23.y);
+            uint2 ov;
+            ov.x = *reinterpret_cast<uint32_t*>(&o0);
+            ov.y = *reinterpret_cast<uint32_t*>(&o1);
+            *reinterpret_cast<uint2*>(xn + (int64_t)b * H + n) = ov;
+        }
     }
 }
 
-// hidden = (add ? hidden : 0) + sum of the slabs
-__global__ void reduce_add_kernel(const float* __restrict__ ws, int slabs, int64_t MN, float* __restrict__ hidden,
-                                  int add) {
+// act[b][i] = half(silu(gate) * up), silu(x) = x / (1 + exp(-x)) in fp32
+__global__ void sk_swiglu_kernel(SkSlabs g, SkSlabs u, int B, int I, __half* __restrict__ act) {
     griddep_wait();
-    for (int64_t i = (blockIdx.x * (int64_t)blockDim.x + threadIdx.x) * 4; i < MN;
-         i += (int64_t)gridDim.x * blockDim.x * 4) {
-        float4 a = *reinterpret_cast<const float4*>(ws + i);
-        for (int z = 1; z < slabs; ++z) {
-            const float4 v = *reinterpret_cast<const float4*>(ws + (int64_t)z * MN + i);
-            a.x += v.x; a.y += v.y; a.z += v.z; a.w += v.w;
-        }
-        float4* h = reinterpret_cast<float4*>(hidden + i);
-        if (add) {
-            const float4 o = *h;
-            a.x += o.x; a.y += o.y; a.z += o.z; a.w += o.w;
-        }
-        *h = a;
+    griddep_launch_dependents();
+    const int64_t n = (int64_t)B * I / 4;
+    for (int64_t e = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; e < n; e += (int64_t)gridDim.x * blockDim.x) {
+        const int b = (int)(4 * e / I), i = (int)(4 * e - (int64_t)b * I);
+        const float4 x = sk_sum4(g, B, b, i), y = sk_sum4(u, B, b, i);
+        __half2 o0 = __floats2half2_rn(x.x / (1.0f + expf(-x.x)) * y.x, x.y / (1.0f + expf(-x.y)) * y.y);
+        __half2 o1 = __floats2half2_rn(x.z / (1.0f + expf(-x.z)) * y.z, x.w / (1.0f + expf(-x.w)) * y.w);
+        uint2 ov;
+        ov.x = *reinterpret_cast<uint32_t*>(&o0);
+        ov.y = *reinterpret_cast<uint32_t*>(&o1);
+        *reinterpret_cast<uint2*>(act + 4 * e) = ov;
     }
 }
 
-// act = half(silu(gate) * up) from the two GEMMs' slabs
-__global__ void reduce_swiglu_kernel(const float* __restrict__ wg, int sg, const float* __restrict__ wu, int su,
-                                     int64_t MN, __half* __restrict__ act) {
-    griddep_wait();
-    for (int64_t i = (blockIdx.x * (int64_t)blockDim.x + threadIdx.x) * 4; i < MN;
-         i += (int64_t)gridDim.x * blockDim.x * 4) {
-        float4 g = *reinterpret_cast<const float4*>(wg + i);
-        for (int z = 1; z < sg; ++z) {
-            const float4 v = *reinterpret_cast<const float4*>(wg + (int64_t)z * MN + i);
-            g.x += v.x; g.y += v.y; g.z += v.z; g.w += v.w;
-        }
-        float4 u = *reinterpret_cast<const float4*>(wu + i);
-        for (int z = 1; z < su; ++z) {
-            const float4 v = *reinterpret_cast<const float4*>(wu + (int64_t)z * MN + i);
-            u.x += v.x; u.y += v.y; u.z += v.z; u.w += v.w;
-        }
-        __half2* o = reinterpret_cast<__half2*>(act + i);
-        o[0] = __floats2half2_rn(g.x / (1.0f + expf(-g.x)) * u.x, g.y / (1.0f + expf(-g.y)) * u.y);
-        o[1] = __floats2half2_rn(g.z / (1.0f + expf(-g.z)) * u.z, g.w / (1.0f + expf(-g.w)) * u.w);
-    }
-}
-
-// packed (value, id) argmax of each logits row, ties to the lower id;
-// ids >= limit are not candidates.  grid (chunks, B); argmax zeroed before.
-__global__ void rows_argmax_kernel(const float* __restrict__ logits, int V, int row_offset, int limit,
-                                   unsigned long long* __restrict__ argmax) {
-    griddep_wait();
+// logits[b][v] = lm_head projection (fp32) and the packed argmax of each row
+// (ties to the lower id, ids >= limit excluded); argmax zeroed before.
+// grid (chunks, B), 256 threads.
+__global__ void sk_logits_argmax_kernel(SkSlabs a, int B, float* __restrict__ logits, int V, int row_offset,
+                                        int limit, unsigned long long* __restrict__ argmax) {
     __shared__ unsigned long long red[32];
+    griddep_wait();
+    griddep_launch_dependents();
     const int b = blockIdx.y;
     unsigned long long best = 0ull;
     for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < V; i += gridDim.x * blockDim.x) {
+        const float x = sk_sum(a, B, b, i);
+        logits[(int64_t)b * V + i] = x;
         const int gid = row_offset + i;
-        if (gid >= limit) break;
-        const unsigned long long k = argmax_key(logits[(int64_t)b * V + i], (uint32_t)gid);
-        best = k > best ? k : best;
+        if (gid < limit) {
+            const unsigned long long k = argmax_key(x, (uint32_t)gid);
+            best = k > best ? k : best;
+        }
     }
     for (int o = 16; o > 0; o >>= 1) {
         const unsigned long long x = __shfl_xor_sync(0xffffffffu, best, o);
@@ -672,11 +780,22 @@ extern "C" int b2_model_create(const b2_model_config* cfg, int tp_rank, int tp_s
     M_ALLOC(m->positions, (size_t)B * sizeof(int));
     M_ALLOC(m->seq_lens, (size_t)B * sizeof(int));
     M_ALLOC(m->hidden2, (size_t)B * H * sizeof(float));
-    if (!gemv_step(m, B)) {  // batched decode step: split-K slabs, q|k|v rows, normed rows
-        size_t nmax = (size_t)m->qkv_rows;
-        if ((size_t)m->inter > nmax) nmax = m->inter;
-        if ((size_t)H > nmax) nmax = H;
-        m->bws_floats = (size_t)kMaxSplitK * B * nmax;
+    if (!gemv_step(m, B)) {  // batched decode step: skinny partial slabs, q|k|v rows, normed rows
+        if (H % (4 * kAddNormCtas) || H > 16 * 128 * kAddNormCtas || m->inter % 4 || D % 8) {
+            b2_model_destroy(m);
+            return B2_ERR_UNSUPPORTED;
+        }
+        const int qd = m->nq * D, I = m->inter;
+        auto need = [&](int N, int K) {
+            const SkinnyPlan p = skinny_plan(N, K);
+            return (size_t)p.max_slabs * B * N;
+        };
+        size_t f = need(m->qkv_rows, H);
+        f = std::max(f, need(H, qd));
+        f = std::max(f, (I % 128) == 0 ? need(2 * I, H) : need(I, H));
+        f = std::max(f, need(H, I));
+        f = std::max(f, need(m->vocab_l, H));
+        m->bws_floats = f;
         M_ALLOC(m->bws_a, m->bws_floats * sizeof(float));
         M_ALLOC(m->bws_b, m->bws_floats * sizeof(float));
         M_ALLOC(m->bqkv, (size_t)B * m->qkv_rows * hs);
@@ -1066,93 +1185,114 @@ static int launch_lm_head(b2_model* m, int B, bool pdl, bool xch = false) {
     return gemv_launch(p, X_NORM, OUT_LOGITS, m->stream, pdl);
 }
 
-// split-K parts that give the GEMM about one CTA per SM
-static int split_for(int M, int N) {
-    const int tiles = ((N + 127) / 128) * ((M + 127) / 128);
-    int ks = (sm_count() + tiles - 1) / tiles;
-    return ks < 1 ? 1 : (ks > kMaxSplitK ? kMaxSplitK : ks);
-}
-
-static unsigned elem_blocks(int64_t n) {
-    int64_t blocks = (n / 4 + 255) / 256;
-    const int64_t cap = (int64_t)sm_count() * 8;
-    if (blocks > cap) blocks = cap;
-    return (unsigned)(blocks > 0 ? blocks : 1);
-}
 
 // Decode step for B > kGemvMaxBatch sequences: every projection is a
 // tensor-core GEMM with M = B (weights streamed once for the whole batch),
 // split along K so the grid covers the SMs; the partial slabs are reduced in
 // order by kernels fused with bias, RoPE + KV append, SwiGLU or the residual
 // add.  Attention, step begin / end are those of the GEMV step.
-// Final norm, lm_head GEMM (M = B) and the packed argmax of each row, on
-// m->hidden; argmax must be zero before.
+// Skinny projection X W^T of B rows into `ws`, and the slab descriptor its
+// consumer kernel reads.
+static int sk_proj(b2_model* m, const __half* X, int B, const __half* W0, int N0, const __half* W1, int N1, int K,
+                   float* ws, SkSlabs* out) {
+    SkinnyPlan pl;
+    M_TRY(gemm_skinny(X, B, W0, N0, W1, N1, K, ws, m->bws_floats, &pl, m->stream));
+    out->ws = ws;
+    out->N = N0 + N1;
+    out->nk = pl.nk;
+    out->per = pl.per;
+    out->col0 = 0;
+    return B2_OK;
+}
+
+// lm_head of the normalised rows m->bxn (skinny projection), logits and the
+// packed argmax of each row; argmax must be zero before.
 static int lm_head_rows(b2_model* m, int B) {
     const b2_model_config& c = m->cfg;
-    cudaStream_t s = m->stream;
-    rmsnorm_rows_kernel<<<B, 256, 0, s>>>(m->hidden, m->final_norm, m->bxn, c.hidden_size, c.rms_norm_eps);
-    B2_CHECK_LAUNCH();
-    M_TRY(gemm_tc(m->bxn, m->lm_head, m->logits, B, m->vocab_l, c.hidden_size, TC_F32, s));
+    SkSlabs lg;
+    M_TRY(sk_proj(m, m->bxn, B, m->lm_head, m->vocab_l, nullptr, 0, c.hidden_size, m->bws_a, &lg));
     const int limit = c.vocab_size > 151665 ? 151665 : c.vocab_size;
     const unsigned chunks = (unsigned)((m->vocab_l + 4095) / 4096);
-    rows_argmax_kernel<<<dim3(chunks, (unsigned)B), 256, 0, s>>>(m->logits, m->vocab_l, m->vocab_off, limit,
-                                                                m->argmax);
-    B2_CHECK_LAUNCH();
+    B2_TRY(launch(sk_logits_argmax_kernel, dim3(chunks, (unsigned)B), dim3(256), 0, m->stream, true, lg, B,
+                  m->logits, m->vocab_l, m->vocab_off, limit, m->argmax));
     return B2_OK;
 }
 
 // one thread per sequence for the step / prefill end kernels
 static unsigned end_threads(int B) { return (unsigned)(((B + 31) / 32) * 32); }
 
+// hidden += projection (rank 0 adds the residual), then the next RMSNorm
+// into m->bxn: fused when there is no all-reduce in between.
+static int add_and_norm(b2_model* m, const SkSlabs& a, int B, const __half* norm_w) {
+    const b2_model_config& c = m->cfg;
+    const int H = c.hidden_size;
+    const int add = m->rank == 0 ? 1 : 0;
+    if (m->tp == 1) {
+        B2_TRY(launch_cluster(sk_add_norm_kernel, dim3(kAddNormCtas, (unsigned)B), dim3(128), 0, m->stream, true,
+                              kAddNormCtas, a, B, m->hidden, add, H, norm_w, m->bxn, c.rms_norm_eps));
+        return B2_OK;
+    }
+    B2_TRY(launch_cluster(sk_add_norm_kernel, dim3(kAddNormCtas, (unsigned)B), dim3(128), 0, m->stream, true,
+                          kAddNormCtas, a, B, m->hidden, add, H, (const __half*)nullptr, (__half*)nullptr,
+                          c.rms_norm_eps));
+    M_TRY(nccl_sum_hidden(m, B));
+    rmsnorm_rows_kernel<<<B, 256, 0, m->stream>>>(m->hidden, norm_w, m->bxn, H, c.rms_norm_eps);
+    B2_CHECK_LAUNCH();
+    return B2_OK;
+}
+
+// Decode step for batches the GEMV step does not take (B > kGemvMaxBatch, or
+// a weight width that caps the GEMV batch tile below B): every projection is
+// a skinny tensor-core weight stream (skinny.cu) whose partial slabs are
+// summed by the kernel of the operation that follows it -- q|k|v + RoPE + KV
+// append, residual add + next RMSNorm, SwiGLU, logits + argmax.  Attention,
+// step begin / end are those of the GEMV step.
 static int enqueue_step_batched(b2_model* m, int B) {
     const b2_model_config& c = m->cfg;
     cudaStream_t s = m->stream;
     const int H = c.hidden_size, D = c.head_dim, I = m->inter, qd = m->nq * D, R = m->qkv_rows;
-    const float eps = c.rms_norm_eps;
-    int sl = 1, sg = 1, su = 1;
+    const bool fuse_gu = (I % 128) == 0;
     B2_TRY(launch(step_begin_kernel, dim3(B), dim3(256), 0, s, true, (const int64_t*)m->tokens,
                   (const int*)m->positions, (const __half*)m->embed, m->hidden, H, m->seq_lens, m->argmax, m->hist,
                   (const int*)m->hist_count, m->hist_cap, TraceSlot{nullptr, 0}));
+    rmsnorm_rows_kernel<<<B, 256, 0, s>>>(m->hidden, m->layers[0].ln1, m->bxn, H, c.rms_norm_eps);
+    B2_CHECK_LAUNCH();
     for (int l = 0; l < c.num_layers; ++l) {
         LayerW& w = m->layers[l];
         __half* kbase = m->kv + (int64_t)l * m->kv_s_layer;
-        rmsnorm_rows_kernel<<<B, 256, 0, s>>>(m->hidden, w.ln1, m->bxn, H, eps);
-        B2_CHECK_LAUNCH();
-        M_TRY(gemm_tc_split(m->bxn, w.wqkv, m->bws_a, B, R, H, TC_F32, split_for(B, R), &sl, s));
-        reduce_half_kernel<<<elem_blocks((int64_t)B * R), 256, 0, s>>>(m->bws_a, sl, (int64_t)B * R, R, w.bqkv,
-                                                                       m->bqkv);
-        B2_CHECK_LAUNCH();
-        rope_append_kernel<<<dim3((unsigned)B, (unsigned)(m->nq + 2 * m->nkv)), D / 2, 0, s>>>(
-            m->bqkv, R, m->rope, 1, m->nq, m->nkv, D, kbase, kbase + m->kv_s_kv, m->kv_s_batch, m->kv_s_head,
-            m->positions);
-        B2_CHECK_LAUNCH();
+        SkSlabs qkv, o, g, u, d;
+        M_TRY(sk_proj(m, m->bxn, B, w.wqkv, R, nullptr, 0, H, m->bws_a, &qkv));
+        const unsigned qkv_threads = (unsigned)((m->nq + 2 * m->nkv) * (D / 8));
+        B2_TRY(launch(sk_qkv_rope_kernel, dim3((unsigned)B, (qkv_threads + 255) / 256), dim3(256), 0, s, true,
+                      qkv, B, (const __half*)w.bqkv, m->bqkv, (int64_t)R, (const float2*)m->rope, m->nq, m->nkv, D,
+                      kbase, kbase + m->kv_s_kv, m->kv_s_batch, m->kv_s_head, (const int*)m->positions));
         M_TRY(attn_decode_launch_step_q(m->bqkv, R, kbase, kbase + m->kv_s_kv, m->kv_s_batch, m->kv_s_head, D,
                                         m->seq_lens, m->attn, m->part, m->splits, B, m->nq, m->nkv, D, s));
-        M_TRY(gemm_tc_split(m->attn, w.wo, m->bws_a, B, H, qd, TC_F32, split_for(B, H), &sl, s));
-        reduce_add_kernel<<<elem_blocks((int64_t)B * H), 256, 0, s>>>(m->bws_a, sl, (int64_t)B * H, m->hidden,
-                                                                      m->rank == 0 ? 1 : 0);
-        B2_CHECK_LAUNCH();
-        M_TRY(nccl_sum_hidden(m, B));
-        rmsnorm_rows_kernel<<<B, 256, 0, s>>>(m->hidden, w.ln2, m->bxn, H, eps);
-        B2_CHECK_LAUNCH();
-        M_TRY(gemm_tc_split(m->bxn, w.wg, m->bws_a, B, I, H, TC_F32, split_for(B, I), &sg, s));
-        M_TRY(gemm_tc_split(m->bxn, w.wu, m->bws_b, B, I, H, TC_F32, split_for(B, I), &su, s));
-        reduce_swiglu_kernel<<<elem_blocks((int64_t)B * I), 256, 0, s>>>(m->bws_a, sg, m->bws_b, su,
-                                                                         (int64_t)B * I, m->act);
-        B2_CHECK_LAUNCH();
-        M_TRY(gemm_tc_split(m->act, w.wd, m->bws_a, B, H, I, TC_F32, split_for(B, H), &sl, s));
-        reduce_add_kernel<<<elem_blocks((int64_t)B * H), 256, 0, s>>>(m->bws_a, sl, (int64_t)B * H, m->hidden,
-                                                                      m->rank == 0 ? 1 : 0);
-        B2_CHECK_LAUNCH();
-        M_TRY(nccl_sum_hidden(m, B));
+        M_TRY(sk_proj(m, m->attn, B, w.wo, H, nullptr, 0, qd, m->bws_a, &o));
+        M_TRY(add_and_norm(m, o, B, w.ln2));
+        if (fuse_gu) {
+            M_TRY(sk_proj(m, m->bxn, B, w.wg, I, w.wu, I, H, m->bws_a, &g));
+            u = g;
+            u.col0 = I;
+        } else {
+            M_TRY(sk_proj(m, m->bxn, B, w.wg, I, nullptr, 0, H, m->bws_a, &g));
+            M_TRY(sk_proj(m, m->bxn, B, w.wu, I, nullptr, 0, H, m->bws_b, &u));
+        }
+        {
+            int64_t blocks = ((int64_t)B * I / 4 + 255) / 256;
+            if (blocks > (int64_t)sm_count() * 8) blocks = (int64_t)sm_count() * 8;
+            B2_TRY(launch(sk_swiglu_kernel, dim3((unsigned)blocks), dim3(256), 0, s, true, g, u, B, I, m->act));
+        }
+        M_TRY(sk_proj(m, m->act, B, w.wd, H, nullptr, 0, I, m->bws_a, &d));
+        M_TRY(add_and_norm(m, d, B, l + 1 < c.num_layers ? m->layers[l + 1].ln1 : m->final_norm));
     }
     M_TRY(lm_head_rows(m, B));
     if (m->tp > 1) {
         if (nccl().AllReduce(m->argmax, m->argmax, (size_t)B, ncclUint64, ncclMax, m->comm, s) != ncclSuccess)
             return B2_ERR_NCCL;
     }
-    B2_TRY(launch(step_end_kernel, dim3(1), dim3(end_threads(B)), 0, s, false, (const unsigned long long*)m->argmax, m->tokens,
-                  m->positions, B, m->hist_count, m->hist_cap, 0, (const unsigned long long*)nullptr,
+    B2_TRY(launch(step_end_kernel, dim3(1), dim3(end_threads(B)), 0, s, true, (const unsigned long long*)m->argmax,
+                  m->tokens, m->positions, B, m->hist_count, m->hist_cap, 0, (const unsigned long long*)nullptr,
                   (const unsigned*)nullptr, m->tp, c.max_batch, m->step_ctr, (int*)nullptr, TraceSlot{nullptr, 0}));
     return B2_OK;
 }
@@ -1357,8 +1497,13 @@ static int prefill_batched(b2_model* m, int B, int S) {
     gather_last_kernel<<<B, 256, 0, st>>>(m->pf_hidden, m->hidden, S, H);
     B2_CHECK_LAUNCH();
     B2_TRY(cudaMemsetAsync(m->argmax, 0, (size_t)B * sizeof(unsigned long long), st));
-    if (gemv_step(m, B)) M_TRY(launch_lm_head(m, B, false));
-    else M_TRY(lm_head_rows(m, B));
+    if (gemv_step(m, B)) {
+        M_TRY(launch_lm_head(m, B, false));
+    } else {
+        rmsnorm_rows_kernel<<<B, 256, 0, st>>>(m->hidden, m->final_norm, m->bxn, H, c.rms_norm_eps);
+        B2_CHECK_LAUNCH();
+        M_TRY(lm_head_rows(m, B));
+    }
     if (m->tp > 1) {
         if (nccl().AllReduce(m->argmax, m->argmax, (size_t)B, ncclUint64, ncclMax, m->comm, st) != ncclSuccess)
             return B2_ERR_NCCL;

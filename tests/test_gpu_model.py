@@ -248,11 +248,13 @@ def _batched_teacher_forced(cfg, seed, B, S0, n_dec, max_seq=64):
     m.close()
 
 
-def test_batched_tensor_core_step_matches_oracle(cuda):
-    """B = 12 > the GEMV step's batch limit: every projection is a split-K
-    tcgen05 GEMM with M = B, partial slabs reduced with bias / RoPE / SwiGLU /
-    residual, lm_head GEMM + row argmax."""
-    _batched_teacher_forced(SMALL, 404, B=12, S0=8, n_dec=4)
+@pytest.mark.parametrize("B", [12, 40, 130])
+def test_batched_tensor_core_step_matches_oracle(cuda, B):
+    """B > the GEMV step's batch limit: every projection is a skinny
+    tcgen05 weight stream (batch on the MMA's N side: 32, 64 or 256 columns
+    for these B), partial slabs summed by the fused consumers (q|k|v + RoPE +
+    KV append, residual + RMSNorm, SwiGLU, logits + argmax)."""
+    _batched_teacher_forced(SMALL, 404 + B, B=B, S0=8, n_dec=4)
 
 
 def test_batched_tensor_core_step_llama8b_width(cuda):
