@@ -104,13 +104,18 @@ int b2_decode_gqa(const void* q, const void* k_cache, const void* v_cache, void*
 /* Split-KV GQA decode attention: one query token per sequence, q/out
  * [B, nq, D] half, seq_lens int32 [B] on the device (read by the kernel, so
  * the call is graph-capturable across steps), K/V through strided views.
- * The positions of each (sequence, kv head) are cut into splits of at least
- * one kernel iteration (16 to 64 positions), as many as split_buffer holds (about
- * split_buffer_floats / (B*nq*(D+2)); a few floats hold per-(sequence,
- * kv head) counters).  Each split writes a partial output and its (max, sum)
- * pair into split_buffer and the last split to finish merges them, in the
- * same kernel.  split_buffer may be NULL (one split per (sequence, kv head),
- * no scratch).  max_seq_len bounds seq_lens and sizes the split count.
+ * The positions of each (sequence, kv head) are cut into up to 8 splits
+ * that form one thread-block cluster; K/V tiles arrive by TMA and the splits
+ * are merged through distributed shared memory in the same kernel, so
+ * split_buffer is not used (head_dim 32/64/128/256 with 8-element-aligned
+ * view strides).  Other shapes take the global-merge kernel: splits of at
+ * least one kernel iteration (16 to 64 positions), as many as split_buffer
+ * holds (about split_buffer_floats / (B*nq*(D+2)); a few floats hold
+ * per-(sequence, kv head) counters), each writing a partial output and its
+ * (max, sum) pair that the last split to finish merges; split_buffer may be
+ * NULL there (one split per (sequence, kv head)).  max_seq_len bounds
+ * seq_lens, sizes the split count, and the views must cover max_seq_len
+ * positions of every (sequence, kv head).
  * Replaces engine::cuda::decode_gqa_split (src/cuda/kernels.h:120-133,
  * src/cuda/decode_attention_split.cu:183-214). */
 int b2_decode_gqa_split(const void* q, b2_kv_view k_view, b2_kv_view v_view, const int* seq_lens,

@@ -40,8 +40,8 @@ static PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
     return fn;
 }
 
-int make_tensor_map(CUtensorMap* map, CUtensorMapDataType type, int rank, const void* base, const uint64_t* dims,
-                    const uint64_t* strides_bytes, const uint32_t* box) {
+static int encode_map(CUtensorMap* map, CUtensorMapDataType type, int rank, const void* base, const uint64_t* dims,
+                      const uint64_t* strides_bytes, const uint32_t* box, CUtensorMapSwizzle swz) {
     auto fn = encode_fn();
     if (!fn) return B2_ERR_UNSUPPORTED;
     cuuint64_t d[5], st[4];
@@ -53,9 +53,19 @@ int make_tensor_map(CUtensorMap* map, CUtensorMapDataType type, int rank, const 
         if (i + 1 < rank) st[i] = strides_bytes[i];
     }
     const CUresult r = fn(map, type, (cuuint32_t)rank, const_cast<void*>(base), d, st, bx, es,
-                          CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
-                          CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+                          CU_TENSOR_MAP_INTERLEAVE_NONE, swz, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                          CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     return r == CUDA_SUCCESS ? B2_OK : B2_ERR_UNSUPPORTED;
+}
+
+int make_tensor_map(CUtensorMap* map, CUtensorMapDataType type, int rank, const void* base, const uint64_t* dims,
+                    const uint64_t* strides_bytes, const uint32_t* box) {
+    return encode_map(map, type, rank, base, dims, strides_bytes, box, CU_TENSOR_MAP_SWIZZLE_128B);
+}
+
+int make_tensor_map_plain(CUtensorMap* map, CUtensorMapDataType type, int rank, const void* base,
+                          const uint64_t* dims, const uint64_t* strides_bytes, const uint32_t* box) {
+    return encode_map(map, type, rank, base, dims, strides_bytes, box, CU_TENSOR_MAP_SWIZZLE_NONE);
 }
 
 }  // namespace b2

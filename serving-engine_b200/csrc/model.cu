@@ -76,6 +76,9 @@ int attn_decode_launch_step_q(const __half* q, int64_t q_sb, const __half* kbase
                               int64_t sh, int64_t ss, const int* seq_lens, __half* out, float* part, int splits,
                               int B, int nq, int nkv, int D, cudaStream_t s);
 int* wait_error_word();
+int attn_cl_launch(const __half* q, int64_t q_sb, __half* out, int64_t o_sb, const __half* k, const __half* v,
+                   int64_t sb, int64_t sh, int64_t ss, int max_len, const int* seq_lens, int len_const, int B,
+                   int nq, int nkv, int D, int early_kv, TraceSlot trace, cudaStream_t s, bool pdl);
 
 // ---------------------------------------------------------------------------
 // seeded initialisation (bit-identical to oracle/b2oracle.c ora_init_value)
@@ -1093,8 +1096,13 @@ static int launch_attn(b2_model* m, int l, int B, bool pdl) {
     (void)pdl;  // the step form always uses programmatic launch
     const int D = m->cfg.head_dim;
     __half* kbase = m->kv + (int64_t)l * m->kv_s_layer;
+    const TraceSlot tr = next_trace(m);
+    const int qd = m->nq * D;
+    const int rc = attn_cl_launch(m->q, qd, m->attn, qd, kbase, kbase + m->kv_s_kv, m->kv_s_batch, m->kv_s_head, D,
+                                  m->cfg.max_seq, m->seq_lens, 0, B, m->nq, m->nkv, D, 1, tr, m->stream, true);
+    if (rc != B2_ERR_UNSUPPORTED) return rc;
     return attn_decode_launch_step(m->q, kbase, kbase + m->kv_s_kv, m->kv_s_batch, m->kv_s_head, D, m->seq_lens,
-                                   m->attn, m->part, m->splits, B, m->nq, m->nkv, D, m->stream, next_trace(m));
+                                   m->attn, m->part, m->splits, B, m->nq, m->nkv, D, m->stream, tr);
 }
 
 static int launch_o(b2_model* m, int l, int B, bool pdl, bool xch = false) {
@@ -1266,8 +1274,16 @@ static int enqueue_step_batched(b2_model* m, int B) {
         B2_TRY(launch(sk_qkv_rope_kernel, dim3((unsigned)B, (qkv_threads + 255) / 256), dim3(256), 0, s, true,
                       qkv, B, (const __half*)w.bqkv, m->bqkv, (int64_t)R, (const float2*)m->rope, m->nq, m->nkv, D,
                       kbase, kbase + m->kv_s_kv, m->kv_s_batch, m->kv_s_head, (const int*)m->positions));
-        M_TRY(attn_decode_launch_step_q(m->bqkv, R, kbase, kbase + m->kv_s_kv, m->kv_s_batch, m->kv_s_head, D,
-                                        m->seq_lens, m->attn, m->part, m->splits, B, m->nq, m->nkv, D, s));
+        {
+            const int rc = attn_cl_launch(m->bqkv, R, m->attn, qd, kbase, kbase + m->kv_s_kv, m->kv_s_batch,
+                                          m->kv_s_head, D, c.max_seq, m->seq_lens, 0, B, m->nq, m->nkv, D, 1,
+                                          TraceSlot{nullptr, 0}, s, true);
+            if (rc == B2_ERR_UNSUPPORTED)
+                M_TRY(attn_decode_launch_step_q(m->bqkv, R, kbase, kbase + m->kv_s_kv, m->kv_s_batch, m->kv_s_head, D,
+                                                m->seq_lens, m->attn, m->part, m->splits, B, m->nq, m->nkv, D, s));
+            else
+                M_TRY(rc);
+        }
         M_TRY(sk_proj(m, m->attn, B, w.wo, H, nullptr, 0, qd, m->bws_a, &o));
         M_TRY(add_and_norm(m, o, B, w.ln2));
         if (fuse_gu) {

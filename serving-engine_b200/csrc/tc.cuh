@@ -209,6 +209,10 @@ __device__ __forceinline__ void mma_commit(uint64_t* bar) {
 // dims/strides innermost first; strides in bytes for dims 1..rank-1.
 int make_tensor_map(CUtensorMap* map, CUtensorMapDataType type, int rank, const void* base, const uint64_t* dims,
                     const uint64_t* strides_bytes, const uint32_t* box);
+// As make_tensor_map without swizzle: the box lands in shared memory as
+// dense rows (inner box extent up to 256 elements).
+int make_tensor_map_plain(CUtensorMap* map, CUtensorMapDataType type, int rank, const void* base,
+                          const uint64_t* dims, const uint64_t* strides_bytes, const uint32_t* box);
 
 // Device address of the library's bounded-wait error word on the current
 // device (0 while no wait has given up).
