@@ -456,28 +456,30 @@ def run_op(args):
         # split-KV decode attention: fp16 q [B,32,128], K/V [B,ctx,8,128] token-major, GQA 4:1
         nq, nkv, D = 32, 8, 128
         cases = []
-        for B in (1, 8, 32):
-            for ctx in (512, 4096, 32768):
-                g = torch.Generator(device="cuda").manual_seed(B * 100003 + ctx)
-                q = torch.randn(B, nq, D, generator=g, device="cuda").half()
-                k = torch.randn(B, ctx, nkv, D, generator=g, device="cuda").half()
-                v = torch.randn(B, ctx, nkv, D, generator=g, device="cuda").half()
-                lens = torch.full((B,), ctx, dtype=torch.int32, device="cuda")
-                o = torch.empty_like(q)
-                split = torch.empty(B * nq * 132 * (D + 2) + 4096, dtype=torch.float32, device="cuda")
-                kv = b2.KVView(k.data_ptr(), ctx * nkv * D, D, nkv * D, 1)
-                vv = b2.KVView(v.data_ptr(), ctx * nkv * D, D, nkv * D, 1)
+        shapes = [(B, ctx) for B in (1, 8, 32) for ctx in (512, 4096, 32768)]
+        if args.seq:  # one case: --batch B --seq ctx
+            shapes = [(args.batch, args.seq)]
+        for B, ctx in shapes:
+            g = torch.Generator(device="cuda").manual_seed(B * 100003 + ctx)
+            q = torch.randn(B, nq, D, generator=g, device="cuda").half()
+            k = torch.randn(B, ctx, nkv, D, generator=g, device="cuda").half()
+            v = torch.randn(B, ctx, nkv, D, generator=g, device="cuda").half()
+            lens = torch.full((B,), ctx, dtype=torch.int32, device="cuda")
+            o = torch.empty_like(q)
+            split = torch.empty(B * nq * 132 * (D + 2) + 4096, dtype=torch.float32, device="cuda")
+            kv = b2.KVView(k.data_ptr(), ctx * nkv * D, D, nkv * D, 1)
+            vv = b2.KVView(v.data_ptr(), ctx * nkv * D, D, nkv * D, 1)
 
-                def fn():
-                    b2.call("b2_decode_gqa_split", q.data_ptr(), kv, vv, lens.data_ptr(), o.data_ptr(), B, nq, nkv, D,
-                            ctx, split.data_ptr(), split.numel(), st)
-                for _ in range(warm):
-                    fn()
-                ms = _events_time(fn, iters, flush)
-                nbytes = 4.0 * B * ctx * nkv * D + 4.0 * B * nq * D
-                gbs = nbytes / (ms * 1e-3) / 1e9
-                cases.append({"B": B, "ctx": ctx, "us": ms * 1e3, "bytes": nbytes, "GBs": gbs, "frac": gbs / peak_hbm})
-                del q, k, v, o, split
+            def fn():
+                b2.call("b2_decode_gqa_split", q.data_ptr(), kv, vv, lens.data_ptr(), o.data_ptr(), B, nq, nkv, D,
+                        ctx, split.data_ptr(), split.numel(), st)
+            for _ in range(warm):
+                fn()
+            ms = _events_time(fn, iters, flush)
+            nbytes = 4.0 * B * ctx * nkv * D + 4.0 * B * nq * D
+            gbs = nbytes / (ms * 1e-3) / 1e9
+            cases.append({"B": B, "ctx": ctx, "us": ms * 1e3, "bytes": nbytes, "GBs": gbs, "frac": gbs / peak_hbm})
+            del q, k, v, o, split
         out.update({"metric": "split-KV decode attention achieved HBM GB/s (fp16, Hq 32 / Hkv 8, D 128)",
                     "value": max(c["GBs"] for c in cases), "unit": "GB/s", "higher_is_better": True,
                     "dtype": "f16", "config": {"workload": "BASELINE split-KV decode attention microbench",
@@ -544,7 +546,8 @@ def main():
     ap.add_argument("--trace", action="store_true", help="add a per-kernel device trace of a few steps")
     ap.add_argument("--op", default=None, choices=["attention", "flash_prefill", "gemm"],
                     help="kernel microbenchmark instead of the decode metric (1 GPU)")
-    ap.add_argument("--seq", type=int, default=0, help="--op flash_prefill: one sequence length")
+    ap.add_argument("--seq", type=int, default=0,
+                    help="--op flash_prefill: one sequence length; --op attention: one context (with --batch)")
     ap.add_argument("--exchange", default="p2p", choices=["p2p", "nccl"],
                     help="tensor-parallel decode reduction: fused peer-memory exchange or NCCL all-reduce")
     ap.add_argument("--prompt", type=int, default=PROMPT, help="prompt length (512 for the metric)")

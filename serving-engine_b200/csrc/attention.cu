@@ -454,7 +454,7 @@ static bool view_ok(const b2_kv_view& v) {
 namespace b2 {
 int attn_cl_launch(const __half* q, int64_t q_sb, __half* out, int64_t o_sb, const __half* k, const __half* v,
                    int64_t sb, int64_t sh, int64_t ss, int max_len, const int* seq_lens, int len_const, int B,
-                   int nq, int nkv, int D, int early_kv, TraceSlot trace, cudaStream_t s, bool pdl);
+                   int nq, int nkv, int D, int early_kv, int lean, TraceSlot trace, cudaStream_t s, bool pdl);
 }
 
 using namespace b2;
@@ -471,7 +471,7 @@ extern "C" int b2_decode_gqa_split(const void* q, b2_kv_view kv, b2_kv_view vv, 
     {   // cluster-merged kernel: no scratch needed (split_buffer unused)
         const int rc = attn_cl_launch((const __half*)q, (int64_t)nq * D, (__half*)out, (int64_t)nq * D,
                                       (const __half*)kv.data, (const __half*)vv.data, kv.stride_b, kv.stride_h,
-                                      kv.stride_s, max_seq_len, seq_lens, 0, B, nq, nkv, D, 0, TraceSlot{nullptr, 0},
+                                      kv.stride_s, max_seq_len, seq_lens, 0, B, nq, nkv, D, 0, 0, TraceSlot{nullptr, 0},
                                       as_stream(stream), true);
         if (rc != B2_ERR_UNSUPPORTED) return rc;
     }
@@ -510,7 +510,7 @@ extern "C" int b2_decode_gqa(const void* q, const void* kc, const void* vc, void
     {
         const int rc = attn_cl_launch((const __half*)q, (int64_t)nq * D, (__half*)out, (int64_t)nq * D,
                                       (const __half*)kc, (const __half*)vc, 0, (int64_t)max_seq * D, D, max_seq,
-                                      nullptr, total_seq_len, 1, nq, nkv, D, 0, TraceSlot{nullptr, 0},
+                                      nullptr, total_seq_len, 1, nq, nkv, D, 0, 0, TraceSlot{nullptr, 0},
                                       as_stream(stream), true);
         if (rc != B2_ERR_UNSUPPORTED) return rc;
     }

@@ -400,11 +400,22 @@ int attn_cl_splits(int batch, int nq, int nkv, int D, int max_len) {
 }
 
 // Launch: q [B] rows q_sb apart, out [B] rows o_sb apart, K/V views
-// (sb, sh, ss) covering max_len positions.  B2_ERR_UNSUPPORTED when the
-// shape does not fit (the caller then uses attn_decode_launch).
+// (sb, sh, ss) covering max_len positions.  head_dim 128 runs on the tensor
+// cores (attention_tc.cu), other head dims on this file's kernel.
+// B2_ERR_UNSUPPORTED when the shape fits neither (the caller then uses
+// attn_decode_launch).
+int attn_tc_launch(const __half* q, int64_t q_sb, __half* out, int64_t o_sb, const __half* k, const __half* v,
+                   int64_t sb, int64_t sh, int64_t ss, int max_len, const int* seq_lens, int len_const, int B,
+                   int nq, int nkv, int D, int early_kv, int lean, TraceSlot trace, cudaStream_t s, bool pdl);
+
 int attn_cl_launch(const __half* q, int64_t q_sb, __half* out, int64_t o_sb, const __half* k, const __half* v,
                    int64_t sb, int64_t sh, int64_t ss, int max_len, const int* seq_lens, int len_const, int B,
-                   int nq, int nkv, int D, int early_kv, TraceSlot trace, cudaStream_t s, bool pdl) {
+                   int nq, int nkv, int D, int early_kv, int lean, TraceSlot trace, cudaStream_t s, bool pdl) {
+    if (attn_cl_enabled()) {  // head_dim 128: the tensor-core form (attention_tc.cu)
+        const int rc = attn_tc_launch(q, q_sb, out, o_sb, k, v, sb, sh, ss, max_len, seq_lens, len_const, B, nq, nkv,
+                                      D, early_kv, lean, trace, s, pdl);
+        if (rc != B2_ERR_UNSUPPORTED) return rc;
+    }
     if (!attn_cl_supported(D, sb, sh, ss, k, v) || max_len < 1 || B < 1 || B > 65535) return B2_ERR_UNSUPPORTED;
     // Long streams (more than 8192 positions per kv head over the batch) run
     // faster on the global-merge kernel's many small CTAs: this kernel's four

@@ -78,7 +78,7 @@ int attn_decode_launch_step_q(const __half* q, int64_t q_sb, const __half* kbase
 int* wait_error_word();
 int attn_cl_launch(const __half* q, int64_t q_sb, __half* out, int64_t o_sb, const __half* k, const __half* v,
                    int64_t sb, int64_t sh, int64_t ss, int max_len, const int* seq_lens, int len_const, int B,
-                   int nq, int nkv, int D, int early_kv, TraceSlot trace, cudaStream_t s, bool pdl);
+                   int nq, int nkv, int D, int early_kv, int lean, TraceSlot trace, cudaStream_t s, bool pdl);
 
 // ---------------------------------------------------------------------------
 // seeded initialisation (bit-identical to oracle/b2oracle.c ora_init_value)
@@ -1099,7 +1099,7 @@ static int launch_attn(b2_model* m, int l, int B, bool pdl) {
     const TraceSlot tr = next_trace(m);
     const int qd = m->nq * D;
     const int rc = attn_cl_launch(m->q, qd, m->attn, qd, kbase, kbase + m->kv_s_kv, m->kv_s_batch, m->kv_s_head, D,
-                                  m->cfg.max_seq, m->seq_lens, 0, B, m->nq, m->nkv, D, 1, tr, m->stream, true);
+                                  m->cfg.max_seq, m->seq_lens, 0, B, m->nq, m->nkv, D, 1, 1, tr, m->stream, true);
     if (rc != B2_ERR_UNSUPPORTED) return rc;
     return attn_decode_launch_step(m->q, kbase, kbase + m->kv_s_kv, m->kv_s_batch, m->kv_s_head, D, m->seq_lens,
                                    m->attn, m->part, m->splits, B, m->nq, m->nkv, D, m->stream, tr);
@@ -1276,7 +1276,7 @@ static int enqueue_step_batched(b2_model* m, int B) {
                       kbase, kbase + m->kv_s_kv, m->kv_s_batch, m->kv_s_head, (const int*)m->positions));
         {
             const int rc = attn_cl_launch(m->bqkv, R, m->attn, qd, kbase, kbase + m->kv_s_kv, m->kv_s_batch,
-                                          m->kv_s_head, D, c.max_seq, m->seq_lens, 0, B, m->nq, m->nkv, D, 1,
+                                          m->kv_s_head, D, c.max_seq, m->seq_lens, 0, B, m->nq, m->nkv, D, 1, 0,
                                           TraceSlot{nullptr, 0}, s, true);
             if (rc == B2_ERR_UNSUPPORTED)
                 M_TRY(attn_decode_launch_step_q(m->bqkv, R, kbase, kbase + m->kv_s_kv, m->kv_s_batch, m->kv_s_head, D,

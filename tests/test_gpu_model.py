@@ -86,6 +86,15 @@ def test_head_dim_64_and_128(cuda):
         run_teacher_forced(cfg, 5 + D, rng.integers(0, cfg.vocab, 7), rng.integers(0, cfg.vocab, 5))
 
 
+def test_decode_attention_multi_tile_splits(cuda):
+    """head_dim 128 decode with max_seq 2048 and a 1100-token context: the
+    tensor-core attention runs 8-CTA clusters whose splits hold more than one
+    128-position tile, through the 2-stage ring of the GEMV decode step."""
+    cfg = O.Config(vocab=300, hidden=1024, inter=512, layers=1, nq=8, nkv=2, head_dim=128, theta=5e5)
+    rng = np.random.default_rng(1100)
+    run_teacher_forced(cfg, 77, rng.integers(0, cfg.vocab, 1100), rng.integers(0, cfg.vocab, 4), max_seq=2048)
+
+
 def test_greedy_generation_matches_oracle(cuda):
     cfg = SMALL
     rng = np.random.default_rng(11)
