@@ -16,9 +16,9 @@
 // memory.  Per CTA (192 threads, one CTA per SM):
 //   warp 4      TMA producer: K and V tiles (128 positions x 128, 128-byte
 //               swizzle, 4-D tensor map over the cache view) into a ring of
-//               3 stages (fewer beside register-streaming GEMVs); tiles
-//               holding only rows older than the newest position go out
-//               before the programmatic-launch wait;
+//               3 stages (fewer beside register-streaming GEMVs); in the
+//               decode step all tiles go out before the programmatic-launch
+//               wait and the newest row is copied into its tile after it;
 //   warp 5      MMA issuer: S_j, then O += P_{j-1} V_{j-1};
 //   warps 0..3  thread t = position t of the tile: its S row (16 heads) from
 //               TMEM, scale and mask, per-head tile max across the 128
@@ -50,6 +50,9 @@ struct AttnTcParams {
     float scale_log2;
     int early_kv;
     int head_inner;
+    const __half* kp;  // the cache views as pointers (the newest row is copied in directly)
+    const __half* vp;
+    int64_t sb, sh, ss;
     int* err;
     TraceSlot trace;
 };
@@ -107,7 +110,8 @@ __global__ void __launch_bounds__(192, 1) attn_tc_kernel(const __grid_constant__
     uint64_t* s_full = q_ready + 1;             // [2]
     uint64_t* p_full = q_ready + 3;             // [2]
     uint64_t* o_done = q_ready + 5;             // [2]: O += P_j V_j done, on o_done[j & 1]
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(q_ready + 7);
+    uint64_t* patch_bar = q_ready + 7;          // newest row copied into its tile
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(q_ready + 8);
     __shared__ float s_red[2][4][G];
     __shared__ float s_lsum[4][G];
     __shared__ float2 s_pm[G];
@@ -133,6 +137,7 @@ __global__ void __launch_bounds__(192, 1) attn_tc_kernel(const __grid_constant__
             tc::mbar_init(&p_full[s], 128);
             tc::mbar_init(&o_done[s], 1);
         }
+        tc::mbar_init(patch_bar, 1);
         tc::fence_barrier_init();
     }
     // Q and both P^T buffers start at zero (rows past the group's heads stay zero)
@@ -168,18 +173,19 @@ __global__ void __launch_bounds__(192, 1) attn_tc_kernel(const __grid_constant__
 
     if (warp == 4) {
         // ---------------- TMA producer ----------------
+        // Decode step: every tile goes out before the programmatic-launch
+        // wait.  The newest row (position L - 1) is being written by the
+        // previous kernel, so whatever its tile brought for it is replaced,
+        // after the wait and after that tile has landed, by the row read
+        // from the cache directly; the MMA waits for that copy on patch_bar.
+        const bool patch = p.early_kv && active && end == L;
         if (lane == 0) {
-            bool waited = !p.early_kv;
             for (int i = 0; i < nt; ++i) {
                 const int s = i % kAtStages;
                 if (i >= kAtStages &&
                     !tc::mbar_wait(&kv_empty[s], (uint32_t)((i / kAtStages) - 1) & 1u, p.err, 71))
                     break;
                 const int pos0 = start + i * kAtP;
-                if (!waited && pos0 + kAtP > L - 1) {  // this tile holds the newest row
-                    griddep_wait();
-                    waited = true;
-                }
                 uint8_t* st = ring + (size_t)s * kAtStage;
                 tc::mbar_arrive_expect_tx(&kv_full[s], kAtStage);
 #pragma unroll
@@ -194,10 +200,28 @@ __global__ void __launch_bounds__(192, 1) attn_tc_kernel(const __grid_constant__
                 }
             }
         }
+        __syncwarp();
         griddep_wait();
+        if (patch) {
+            const int i = nt - 1, s = i % kAtStages;
+            const int row = (L - 1) - (start + i * kAtP);
+            const bool ok = __all_sync(0xffffffffu, tc::mbar_wait(&kv_full[s], (uint32_t)(i / kAtStages) & 1u, p.err, 79));
+            if (ok) {
+                const int c = lane & 15;  // 16-byte chunk of the K (lanes 0-15) or V (16-31) row
+                const __half* src = (lane < 16 ? p.kp : p.vp) + (int64_t)b * p.sb + (int64_t)kvh * p.sh +
+                                    (int64_t)(L - 1) * p.ss + c * 8;
+                uint8_t* dst = ring + (size_t)s * kAtStage + (lane < 16 ? 0u : kAtKV) + (uint32_t)(c >> 3) * kAtAtom +
+                               (uint32_t)row * 128u + ((((uint32_t)c & 7u) ^ ((uint32_t)row & 7u)) << 4);
+                *reinterpret_cast<uint4*>(dst) = __ldcg(reinterpret_cast<const uint4*>(src));
+                tc::fence_proxy_async_smem();
+            }
+            __syncwarp();
+            if (lane == 0 && ok) tc::mbar_arrive(patch_bar);
+        }
         griddep_launch_dependents();
     } else if (warp == 5) {
         // ---------------- MMA issuer ----------------
+        const bool patch = p.early_kv && active && end == L;
         if (lane == 0 && nt > 0) {
             constexpr uint32_t idS = tc::idesc_f16(128, kAtN, false, false);
             constexpr uint32_t idO = tc::idesc_f16(128, kAtN, false, false, true);
@@ -207,6 +231,7 @@ __global__ void __launch_bounds__(192, 1) attn_tc_kernel(const __grid_constant__
                 if (j < nt) {
                     const int s = j % kAtStages;
                     ok = tc::mbar_wait(&kv_full[s], (uint32_t)(j / kAtStages) & 1u, p.err, 73);
+                    if (ok && patch && j == nt - 1) ok = tc::mbar_wait(patch_bar, 0, p.err, 80);
                     if (!ok) break;
                     tc::fence_after_sync();
                     const uint32_t aK = aR + (uint32_t)s * kAtStage;
@@ -464,6 +489,11 @@ int attn_tc_launch(const __half* q, int64_t q_sb, __half* out, int64_t o_sb, con
     p.hg = (group + G - 1) / G;
     p.scale_log2 = 1.4426950408889634f / sqrtf((float)D);
     p.early_kv = early_kv;
+    p.kp = k;
+    p.vp = v;
+    p.sb = sb;
+    p.sh = sh;
+    p.ss = ss;
     p.err = err;
     p.trace = trace;
     const bool head_inner = sh < ss;
