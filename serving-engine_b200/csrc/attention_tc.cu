@@ -227,38 +227,49 @@ __global__ void __launch_bounds__(192, 1) attn_tc_kernel(const __grid_constant__
             constexpr uint32_t idO = tc::idesc_f16(128, kAtN, false, false, true);
             const uint32_t aQ = tc::smem_u32(sQ), aP = tc::smem_u32(sP), aR = tc::smem_u32(ring);
             bool ok = tc::mbar_wait(q_ready, 0, p.err, 72);
-            for (int j = 0; ok && j <= nt; ++j) {
-                if (j < nt) {
-                    const int s = j % kAtStages;
-                    ok = tc::mbar_wait(&kv_full[s], (uint32_t)(j / kAtStages) & 1u, p.err, 73);
-                    if (ok && patch && j == nt - 1) ok = tc::mbar_wait(patch_bar, 0, p.err, 80);
-                    if (!ok) break;
-                    tc::fence_after_sync();
-                    const uint32_t aK = aR + (uint32_t)s * kAtStage;
+            auto issue_s = [&](int j) -> bool {
+                const int s = j % kAtStages;
+                bool good = tc::mbar_wait(&kv_full[s], (uint32_t)(j / kAtStages) & 1u, p.err, 73);
+                if (good && patch && j == nt - 1) good = tc::mbar_wait(patch_bar, 0, p.err, 80);
+                if (!good) return false;
+                tc::fence_after_sync();
+                const uint32_t aK = aR + (uint32_t)s * kAtStage;
 #pragma unroll
-                    for (int kk = 0; kk < kAtD / 16; ++kk) {
-                        const uint32_t offk = (uint32_t)(kk >> 2) * kAtAtom + (uint32_t)(kk & 3) * 32;
-                        const uint32_t offq = (uint32_t)(kk >> 2) * kAtQAtom + (uint32_t)(kk & 3) * 32;
-                        tc::mma_f16(tmem + (uint32_t)(j & 1) * 16, tc::desc_k_sw128(aK + offk),
-                                    tc::desc_k_sw128(aQ + offq), idS, kk > 0 ? 1u : 0u);
-                    }
-                    tc::mma_commit(&s_full[j & 1]);
+                for (int kk = 0; kk < kAtD / 16; ++kk) {
+                    const uint32_t offk = (uint32_t)(kk >> 2) * kAtAtom + (uint32_t)(kk & 3) * 32;
+                    const uint32_t offq = (uint32_t)(kk >> 2) * kAtQAtom + (uint32_t)(kk & 3) * 32;
+                    tc::mma_f16(tmem + (uint32_t)(j & 1) * 16, tc::desc_k_sw128(aK + offk),
+                                tc::desc_k_sw128(aQ + offq), idS, kk > 0 ? 1u : 0u);
                 }
-                if (j > 0) {
-                    const int jj = j - 1, sv = jj % kAtStages;
-                    ok = tc::mbar_wait(&p_full[jj & 1], (uint32_t)(jj >> 1) & 1u, p.err, 74);
-                    if (!ok) break;
-                    tc::fence_after_sync();
-                    const uint32_t aV = aR + (uint32_t)sv * kAtStage + kAtKV;
-                    const uint32_t aPb = aP + (uint32_t)(jj & 1) * kAtPBytes;
+                tc::mma_commit(&s_full[j & 1]);
+                return true;
+            };
+            auto issue_pv = [&](int jj) -> bool {
+                const int sv = jj % kAtStages;
+                if (!tc::mbar_wait(&p_full[jj & 1], (uint32_t)(jj >> 1) & 1u, p.err, 74)) return false;
+                tc::fence_after_sync();
+                const uint32_t aV = aR + (uint32_t)sv * kAtStage + kAtKV;
+                const uint32_t aPb = aP + (uint32_t)(jj & 1) * kAtPBytes;
 #pragma unroll
-                    for (int kk = 0; kk < kAtP / 16; ++kk) {
-                        const uint32_t offp = (uint32_t)(kk >> 2) * kAtQAtom + (uint32_t)(kk & 3) * 32;
-                        tc::mma_f16(tmem + kAtColO, tc::desc_mn_sw128(aV + (uint32_t)kk * 2048u, kAtAtom),
-                                    tc::desc_k_sw128(aPb + offp), idO, (jj > 0 || kk > 0) ? 1u : 0u);
-                    }
-                    tc::mma_commit(&o_done[jj & 1]);
-                    tc::mma_commit(&kv_empty[sv]);
+                for (int kk = 0; kk < kAtP / 16; ++kk) {
+                    const uint32_t offp = (uint32_t)(kk >> 2) * kAtQAtom + (uint32_t)(kk & 3) * 32;
+                    tc::mma_f16(tmem + kAtColO, tc::desc_mn_sw128(aV + (uint32_t)kk * 2048u, kAtAtom),
+                                tc::desc_k_sw128(aPb + offp), idO, (jj > 0 || kk > 0) ? 1u : 0u);
+                }
+                tc::mma_commit(&o_done[jj & 1]);
+                tc::mma_commit(&kv_empty[sv]);
+                return true;
+            };
+            // S_j goes ahead of P_{j-1} V_{j-1} so that it overlaps softmax j-1;
+            // with a single stage tile j can only land after P_{j-1} V_{j-1}
+            // has released it, so there the order is reversed.
+            for (int j = 0; ok && j <= nt; ++j) {
+                if (kAtStages == 1) {
+                    if (j > 0) ok = issue_pv(j - 1);
+                    if (ok && j < nt) ok = issue_s(j);
+                } else {
+                    if (j < nt) ok = issue_s(j);
+                    if (ok && j > 0) ok = issue_pv(j - 1);
                 }
             }
         }
@@ -523,7 +534,14 @@ int attn_tc_launch(const __half* q, int64_t q_sb, __half* out, int64_t o_sb, con
     // in-flight loads need the SM's L1, and an SM configured for 210 KB of
     // shared memory keeps only ~28 KB of it: they get 2 stages (~146 KB),
     // or 1 when no split can hold more than one tile.
-    const int stages = !lean ? 3 : ((max_len + cs - 1) / cs <= kAtP ? 1 : 2);
+    // More CTAs than SMs (many sequences) at moderate context: a 1-stage
+    // ring (76 KB) lets two or three CTAs share an SM, so the grid runs as
+    // one wave instead of 1.7 waves of one CTA per SM (batch 32, ctx 512:
+    // 24.6 vs 28.7 us).  Long contexts keep the deeper ring (ctx 32K: 638
+    // vs 692 us).
+    const long ctas = (long)cs * B * nkv * p.hg;
+    const bool many = ctas > sm_count() && max_len <= 8192;
+    const int stages = many ? 1 : (!lean ? 3 : ((max_len + cs - 1) / cs <= kAtP ? 1 : 2));
     if (G == 4) {
         if (stages == 1) return launch_tc_g<4, 1>(tk, tv, p, cs, B, s, pdl);
         if (stages == 2) return launch_tc_g<4, 2>(tk, tv, p, cs, B, s, pdl);
