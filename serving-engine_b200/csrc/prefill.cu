@@ -423,6 +423,289 @@ __global__ void __launch_bounds__(FlashCfg<D, ROPE>::THREADS, 1)
     }
 }
 
+// ---------------------------------------------------------------------------
+// Two-Q-tile form (head_dim 128): one CTA computes two consecutive 128-query
+// tiles A and B of one head, so the tensor core always has the other tile's
+// work while one tile's softmax runs, and P stays in TMEM.
+//   TMEM (512 columns): tile t's S_j / P_j at 256 t (P_j, 16-bit, packed two
+//   per column, overwrites the first 64 columns of S_j once the softmax has
+//   read S_j), its O at 256 t + 128.
+//   MMA order per key tile j: PV_A,j, S_A,j+1, PV_B,j, S_B,j+1 -- each S is
+//   issued behind the PV that reads the P it overwrites, and its completion
+//   (s_full) also tells the softmax that the previous PV is done, so the O
+//   rescale and the P write need no other wait.
+//   PV_t,j = P_t,j (A operand read from TMEM) x V_j (MN-major, shared memory).
+// Warps: 0..3 softmax of tile A, 4..7 of tile B (one query row per thread),
+// 8 TMA producer (Q_A, Q_B once, K/V 2-stage rings shared by both tiles),
+// 9 MMA issuer.  Causal: tile A needs key tiles 0..2p, tile B 0..2p+1.
+// ---------------------------------------------------------------------------
+struct F2Cfg {
+    static constexpr uint32_t TILE = 128 * 128 * 2;  // a Q, K or V tile (D = 128)
+    static constexpr uint32_t ATOM = 128 * 128;
+    static constexpr uint32_t OFF_Q = 0;             // 2 tiles
+    static constexpr uint32_t OFF_K = 2 * TILE;      // 2 stages
+    static constexpr uint32_t OFF_V = 4 * TILE;      // 2 stages
+    static constexpr uint32_t OFF_BAR = 6 * TILE;
+    static constexpr size_t SMEM = OFF_BAR + 256 + 1024;
+    static constexpr int THREADS = 320;
+};
+
+template <bool BF16, bool ROPE>
+__global__ void __launch_bounds__(F2Cfg::THREADS, 1)
+    flash2_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
+                     const __grid_constant__ CUtensorMap tmV, void* __restrict__ out, int64_t ldo, int S, int nq,
+                     int nkv, float scale_log2, float rope_theta, int pos0, int* err) {
+    constexpr int D = 128;
+    constexpr uint32_t TILE = F2Cfg::TILE, ATOM = F2Cfg::ATOM;
+    extern __shared__ uint8_t smem_raw[];
+    __shared__ float s_invf[64];
+    uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint8_t* sQ = sm + F2Cfg::OFF_Q;
+    uint8_t* sK = sm + F2Cfg::OFF_K;
+    uint8_t* sV = sm + F2Cfg::OFF_V;
+    uint64_t* bar = reinterpret_cast<uint64_t*>(sm + F2Cfg::OFF_BAR);
+    uint64_t* q_full = bar + 0;
+    uint64_t* q_ready = bar + 1;
+    uint64_t* k_full = bar + 2;    // [2]
+    uint64_t* k_empty = bar + 4;   // [2]
+    uint64_t* v_full = bar + 6;    // [2]
+    uint64_t* v_empty = bar + 8;   // [2]
+    uint64_t* s_full = bar + 10;   // [tile]
+    uint64_t* p_full = bar + 12;   // [tile]
+    uint64_t* o_done = bar + 14;   // [tile]
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bar + 16);
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int pt = (int)gridDim.x - 1 - (int)blockIdx.x;  // heaviest pairs first
+    const int h = blockIdx.y, b = blockIdx.z;
+    const int kvh = h / (nq / nkv);
+    const int q0 = pt * 256;
+    const bool hasB = q0 + 128 < S;
+    const int ntA = 2 * pt + 1;
+    const int ntB = hasB ? 2 * pt + 2 : 0;
+    const int nt = hasB ? ntB : ntA;
+
+    if (threadIdx.x == 0) {
+        tc::mbar_init(q_full, 1);
+        tc::mbar_init(q_ready, 256);
+        for (int s = 0; s < 2; ++s) {
+            tc::mbar_init(&k_full[s], 1);
+            tc::mbar_init(&k_empty[s], 1);
+            tc::mbar_init(&v_full[s], 1);
+            tc::mbar_init(&v_empty[s], 1);
+            tc::mbar_init(&s_full[s], 1);
+            tc::mbar_init(&p_full[s], 128);
+            tc::mbar_init(&o_done[s], 1);
+        }
+        tc::fence_barrier_init();
+    }
+    if (ROPE && threadIdx.x < D / 2) s_invf[threadIdx.x] = 1.0f / powf(rope_theta, (float)(2 * threadIdx.x) / (float)D);
+    if (warp == 0) tc::tmem_alloc(tmem_slot, 512);
+    tc::fence_before_sync();
+    __syncthreads();
+    tc::fence_after_sync();
+    const uint32_t tmem = *tmem_slot;
+
+    griddep_wait();
+    griddep_launch_dependents();
+
+    if (warp == 8) {
+        // ---------------- TMA producer ----------------
+        if (lane == 0) {
+            tc::mbar_arrive_expect_tx(q_full, 2 * TILE);
+#pragma unroll
+            for (int t = 0; t < 2; ++t)
+#pragma unroll
+                for (int a = 0; a < 2; ++a)
+                    tc::tma_load_4d(sQ + t * TILE + a * ATOM, &tmQ, q_full, a * 64, h, q0 + t * 128, b);
+            for (int j = 0; j < nt; ++j) {
+                const int s = j & 1;
+                const uint32_t u = (uint32_t)j >> 1;
+                if (j >= 2 && !tc::mbar_wait(&k_empty[s], (u - 1) & 1u, err, 31)) break;
+                tc::mbar_arrive_expect_tx(&k_full[s], TILE);
+#pragma unroll
+                for (int a = 0; a < 2; ++a)
+                    tc::tma_load_4d(sK + s * TILE + a * ATOM, &tmK, &k_full[s], a * 64, kvh, j * 128, b);
+                if (j >= 2 && !tc::mbar_wait(&v_empty[s], (u - 1) & 1u, err, 32)) break;
+                tc::mbar_arrive_expect_tx(&v_full[s], TILE);
+#pragma unroll
+                for (int a = 0; a < 2; ++a)
+                    tc::tma_load_4d(sV + s * TILE + a * ATOM, &tmV, &v_full[s], a * 64, kvh, j * 128, b);
+            }
+        }
+    } else if (warp == 9) {
+        // ---------------- MMA issuer ----------------
+        if (lane == 0) {
+            constexpr uint32_t idS = tc::idesc_f16(128, 128, BF16, false);
+            constexpr uint32_t idO = tc::idesc_f16(128, D, BF16, true);
+            const uint32_t aQ = tc::smem_u32(sQ), aK = tc::smem_u32(sK), aV = tc::smem_u32(sV);
+            auto issue_s = [&](int t, int j) {
+                const uint32_t kb = aK + (uint32_t)(j & 1) * TILE, qb = aQ + (uint32_t)t * TILE;
+#pragma unroll
+                for (int kk = 0; kk < D / 16; ++kk) {
+                    const uint32_t off = (uint32_t)(kk >> 2) * ATOM + (uint32_t)(kk & 3) * 32;
+                    tc::mma_f16(tmem + (uint32_t)t * 256, tc::desc_k_sw128(qb + off), tc::desc_k_sw128(kb + off), idS,
+                                kk > 0 ? 1u : 0u);
+                }
+                tc::mma_commit(&s_full[t]);
+            };
+            auto issue_pv = [&](int t, int j) {
+                const uint32_t vb = aV + (uint32_t)(j & 1) * TILE;
+#pragma unroll
+                for (int kk = 0; kk < 8; ++kk)
+                    tc::mma_f16_ts(tmem + (uint32_t)t * 256 + 128, tmem + (uint32_t)t * 256 + (uint32_t)kk * 8,
+                                   tc::desc_mn_sw128(vb + (uint32_t)kk * 2048u, ATOM), idO, (j > 0 || kk > 0) ? 1u : 0u);
+                tc::mma_commit(&o_done[t]);
+            };
+            bool ok = tc::mbar_wait(ROPE ? q_ready : q_full, 0, err, 33) && tc::mbar_wait(&k_full[0], 0, err, 34);
+            if (ok) {
+                tc::fence_after_sync();
+                issue_s(0, 0);
+                if (hasB) issue_s(1, 0);
+                tc::mma_commit(&k_empty[0]);
+            }
+            for (int j = 0; ok && j < nt; ++j) {
+                const int s = j & 1;
+                const uint32_t u = (uint32_t)j >> 1;
+                const int n1 = j + 1;
+                bool v_ok = false, k_ok = false;
+                if (j < ntA) {
+                    ok = tc::mbar_wait(&p_full[0], (uint32_t)j & 1u, err, 35) && tc::mbar_wait(&v_full[s], u & 1u, err, 36);
+                    if (!ok) break;
+                    v_ok = true;
+                    tc::fence_after_sync();
+                    issue_pv(0, j);
+                    if (n1 < ntA) {
+                        ok = tc::mbar_wait(&k_full[n1 & 1], (uint32_t)(n1 >> 1) & 1u, err, 37);
+                        if (!ok) break;
+                        k_ok = true;
+                        tc::fence_after_sync();
+                        issue_s(0, n1);
+                    }
+                }
+                if (hasB) {
+                    ok = tc::mbar_wait(&p_full[1], (uint32_t)j & 1u, err, 38) &&
+                         (v_ok || tc::mbar_wait(&v_full[s], u & 1u, err, 39));
+                    if (!ok) break;
+                    tc::fence_after_sync();
+                    issue_pv(1, j);
+                    if (n1 < ntB) {
+                        if (!k_ok) ok = tc::mbar_wait(&k_full[n1 & 1], (uint32_t)(n1 >> 1) & 1u, err, 40);
+                        if (!ok) break;
+                        tc::fence_after_sync();
+                        issue_s(1, n1);
+                    }
+                }
+                tc::mma_commit(&v_empty[s]);
+                if (n1 < nt) tc::mma_commit(&k_empty[n1 & 1]);
+            }
+        }
+    } else {
+        // ---------------- softmax and output: tile t, one query row per thread ----------------
+        const int t = warp >> 2, rq = warp & 3;
+        const int r = rq * 32 + lane;
+        const int qrow0 = q0 + t * 128;
+        const int qpos = qrow0 + r;
+        const uint32_t lane_base = (uint32_t)(rq * 32) << 16;
+        const uint32_t tS = tmem + (uint32_t)t * 256, tO = tS + 128;
+        const int ntt = t == 0 ? ntA : ntB;
+        float m = -1e30f, l = 0.f;
+        bool ok = true;
+        if constexpr (ROPE) {
+            ok = __all_sync(0xffffffffu, tc::mbar_wait(q_full, 0, err, 41));
+            if (ok && ntt > 0) rope_row<D, BF16>(sQ + t * TILE, r, pos0 + qpos, s_invf);
+            tc::fence_proxy_async_smem();
+            tc::mbar_arrive(q_ready);
+        }
+        for (int j = 0; ok && j < ntt; ++j) {
+            ok = __all_sync(0xffffffffu, tc::mbar_wait(&s_full[t], (uint32_t)j & 1u, err, 42));
+            if (!ok) break;
+            tc::fence_after_sync();
+            uint32_t v[128];
+#pragma unroll
+            for (int c = 0; c < 4; ++c)
+                tc::tmem_ld32(tS + lane_base + 32 * c, *reinterpret_cast<uint32_t(*)[32]>(&v[32 * c]));
+            tc::tmem_wait_ld();
+            const int kbase = j * 128;
+            if (kbase + 127 > qrow0 || kbase + 128 > S) {  // diagonal or ragged tile (warp-uniform)
+#pragma unroll
+                for (int e = 0; e < 128; ++e)
+                    if (kbase + e > qpos || kbase + e >= S) v[e] = 0xff800000u;  // -inf
+            }
+            float mx4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
+#pragma unroll
+            for (int e = 0; e < 128; ++e) mx4[e & 3] = fmaxf(mx4[e & 3], __uint_as_float(v[e]));
+            const float mx = fmaxf(fmaxf(mx4[0], mx4[1]), fmaxf(mx4[2], mx4[3])) * scale_log2;
+            const float m_new = fmaxf(m, mx);
+            const bool resc = m_new > m + 8.f;
+            const float m_use = resc ? m_new : m;
+            const float alpha = fast_exp2(m - m_use);
+            if (j > 0 && __any_sync(0xffffffffu, resc)) {
+                // PV_{j-1} has completed (S_j, issued behind it, has)
+#pragma unroll 1
+                for (int c = 0; c < D; c += 32) {
+                    uint32_t o[32];
+                    tc::tmem_ld32(tO + lane_base + c, o);
+                    tc::tmem_wait_ld();
+#pragma unroll
+                    for (int e = 0; e < 32; ++e) o[e] = __float_as_uint(__uint_as_float(o[e]) * alpha);
+                    tc::tmem_st32(tO + lane_base + c, o);
+                }
+            }
+            m = m_use;
+            float l4[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+            for (int c = 0; c < 128; c += 32) {
+                uint32_t pk[16];
+#pragma unroll
+                for (int e = 0; e < 32; e += 2) {
+                    const float p0 = fast_exp2(fmaf(__uint_as_float(v[c + e]), scale_log2, -m));
+                    const float p1 = fast_exp2(fmaf(__uint_as_float(v[c + e + 1]), scale_log2, -m));
+                    l4[(e >> 1) & 3] += p0 + p1;
+                    pk[e >> 1] = pack2<BF16>(p0, p1);
+                }
+                tc::tmem_st16(tS + lane_base + (uint32_t)(c >> 1), pk);
+            }
+            l = l * alpha + ((l4[0] + l4[1]) + (l4[2] + l4[3]));
+            tc::tmem_wait_st();
+            tc::fence_before_sync();
+            tc::mbar_arrive(&p_full[t]);
+        }
+        if (ok && ntt > 0) {
+            const uint32_t jl = (uint32_t)(ntt - 1);
+            ok = __all_sync(0xffffffffu, tc::mbar_wait(&o_done[t], jl & 1u, err, 43));
+        }
+        tc::fence_after_sync();
+        const float inv_l = l > 0.f ? 1.f / l : 0.f;
+        using T = typename std::conditional<BF16, __nv_bfloat16, __half>::type;
+        T* orow = static_cast<T*>(out) + ((int64_t)b * S + qpos) * ldo + (int64_t)h * D;
+        if (ntt > 0) {
+#pragma unroll 1
+            for (int c = 0; c < D; c += 32) {
+                uint32_t vv[32];
+                tc::tmem_ld32(tO + lane_base + c, vv);
+                tc::tmem_wait_ld();
+                if (!ok || qpos >= S) continue;
+#pragma unroll
+                for (int q = 0; q < 4; ++q) {
+                    uint4 w;
+                    w.x = pack2<BF16>(__uint_as_float(vv[8 * q + 0]) * inv_l, __uint_as_float(vv[8 * q + 1]) * inv_l);
+                    w.y = pack2<BF16>(__uint_as_float(vv[8 * q + 2]) * inv_l, __uint_as_float(vv[8 * q + 3]) * inv_l);
+                    w.z = pack2<BF16>(__uint_as_float(vv[8 * q + 4]) * inv_l, __uint_as_float(vv[8 * q + 5]) * inv_l);
+                    w.w = pack2<BF16>(__uint_as_float(vv[8 * q + 6]) * inv_l, __uint_as_float(vv[8 * q + 7]) * inv_l);
+                    *reinterpret_cast<uint4*>(orow + c + 8 * q) = w;
+                }
+            }
+        }
+    }
+    tc::fence_before_sync();
+    __syncthreads();
+    if (warp == 0) {
+        tc::fence_after_sync();
+        tc::tmem_dealloc(tmem, 512);
+    }
+}
+
 // Rotated-key buffer of the RoPE form: one per device, grown on demand and
 // kept (freed at process exit).  Calls with RoPE on one device that overlap
 // in time (different streams) would share it and must not be issued.
@@ -444,6 +727,16 @@ static int rotated_key_buffer(size_t bytes, void** out) {
     }
     *out = g_rk_buf[dev];
     return B2_OK;
+}
+
+// B2_FLASH2=0 in the environment selects the one-Q-tile kernel for head_dim 128.
+static bool flash2_enabled() {
+    static int on = -1;
+    if (on < 0) {
+        const char* e = getenv("B2_FLASH2");
+        on = (e && e[0] == '0') ? 0 : 1;
+    }
+    return on == 1;
 }
 
 template <int D, bool BF16, bool ROPE>
@@ -483,10 +776,18 @@ static int launch_flash(const FlashArgs& a_in, cudaStream_t s) {
         rc = make_tensor_map(&tv, dt, 4, a.v, dims, st, box);
         if (rc != B2_OK) return rc;
     }
+    const float scale_log2 = 1.4426950408889634f / sqrtf((float)D);
+    if (D == 128 && flash2_enabled()) {
+        auto kern2 = flash2_tc_kernel<BF16, ROPE>;
+        B2_TRY(cudaFuncSetAttribute(kern2, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)F2Cfg::SMEM));
+        dim3 grid2((unsigned)((a.S + 255) / 256), (unsigned)a.nq, (unsigned)a.batch);
+        B2_TRY(launch(kern2, grid2, dim3(F2Cfg::THREADS), F2Cfg::SMEM, s, true, tq, tk, tv, a.out, a.ldo, a.S, a.nq,
+                      a.nkv, scale_log2, a.rope_theta, a.pos0, err));
+        return B2_OK;
+    }
     auto kern = flash_tc_kernel<D, BF16, ROPE>;
     B2_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)Cfg::SMEM));
     dim3 grid((unsigned)((a.S + 127) / 128), (unsigned)a.nq, (unsigned)a.batch);
-    const float scale_log2 = 1.4426950408889634f / sqrtf((float)D);
     B2_TRY(launch(kern, grid, dim3(Cfg::THREADS), Cfg::SMEM, s, true, tq, tk, tv, a.out, a.ldo, a.S, a.nq, a.nkv,
                   scale_log2, a.rope_theta, a.pos0, err));
     return B2_OK;
