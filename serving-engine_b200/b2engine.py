@@ -281,16 +281,33 @@ class Model:
         call("b2_model_prefill", self.h, a.ctypes.data, B, S, out.ctypes.data if out is not None else None)
         return out
 
-    def decode_step(self, tokens, positions, want_logits=True, want_next=False):
+    def decode_step(self, tokens, positions, want_logits=True, want_next=False, logits_out=None):
+        """One decode step through b2_model_decode_step.  logits_out: an
+        optional reusable host buffer for the fp32 logits [B, vocab] (a numpy
+        array, or a CPU torch tensor; page-locked memory, e.g. a torch tensor
+        made with pin_memory=True, is written by the copy engine directly)."""
         import numpy as np
         t = np.ascontiguousarray(np.asarray(tokens, dtype=np.int64).reshape(-1))
         p = np.ascontiguousarray(np.asarray(positions, dtype=np.int32).reshape(-1))
         B = t.size
         self._B = B
-        lg = np.empty((B, self.vocab), np.float32) if want_logits else None
+        lg_ptr = None
+        lg = None
+        if logits_out is not None:
+            if hasattr(logits_out, "data_ptr"):
+                assert logits_out.is_contiguous() and logits_out.numel() >= B * self.vocab
+                lg_ptr = logits_out.data_ptr()
+            else:
+                assert logits_out.flags["C_CONTIGUOUS"] and logits_out.size >= B * self.vocab
+                assert logits_out.dtype == np.float32
+                lg_ptr = logits_out.ctypes.data
+            lg = logits_out
+        elif want_logits:
+            lg = np.empty((B, self.vocab), np.float32)
+            lg_ptr = lg.ctypes.data
         nx = np.empty(B, np.int64) if want_next else None
-        call("b2_model_decode_step", self.h, t.ctypes.data, p.ctypes.data, B,
-             lg.ctypes.data if lg is not None else None, nx.ctypes.data if nx is not None else None)
+        call("b2_model_decode_step", self.h, t.ctypes.data, p.ctypes.data, B, lg_ptr,
+             nx.ctypes.data if nx is not None else None)
         return lg, nx
 
     def generate_greedy(self, steps: int, fetch=True):

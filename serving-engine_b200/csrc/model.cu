@@ -1386,9 +1386,26 @@ extern "C" int b2_model_reset(b2_model* m) {
     return B2_OK;
 }
 
+// true when `p` is page-locked host memory (cudaMallocHost / cudaHostRegister),
+// which the copy engine can write directly
+static bool host_pinned(const void* p) {
+    cudaPointerAttributes a;
+    if (cudaPointerGetAttributes(&a, p) != cudaSuccess) {
+        cudaGetLastError();
+        return false;
+    }
+    return a.type == cudaMemoryTypeHost;
+}
+
 static int copy_logits_out(b2_model* m, int B, float* host_logits) {
     const int V = m->cfg.vocab_size;
     if (m->tp == 1) {
+        if (host_pinned(host_logits)) {  // the caller's buffer is page-locked: no staging copy
+            B2_TRY(cudaMemcpyAsync(host_logits, m->logits, (size_t)B * V * sizeof(float), cudaMemcpyDeviceToHost,
+                                   m->stream));
+            B2_TRY(cudaStreamSynchronize(m->stream));
+            return B2_OK;
+        }
         B2_TRY(cudaMemcpyAsync(m->h_logits, m->logits, (size_t)B * V * sizeof(float), cudaMemcpyDeviceToHost, m->stream));
         B2_TRY(cudaStreamSynchronize(m->stream));
         memcpy(host_logits, m->h_logits, (size_t)B * V * sizeof(float));

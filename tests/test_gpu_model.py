@@ -95,6 +95,22 @@ def test_decode_attention_multi_tile_splits(cuda):
     run_teacher_forced(cfg, 77, rng.integers(0, cfg.vocab, 1100), rng.integers(0, cfg.vocab, 4), max_seq=2048)
 
 
+def test_decode_step_into_pinned_buffer(cuda):
+    """b2_model_decode_step writing logits straight into a caller's
+    page-locked buffer gives the same bytes as the staged copy into pageable
+    memory (the same token at the same position is recomputed)."""
+    import torch
+    rng = np.random.default_rng(21)
+    prompt = rng.integers(0, SMALL.vocab, 9)
+    m = make_model(SMALL, 321, max_seq=64)
+    m.prefill(prompt[None, :])
+    lg_a, nx_a = m.decode_step([5], [9], want_next=True)
+    buf = torch.empty((1, SMALL.vocab), dtype=torch.float32, pin_memory=True)
+    lg_b, nx_b = m.decode_step([5], [9], want_next=True, logits_out=buf)
+    assert np.array_equal(lg_a, buf.numpy()) and np.array_equal(nx_a, nx_b)
+    m.close()
+
+
 def test_greedy_generation_matches_oracle(cuda):
     cfg = SMALL
     rng = np.random.default_rng(11)
