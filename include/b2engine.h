@@ -295,8 +295,11 @@ int b2_model_prefill(b2_model* m, const int64_t* host_ids, int batch, int seq_le
 
 /* One decode step for `batch` sequences: host tokens [batch] at host
  * positions [batch]; appends K/V and produces logits.  host_logits
- * ([batch, vocab] fp32) and/or host_next (greedy ids [batch]) may be NULL.
- * Synchronises.  The step runs as a captured CUDA graph after its first call. */
+ * ([batch, vocab] fp32) and/or host_next (greedy ids [batch]) may be NULL;
+ * page-locked host_logits (cudaMallocHost / cudaHostRegister memory) is
+ * written by the copy engine directly, pageable memory through a staging
+ * buffer.  Synchronises.  The step runs as a captured CUDA graph after its
+ * first call. */
 int b2_model_decode_step(b2_model* m, const int64_t* host_tokens, const int* host_positions, int batch,
                          float* host_logits, int64_t* host_next);
 
