@@ -16,10 +16,15 @@ the 126 MB L2, so no flush is needed.
            every step
   roofline the dominant kernel (gate/up GEMV with SwiGLU epilogue) timed on its
            launch stream, algorithmic bytes / avg launch time vs measured HBM peak
-  cpu_baseline  the reference's own src/cpu forward (oracle/_ref) on the host
+  cpu_baseline  the reference's CPU forward (src/model/forward_cpu.cpp, no KV
+           cache: a decode token recomputes every position) on the host's
+           cores, one decoder layer at the bench's context as the sample
 
-N > 1 runs Megatron tensor parallelism over NCCL (one process per GPU under
-torchrun); `--impl reference` times the reference's CPU path instead.
+N > 1 runs Megatron tensor parallelism (one process per GPU under torchrun),
+the decode-step reductions over NVLink peer memory (or NCCL with --exchange
+nccl); before the timed region a 2-layer sharded model is checked against the
+same model unsharded ("tp_parity").  `--impl reference` times the reference's
+CPU path instead.
 """
 import argparse
 import datetime as dt
@@ -147,81 +152,94 @@ class ClockSampler:
 # CPU: the reference's src/cpu path
 # ---------------------------------------------------------------------------
 
-def _cpu_models():
-    """A 1-layer Llama-3-8B-width model on the reference's forward_cpu (tied
-    lm_head: the reference always ties it) and the reference's lm_head matmul
-    alone (the 0-layer part), or the oracle port when oracle/_ref is absent."""
-    import numpy as np
-    import oracle as O
-    cfg1 = O.Config(**{**LLAMA8B, "layers": 1}, tied=True)
-    W = O.seeded_weights(cfg1, SEED_W)
-    x = np.ones((1, cfg1.hidden), np.float32)
-    if O.ref_lib() is not None:
-        m1 = O.RefModel(cfg1, W)
-        run1 = lambda ids: m1.forward(ids)  # noqa: E731
-        run0 = lambda ids: O.matmul_transB(x, W["embed"], ref=True)  # noqa: E731
-        kind = "reference"
-    else:
-        O.set_threads(1)
-        run1 = lambda ids: O.forward(cfg1, W, ids, logit_row0=len(ids))  # noqa: E731
-        run0 = lambda ids: O.matmul_transB(x, W["embed"])  # noqa: E731
-        kind = "port"
-    return run1, run0, kind, np.array([7], np.int64), W
+class RefLayerSample:
+    """The reference's CPU decode at this bench's widths, as a bounded sample.
+
+    The reference's CPU path (src/model/forward_cpu.cpp:58-174) has no KV
+    cache: to decode the token after a context of c tokens it recomputes the
+    whole forward over c + 1 positions.  One sample is one of its L decoder
+    layers over those c + 1 positions (embedding, the layer, final norm) on
+    all host threads, through the oracle port (oracle/b2oracle.c, pinned
+    bit-exact to the reference's own build by tests/test_oracle.py and
+    split across threads by output row only, so every value is the
+    reference's).  The lm_head is timed once for the LAST position only
+    (the reference computes all c + 1 rows of logits): a decode token then
+    costs L x layer + head, which flatters the reference."""
+
+    def __init__(self, c, ctx1):
+        import numpy as np
+        import oracle as O
+        self.threads = os.cpu_count() or 1
+        O.set_threads(self.threads)
+        self.O, self.L, self.ctx1 = O, c["layers"], ctx1
+        cfg1 = O.Config(**{**c, "layers": 1}, tied=True)
+        self.cfg1 = cfg1
+        self.W = O.seeded_weights(cfg1, SEED_W)
+        self.ids = np.random.default_rng(SEED_P).integers(0, cfg1.vocab, ctx1).astype(np.int64)
+        self.row = np.ones((1, cfg1.hidden), np.float32)
+        self.kind = "port"
+
+    def layer(self):
+        """Seconds for one decoder layer of the recompute over ctx1 positions."""
+        a = time.perf_counter()
+        self.O.forward(self.cfg1, self.W, self.ids, logit_row0=self.ctx1)
+        return time.perf_counter() - a
+
+    def head(self):
+        """Seconds for the lm_head of one position."""
+        a = time.perf_counter()
+        self.O.matmul_transB(self.row, self.W["embed"])
+        return time.perf_counter() - a
+
+    def describe(self):
+        return (f"one decoder layer of the reference CPU forward (no KV cache: full recompute) over the "
+                f"{self.ctx1} positions a decode token at context {self.ctx1 - 1} recomputes, "
+                f"{self.cfg1.hidden}-wide, on {self.threads} host threads (oracle port, bit-identical to the "
+                f"reference, split by output row); tok/s = 1 / ({self.L} x layer + lm_head of the last position "
+                f"only: the reference computes all {self.ctx1} logit rows, so this flatters it)")
 
 
-CPU_SAMPLE = ("one decode step at Llama-3-8B widths through the reference forward_cpu on a 1-token sequence: "
-              "t1 = 1-layer forward (embedding, 1 decoder layer, final norm, 128256x4096 lm_head), "
-              "t0 = the reference lm_head matmul alone, step time = t0 + 32*(t1 - t0); the reference CPU path "
-              "has no KV cache and recomputes all c+1 positions at context c, so this is an upper bound on "
-              "its decode rate")
-
-
-def cpu_baseline_single():
-    run1, run0, kind, ids, keep = _cpu_models()
-    t1s, t0s = [], []
-    for _ in range(3):
-        a = time.perf_counter(); run1(ids); t1s.append(time.perf_counter() - a)
-        a = time.perf_counter(); run0(ids); t0s.append(time.perf_counter() - a)
-    t1, t0 = statistics.median(t1s), statistics.median(t0s)
-    step = t0 + LLAMA8B["layers"] * max(t1 - t0, 0.0)
-    return {"value": 1.0 / step, "unit": "tok/s", "cores": 1, "kind": kind, "sample": CPU_SAMPLE,
-            "step_s": step, "layer_s": t1 - t0, "head_s": t0}
+def cpu_baseline_single(c, ctx1):
+    """cpu_baseline of the GPU arm: two layer samples and one lm_head sample."""
+    smp = RefLayerSample(c, ctx1)
+    lay = min(smp.layer() for _ in range(2))
+    head = smp.head()
+    step = smp.L * lay + head
+    return {"value": 1.0 / step, "unit": "tok/s", "cores": smp.threads, "kind": smp.kind,
+            "sample": smp.describe(), "layer_s": lay, "head_s": head, "token_s": step}
 
 
 def run_reference(args, rank, world):
-    """--impl reference: the reference's CPU implementation on all host threads
-    (independent sequences, one per thread, sharing the read-only weights)."""
+    """--impl reference: the reference's CPU decode at the bench's model and
+    context.  Each warm-up and timed step runs one layer sample (all host
+    threads); ms_per_step is that sample's time, tok/s counts the model's L
+    layers at the timed per-layer cost plus the last row's lm_head."""
     if rank != 0:
         return
-    threads = os.cpu_count() or 1
-    run1, run0, kind, ids, keep = _cpu_models()
-
-    def parallel(fn):
-        ts = [threading.Thread(target=fn, args=(ids,)) for _ in range(threads)]
-        a = time.perf_counter()
-        for t in ts:
-            t.start()
-        for t in ts:
-            t.join()
-        return time.perf_counter() - a
-
-    t0 = statistics.median([parallel(run0) for _ in range(2)])  # head part, measured once
-    layer_times = []
-    for i in range(args.warmup + args.steps):
-        t1 = parallel(run1)
-        if i >= args.warmup:
-            layer_times.append(max(t1 - t0, 1e-9))
-    layer = statistics.median(layer_times)
-    step = t0 + LLAMA8B["layers"] * layer
-    value = threads / step
-    sample = (CPU_SAMPLE + f"; {threads} host threads each decode an independent sequence concurrently; "
-              f"each timed step runs the 1-layer sample on every thread")
+    c = model_cfg(args)
+    ctx1 = args.prompt + args.warmup + args.steps // 2 + 1
+    smp = RefLayerSample(c, ctx1)
+    head = min(smp.head() for _ in range(2))
+    for _ in range(args.warmup):
+        smp.layer()
+    layer_times = [smp.layer() for _ in range(args.steps)]
+    lay = statistics.mean(layer_times)
+    token_s = smp.L * lay + head
+    value = 1.0 / token_s
+    sample = smp.describe() + f"; each of the {args.steps} timed steps runs one layer sample"
+    cfg = config_dict(args, world)
+    cfg["workload"] = (f"{args.model}-shaped bs1 decode at context {ctx1 - 1} on the reference's CPU path: each "
+                       f"step times one of its {smp.L} decoder layers over the {ctx1}-position recompute "
+                       f"(ms_per_step); tok/s = 1 / ({smp.L} x the mean layer time + one lm_head row)")
+    cfg["global_batch"] = 1
     out = {"impl": "reference", "metric": METRIC, "value": value, "unit": "tok/s", "n_gpus": world,
-           "steps": args.steps, "warmup": args.warmup, "ms_per_step": step * 1e3, "higher_is_better": True,
-           "scaling": "strong", "vs_baseline": None, "dtype": "f32",
-           "data": "synthetic: seeded random-init weights ~N(0,0.02) rounded to fp16, 1-token prompt",
-           "config": config_dict(args, world),
-           "cpu_baseline": {"value": value, "unit": "tok/s", "cores": threads, "kind": kind, "sample": sample},
+           "steps": args.steps, "warmup": args.warmup, "ms_per_step": lay * 1e3,
+           "ms_per_token": token_s * 1e3, "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+           "dtype": "f32", "data": "synthetic: seeded random-init weights ~N(0,0.02) rounded to fp16, uniform "
+                                   "random prompt ids",
+           "config": cfg,
+           "cpu_baseline": {"value": value, "unit": "tok/s", "cores": smp.threads, "kind": smp.kind,
+                            "sample": sample, "layer_s": lay, "head_s": head},
            "e2e": {"value": value, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(out), flush=True)
 
@@ -244,6 +262,75 @@ def config_dict(args, world):
 # GPU arm
 # ---------------------------------------------------------------------------
 
+def tp_parity(args, rank, world):
+    """Sharded-path correctness for N > 1, checked before the timed region.
+
+    A 2-layer model at the bench's widths runs tensor-parallel over the N
+    ranks (same exchange as the timed run): prefill of a 16-token prompt, 9
+    greedy tokens from the device loop, then the same positions teacher-forced
+    through b2_model_decode_step with the logits gathered from every rank.
+    Rank 0 runs the identical model unsharded (tp = 1) on its own GPU and
+    compares: logits max-abs <= 2e-2 and cosine >= 0.9999 at every position,
+    and every sharded greedy id equal to the unsharded argmax unless that row's
+    top-1 / top-2 margin is below 0.05.  The unsharded model is the one the
+    -m gpu tests check against the reference's CPU forward at these widths."""
+    import numpy as np
+    import torch.distributed as dist
+
+    import b2engine as b2
+    c = model_cfg(args)
+    S0, n, L2, seed = 16, 9, 2, SEED_W + 1
+
+    def build(r, t, nid):
+        m = b2.Model(c["vocab"], c["hidden"], c["inter"], L2, c["nq"], c["nkv"], c["head_dim"], eps=c["eps"],
+                     theta=c["theta"], tied=False, max_batch=1, max_seq=64, tp_rank=r, tp_size=t, nccl_id=nid)
+        m.init_random(seed, 0.02)
+        return m
+
+    obj = [b2.nccl_unique_id() if rank == 0 else None]
+    dist.broadcast_object_list(obj, src=0)
+    ms = build(rank, world, obj[0])
+    if args.exchange == "p2p":
+        handles = [None] * world
+        dist.all_gather_object(handles, ms.p2p_handle())
+        ms.p2p_open(handles)
+    prompt = np.random.default_rng(SEED_P + 1).integers(0, c["vocab"], (1, S0))
+    lg_s = [ms.prefill(prompt)[0].copy()]
+    gen = ms.generate_greedy(n)[:, 0].copy()
+    ms.reset()
+    ms.prefill(prompt, want_logits=False)
+    for i in range(n - 1):
+        lg, _ = ms.decode_step([gen[i]], [S0 + i])
+        lg_s.append(lg[0].copy())
+    ms.close()
+    res = None
+    if rank == 0:
+        mu = build(0, 1, None)
+        lg_u = [mu.prefill(prompt)[0].copy()]
+        for i in range(n - 1):
+            lg, _ = mu.decode_step([gen[i]], [S0 + i])
+            lg_u.append(lg[0].copy())
+        mu.close()
+        max_abs, cos_min, greedy_ok, ties = 0.0, 1.0, True, 0
+        for i in range(n):
+            a, b = np.asarray(lg_s[i], np.float64), np.asarray(lg_u[i], np.float64)
+            max_abs = max(max_abs, float(np.max(np.abs(a - b))))
+            cos_min = min(cos_min, float(a @ b / (np.linalg.norm(a) * np.linalg.norm(b) + 1e-30)))
+            if int(gen[i]) != int(np.argmax(b)):
+                srt = np.sort(b)[::-1]
+                if srt[0] - srt[1] < 0.05:
+                    ties += 1
+                else:
+                    greedy_ok = False
+        ok = max_abs <= 2e-2 and cos_min >= 0.9999 and greedy_ok
+        res = {"ok": ok, "max_abs": max_abs, "cos_min": cos_min, "greedy_ok": greedy_ok, "near_tie_flips": ties,
+               "greedy_tokens": n, "positions": n, "layers": L2, "tp": world, "exchange": args.exchange,
+               "reference": "the same seeded 2-layer model unsharded (tp=1) on rank 0's GPU"}
+        log(f"[rank 0] tp parity: {res}")
+    dist.barrier()
+    return res
+
+
 def run_b2(args, rank, world, local):
     import numpy as np
     import torch
@@ -253,6 +340,7 @@ def run_b2(args, rank, world, local):
 
     torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
+    parity = tp_parity(args, rank, world) if world > 1 and not args.no_tp_parity else None
     nccl_id = None
     if world > 1:
         obj = [b2.nccl_unique_id() if rank == 0 else None]
@@ -401,9 +489,11 @@ def run_b2(args, rank, world, local):
         }
         if trace:
             out["trace"] = trace
+        if parity is not None:
+            out["tp_parity"] = parity
         if world == 1 and not args.no_cpu_baseline and args.model == "llama3-8b":
             try:
-                out["cpu_baseline"] = cpu_baseline_single()
+                out["cpu_baseline"] = cpu_baseline_single(c, ctx_mid + 1)
             except Exception as ex:  # reported, never fatal
                 out["cpu_baseline"] = {"value": None, "error": str(ex)[:200]}
         print(json.dumps(out), flush=True)
@@ -545,6 +635,8 @@ def main():
     ap.add_argument("--batch", type=int, default=1)
     ap.add_argument("--impl", default="b2", choices=["b2", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-tp-parity", action="store_true",
+                    help="skip the sharded-vs-unsharded check run before the timed region at N > 1")
     ap.add_argument("--trace", action="store_true", help="add a per-kernel device trace of a few steps")
     ap.add_argument("--op", default=None, choices=["attention", "flash_prefill", "gemm"],
                     help="kernel microbenchmark instead of the decode metric (1 GPU)")

@@ -127,16 +127,20 @@ int b2_decode_gqa_split(const void* q, b2_kv_view k_view, b2_kv_view v_view, con
  * running inside an allocator or memory-pool callback, plugin hosts that own
  * every device byte, hot paths that must avoid allocator locks).  It has no
  * counterpart in the reference.  Same arguments and result as
- * b2_decode_gqa_split minus the scratch buffer: the partial results live in a
- * fixed 4 MiB array inside the library's device image, which every GPU that
- * loads the library keeps until the process exits.  The call allocates
- * nothing.  Limit: the partial results for the split count the shape prefers
- * must fit in 4 MiB (every head_dim <= 128 configuration does); larger
- * problems return B2_ERR_WORKSPACE.  The first call on a device looks up the
- * array's device address (with that device current); make that first call
- * before any stream capture.  All calls on one device share the array, so
- * calls that overlap on the GPU race; the arrival counters in it are cleared
- * by each call. */
+ * b2_decode_gqa_split minus the scratch buffer, and the call allocates
+ * nothing.  Shapes the cluster-merged kernels take need no scratch and run
+ * exactly as in b2_decode_gqa_split.  The others run the global-merge kernel,
+ * whose partial results live in a fixed 4 MiB array inside the library's
+ * device image (every GPU that loads the library keeps it until the process
+ * exits): the split count is the one the shape prefers, lowered until the
+ * partials fit 4 MiB (one split needs none), so the array limits the speed of
+ * very large batch x head x context problems, not which shapes run.  The
+ * first call on a device that uses the array looks up its device address
+ * (with that device current) and caches it for the life of the process: make
+ * that first call before any stream capture, and not across a
+ * cudaDeviceReset (the cached address would be stale).  All calls on one
+ * device share the array, so calls that overlap on the GPU race; the arrival
+ * counters in it are cleared by each call. */
 int b2_decode_gqa_split_noalloc(const void* q, b2_kv_view k_view, b2_kv_view v_view, const int* seq_lens,
                                 void* out, int batch_size, int num_q_heads, int num_kv_heads, int head_dim,
                                 int max_seq_len, void* stream);
@@ -296,9 +300,10 @@ int b2_model_prefill(b2_model* m, const int64_t* host_ids, int batch, int seq_le
 /* One decode step for `batch` sequences: host tokens [batch] at host
  * positions [batch]; appends K/V and produces logits.  host_logits
  * ([batch, vocab] fp32) and/or host_next (greedy ids [batch]) may be NULL;
- * page-locked host_logits (cudaMallocHost / cudaHostRegister memory) is
- * written by the copy engine directly, pageable memory through a staging
- * buffer.  Synchronises.  The step runs as a captured CUDA graph after its
+ * host_logits must hold batch * vocab floats.  When its first and last bytes
+ * are page-locked (cudaMallocHost / cudaHostRegister memory covering the
+ * whole [batch, vocab] range) the copy engine writes it directly, otherwise
+ * the logits go through a staging buffer.  Synchronises.  The step runs as a captured CUDA graph after its
  * first call. */
 int b2_model_decode_step(b2_model* m, const int64_t* host_tokens, const int* host_positions, int batch,
                          float* host_logits, int64_t* host_next);

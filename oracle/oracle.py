@@ -47,6 +47,7 @@ def lib():
         L.ora_apply_rope.argtypes = [f32p, f32p, I64, I64, I64, I64, I64, C.c_float]
         L.ora_rope_table.argtypes = [I64, I64, I64, C.c_float, f32p, f32p]
         L.ora_causal_gqa.argtypes = [f32p, f32p, f32p, f32p, I64, I64, I64, I64]
+        L.ora_causal_gqa_rows.argtypes = [f32p, f32p, f32p, f32p, I64, I64, I64, I64, I64]
         L.ora_swiglu.argtypes = [f32p, f32p, f32p, I64]
         L.ora_softmax.argtypes = [f32p, f32p, I64, I64]
         L.ora_embedding_lookup.argtypes = [i64p, f32p, f32p, I64, I64]
@@ -176,6 +177,14 @@ def causal_gqa(q, k, v, S, nq, nkv, D, ref=False):
     out = np.zeros((S, nq * D), np.float32)
     (ref_lib().ref_causal_gqa if ref else lib().ora_causal_gqa)(q, k, v, out, S, nq, nkv, D)
     return out
+
+
+def causal_gqa_rows(q, k, v, S, nq, nkv, D, q_begin):
+    """causal_gqa's output rows [q_begin, S) only (rows are independent)."""
+    q = _c(q); k = _c(k); v = _c(v)
+    out = np.zeros((S, nq * D), np.float32)
+    lib().ora_causal_gqa_rows(q, k, v, out, S, nq, nkv, D, q_begin)
+    return out[q_begin:]
 
 
 def swiglu(g, u, ref=False):

@@ -295,11 +295,17 @@ class Model:
         lg = None
         if logits_out is not None:
             if hasattr(logits_out, "data_ptr"):
-                assert logits_out.is_contiguous() and logits_out.numel() >= B * self.vocab
+                import torch
+                if logits_out.dtype != torch.float32 or logits_out.device.type != "cpu":
+                    raise ValueError("logits_out must be a float32 tensor in host memory")
+                if not logits_out.is_contiguous() or logits_out.numel() < B * self.vocab:
+                    raise ValueError(f"logits_out must be contiguous with at least {B * self.vocab} elements")
                 lg_ptr = logits_out.data_ptr()
             else:
-                assert logits_out.flags["C_CONTIGUOUS"] and logits_out.size >= B * self.vocab
-                assert logits_out.dtype == np.float32
+                if logits_out.dtype != np.float32 or not logits_out.flags["C_CONTIGUOUS"]:
+                    raise ValueError("logits_out must be a C-contiguous float32 array")
+                if logits_out.size < B * self.vocab:
+                    raise ValueError(f"logits_out must hold at least {B * self.vocab} elements")
                 lg_ptr = logits_out.ctypes.data
             lg = logits_out
         elif want_logits:

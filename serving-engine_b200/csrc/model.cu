@@ -1386,21 +1386,27 @@ extern "C" int b2_model_reset(b2_model* m) {
     return B2_OK;
 }
 
-// true when `p` is page-locked host memory (cudaMallocHost / cudaHostRegister),
-// which the copy engine can write directly
-static bool host_pinned(const void* p) {
-    cudaPointerAttributes a;
-    if (cudaPointerGetAttributes(&a, p) != cudaSuccess) {
-        cudaGetLastError();
-        return false;
+// true when the `bytes` at `p` are page-locked host memory (cudaMallocHost /
+// cudaHostRegister), which the copy engine can write directly: both the first
+// and the last byte must be, so a buffer registered only at its start goes
+// through the staging copy instead.
+static bool host_pinned(const void* p, size_t bytes) {
+    const char* ends[2] = {static_cast<const char*>(p), static_cast<const char*>(p) + (bytes ? bytes - 1 : 0)};
+    for (const char* q : ends) {
+        cudaPointerAttributes a;
+        if (cudaPointerGetAttributes(&a, q) != cudaSuccess) {
+            cudaGetLastError();
+            return false;
+        }
+        if (a.type != cudaMemoryTypeHost) return false;
     }
-    return a.type == cudaMemoryTypeHost;
+    return true;
 }
 
 static int copy_logits_out(b2_model* m, int B, float* host_logits) {
     const int V = m->cfg.vocab_size;
     if (m->tp == 1) {
-        if (host_pinned(host_logits)) {  // the caller's buffer is page-locked: no staging copy
+        if (host_pinned(host_logits, (size_t)B * V * sizeof(float))) {  // the caller's buffer is page-locked: no staging copy
             B2_TRY(cudaMemcpyAsync(host_logits, m->logits, (size_t)B * V * sizeof(float), cudaMemcpyDeviceToHost,
                                    m->stream));
             B2_TRY(cudaStreamSynchronize(m->stream));

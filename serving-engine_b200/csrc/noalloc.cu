@@ -5,9 +5,18 @@
 // re-enter the allocator), plugin hosts that own every device byte and hand
 // out no scratch, and hot paths that have to stay free of allocator locks and
 // implicit synchronisation.  b2_decode_gqa_split needs a scratch buffer for
-// its per-split partial results when it cuts a long context into several
-// splits; this file gives those callers the same kernel with its scratch
-// taken from a fixed array that lives in the library's device image.
+// its per-split partial results when its global-merge kernel cuts a long
+// context into several splits; this file gives those callers the same
+// kernels with that scratch taken from a fixed array that lives in the
+// library's device image.
+//
+// Shapes the cluster-merged kernels take (head_dim 32/64/128/256 with
+// 8-element-aligned strides; head_dim 128 on the tensor cores) need no
+// scratch at all and run exactly as b2_decode_gqa_split runs them.  The rest
+// go to the global-merge kernel with as many splits as the shape prefers,
+// capped so that the partial results fit the array: the array bounds the
+// split count (and so the speed of very large problems), never which shapes
+// run.  One split per (sequence, kv head) needs no scratch.
 //
 // The array is a file-scope __device__ object, so every GPU that loads this
 // library holds kNoAllocScratchBytes for it until the process exits, and all
@@ -28,16 +37,19 @@ bool attn_head_dim_supported(int D);
 int attn_decode_launch_model(const __half* q, const __half* kbase, const __half* vbase, int64_t sb, int64_t sh,
                              int64_t ss, const int* seq_lens, __half* out, float* part, int splits, int B, int nq,
                              int nkv, int D, cudaStream_t s, bool pdl);
+int attn_cl_launch(const __half* q, int64_t q_sb, __half* out, int64_t o_sb, const __half* k, const __half* v,
+                   int64_t sb, int64_t sh, int64_t ss, int max_len, const int* seq_lens, int len_const, int B,
+                   int nq, int nkv, int D, int early_kv, int lean, TraceSlot trace, cudaStream_t s, bool pdl);
 
-// 4 MiB: enough for the preferred split count of every configuration with
-// head_dim <= 128 at any batch size and context length.
+// 4 MiB of partial results (1,048,576 floats).
 constexpr size_t kNoAllocScratchBytes = 4u << 20;
 constexpr size_t kNoAllocScratchFloats = kNoAllocScratchBytes / sizeof(float);
 
 static __device__ __align__(256) float g_noalloc_scratch[kNoAllocScratchFloats];
 
-// Device address of g_noalloc_scratch per device, looked up once per device
-// (with that device current) on the first call made on it.
+// Device address of g_noalloc_scratch per device, looked up (with that device
+// current) by the first call on that device that needs it and cached for the
+// life of the process.
 static std::mutex g_noalloc_mu;
 static float* g_noalloc_ptr[64];
 
@@ -69,17 +81,23 @@ extern "C" int b2_decode_gqa_split_noalloc(const void* q, b2_kv_view kv, b2_kv_v
         kv.stride_b != vv.stride_b || kv.stride_h != vv.stride_h || kv.stride_s != vv.stride_s ||
         (kv.stride_b % 8) || (kv.stride_h % 8) || (kv.stride_s % 8) || !aligned16(q) || !aligned16(out))
         return B2_ERR_UNSUPPORTED;
-    // The split count this shape prefers when scratch is not a constraint;
-    // problems whose partial results for that count do not fit the fixed
-    // array are refused rather than silently run with fewer splits.
-    const int splits = attn_pick_splits(B, nq, nkv, D, max_seq_len, (size_t)-1);
-    const size_t need = attn_scratch_floats(B, nq, nkv, D, splits);
-    if (need > kNoAllocScratchFloats) return B2_ERR_WORKSPACE;
-    float* scratch = nullptr;
-    const int rc = noalloc_scratch(&scratch);
-    if (rc != B2_OK) return rc;
     cudaStream_t s = as_stream(stream);
+    {   // cluster-merged kernels: the splits meet in distributed shared memory
+        const int rc = attn_cl_launch((const __half*)q, (int64_t)nq * D, (__half*)out, (int64_t)nq * D,
+                                      (const __half*)kv.data, (const __half*)vv.data, kv.stride_b, kv.stride_h,
+                                      kv.stride_s, max_seq_len, seq_lens, 0, B, nq, nkv, D, 0, 0, TraceSlot{nullptr, 0},
+                                      s, true);
+        if (rc != B2_ERR_UNSUPPORTED) return rc;
+    }
+    // Global-merge kernel: the split count the shape prefers, lowered until
+    // its partial results fit the fixed array (fewer splits give the same
+    // result with fewer CTAs streaming each (sequence, kv head)).
+    const int splits = attn_pick_splits(B, nq, nkv, D, max_seq_len, kNoAllocScratchFloats);
+    float* scratch = nullptr;
     if (splits > 1) {
+        const int rc = noalloc_scratch(&scratch);
+        if (rc != B2_OK) return rc;
+        const size_t need = attn_scratch_floats(B, nq, nkv, D, splits);
         const size_t off = (size_t)B * nq * splits * (D + 2);
         B2_TRY(cudaMemsetAsync(scratch + off, 0, (need - off) * sizeof(int), s));
     }

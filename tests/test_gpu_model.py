@@ -9,6 +9,8 @@ tensors on the device (b2_model_init_random) and in the oracle
     top-2 margin is below 0.05 (the reference's near-tie rule, docs/GATES.md);
   * KV-cache indexing bit-exact.
 """
+import os
+
 import numpy as np
 import pytest
 
@@ -191,24 +193,40 @@ def test_kv_cache_indexing_bit_exact(cuda):
     m.close()
 
 
-def _full_width_check(cfg, seed, S0, n_dec, max_seq=128):
+def _full_width_check(cfg, seed, S0, n_dec, max_seq=128, tf_rows=4):
+    """Prefill S0 random ids, n_dec greedy tokens from the device loop, then
+    the oracle's teacher-forced recompute over prompt + generated ids:
+    every generated id equals the oracle's argmax at its position (near-tie
+    rule), and the logits of the prefill and of the first tf_rows decode
+    steps (re-run through b2_model_decode_step) match the oracle's rows."""
     rng = np.random.default_rng(seed)
     prompt = rng.integers(0, cfg.vocab, S0)
     m = make_model(cfg, seed, max_seq=max_seq)
     lg0 = m.prefill(prompt[None, :])
     gen = m.generate_greedy(n_dec)[:, 0]
+    O.set_threads(os.cpu_count() or 1)
     W = O.seeded_weights(cfg, seed)
     seq = np.concatenate([prompt, gen[:-1]]).astype(np.int64)
     ref = O.forward(cfg, W, seq, logit_row0=S0 - 1)
+    del W
     check_logits(lg0[0], ref[0], "prefill")
     check_greedy(gen, ref, "greedy")
-    # teacher-forced logits for the first generated positions
+    # teacher-forced logits for the generated positions
     m.reset()
     m.prefill(prompt[None, :], want_logits=False)
-    for i in range(min(4, n_dec - 1)):
+    worst = [0.0, 1.0]
+    for i in range(min(tf_rows, n_dec - 1)):
         lg, _ = m.decode_step([gen[i]], [S0 + i])
-        check_logits(lg[0], ref[i + 1], f"decode {i}")
+        d, cos = check_logits(lg[0], ref[i + 1], f"decode {i}")
+        worst = [max(worst[0], d), min(worst[1], cos)]
     m.close()
+    return gen, ref, worst
+
+
+def _near_ties(gen, ref):
+    """Positions where the device's greedy id differs from the oracle's argmax
+    (each one a near tie, or check_greedy would have failed)."""
+    return [i for i, t in enumerate(gen) if int(t) != int(np.argmax(ref[i]))]
 
 
 @pytest.mark.slow
@@ -219,12 +237,40 @@ def test_tinyllama_full_width_reduced_depth(cuda):
     _full_width_check(cfg, 2024, 24, 16)
 
 
+TINYLLAMA = O.Config(vocab=32000, hidden=2048, inter=5632, layers=22, nq=32, nkv=4, head_dim=64, theta=10000.0)
+
+
+@pytest.mark.slow
+def test_tinyllama_full_depth_128_prompt_128_greedy(cuda):
+    """BASELINE configs[0] end to end: the TinyLlama-1.1B-shaped decoder at
+    all 22 layers, random-init from a seed, a 128-token uniform random prompt
+    and 128 greedy steps of the device-resident decode loop, against the
+    reference's CPU forward (full recompute over the 255 positions):
+      * the 128 generated ids equal the oracle's argmax at every position
+        (near-tie rule), so the first 32 greedy tokens match;
+      * the logits of the prefill and of every one of the 127 decode steps
+        (teacher-forced through b2_model_decode_step) are within max-abs 2e-2
+        and cosine >= 0.9999 of the oracle's."""
+    gen, ref, worst = _full_width_check(TINYLLAMA, 1101, 128, 128, max_seq=512, tf_rows=127)
+    assert len(gen) == 128
+    flips = _near_ties(gen, ref)
+    assert not [i for i in flips if i < 32], f"near-tie flips in the first 32 tokens: {flips}"
+    print(f"tinyllama 22 layers: worst max-abs {worst[0]:.3g}, cos {worst[1]:.7f}, near-tie flips {flips}")
+
+
+LLAMA8B_2L = O.Config(vocab=128256, hidden=4096, inter=14336, layers=2, nq=32, nkv=8, head_dim=128,
+                      theta=500000.0)
+
+
 @pytest.mark.slow
 def test_llama8b_full_width_reduced_depth(cuda):
     """Llama-3-8B widths (H 4096, 32/8 heads, D 128, FFN 14336, vocab 128256,
-    theta 5e5) at 2 layers."""
-    cfg = O.Config(vocab=128256, hidden=4096, inter=14336, layers=2, nq=32, nkv=8, head_dim=128, theta=500000.0)
-    _full_width_check(cfg, 88, 16, 8)
+    theta 5e5) at 2 layers: 32 greedy tokens from the device loop equal the
+    oracle's argmax at each position, and the teacher-forced logits of all
+    32 positions match."""
+    gen, ref, worst = _full_width_check(LLAMA8B_2L, 88, 16, 33, tf_rows=32)
+    flips = _near_ties(gen, ref)
+    assert not [i for i in flips if i < 32], f"near-tie flips in the first 32 tokens: {flips}"
 
 
 def test_batched_prefill_matches_token_by_token(cuda):
@@ -282,8 +328,10 @@ def test_batched_tensor_core_step_matches_oracle(cuda, B):
     _batched_teacher_forced(SMALL, 404 + B, B=B, S0=8, n_dec=4)
 
 
-def test_batched_tensor_core_step_llama8b_width(cuda):
-    """Llama-3-8B widths at 2 layers, B = 4: the down projection's width
-    (14336) caps the GEMV batch tile at 2, so the tensor-core step runs."""
-    cfg = O.Config(vocab=128256, hidden=4096, inter=14336, layers=2, nq=32, nkv=8, head_dim=128, theta=500000.0)
-    _batched_teacher_forced(cfg, 405, B=4, S0=6, n_dec=3)
+@pytest.mark.parametrize("B", [4, 8, 32])
+def test_batched_tensor_core_step_llama8b_width(cuda, B):
+    """Llama-3-8B widths at 2 layers, B = 4, 8 and 32 (BASELINE's decode
+    batches): the down projection's width (14336) caps the GEMV batch tile at
+    2, so the tensor-core step runs."""
+    O.set_threads(os.cpu_count() or 1)
+    _batched_teacher_forced(LLAMA8B_2L, 405 + B, B=B, S0=6, n_dec=3)

@@ -81,6 +81,43 @@ def test_flash_prefill_bf16_rope(cuda, S, rope):
     assert float(err.max()) < 2e-2 and float(err.mean()) < 2e-3, (float(err.max()), float(err.mean()))
 
 
+@pytest.mark.slow
+def test_flash_prefill_bf16_rope_s8192_sampled(cuda):
+    """BASELINE's longest causal prefill, S = 8192 (bf16, RoPE theta 5e5 in
+    the kernel), against the oracle on two kv head groups (q heads 0-3 and
+    28-31) for the first 192 query rows (the first tiles, short causal
+    windows) and the last 256 (64 key tiles each)."""
+    import torch
+    S, nq, nkv, D, theta = 8192, 32, 8, 128, 500000.0
+    rng = np.random.default_rng(8192)
+    q = _bf16(rng.standard_normal((S, nq * D)))
+    k = _bf16(rng.standard_normal((S, nkv * D)))
+    v = _bf16(rng.standard_normal((S, nkv * D)))
+    out = torch.empty(S, nq * D, dtype=torch.bfloat16, device="cuda")
+    dq, dk, dv = q.cuda(), k.cuda(), v.cuda()
+    b2.call("b2_flash_prefill_gqa_ex", dq.data_ptr(), dk.data_ptr(), dv.data_ptr(), out.data_ptr(), S, nq, nkv, D, 1,
+            1, theta, 0, b2.stream_ptr())
+    assert b2.device_status() == 0
+    got = out.float().cpu().numpy().reshape(S, nq, D)
+    O.set_threads(os.cpu_count() or 1)
+    qf = q.float().numpy().reshape(S, nq, D)
+    kf = k.float().numpy().reshape(S, nkv, D)
+    vf = v.float().numpy().reshape(S, nkv, D)
+    head, tail = 192, 256
+    for g in (0, nkv - 1):
+        hs = slice(4 * g, 4 * g + 4)
+        qg = np.ascontiguousarray(qf[:, hs, :]).reshape(S, 4 * D)
+        kg = np.ascontiguousarray(kf[:, g, :])
+        vg = np.ascontiguousarray(vf[:, g, :])
+        qg, kg = O.apply_rope(qg, kg, S, 4, 1, D, 0, theta)
+        qg, kg = _bf16(qg).float().numpy(), _bf16(kg).float().numpy()  # rotated rows are kept in bf16
+        ref_head = O.causal_gqa(qg[:head], kg[:head], vg[:head], head, 4, 1, D)
+        ref_tail = O.causal_gqa_rows(qg, kg, vg, S, 4, 1, D, S - tail)
+        for rows, ref in ((slice(0, head), ref_head), (slice(S - tail, S), ref_tail)):
+            err = np.abs(got[rows, hs, :].reshape(ref.shape) - ref)
+            assert float(err.max()) < 2e-2 and float(err.mean()) < 2e-3, (g, rows, float(err.max()))
+
+
 def test_flash_prefill_fp16_rope_matches_separate_rope(cuda):
     """In-kernel RoPE (fp16) equals b2_apply_rope followed by the plain kernel."""
     import torch
