@@ -181,16 +181,34 @@ __global__ void __launch_bounds__(kGemvThreads, 2) gemv_vec_kernel(const GemvPar
     gemv_finish<BT, OM, kGemvThreads>(p, lane, warp, best, s_best, s_push, row0, t_end, push_epoch, push_par);
     __syncthreads();
     trace_end(p.trace);
+    // X_SUM: no CTA leaves while a cluster peer may still read its slice of h
+    if constexpr (XM == X_SUM) cluster_wait_acquire();
 }
 
 // ---------------------------------------------------------------------------
 // launch plumbing
 // ---------------------------------------------------------------------------
 
+// Thread-block cluster size of the X_SUM (exchange-consumer) GEMVs: the CTAs
+// of a cluster share the reads of the exchange words (B2_XSUM_CLUSTER
+// overrides, 1..8).
+static int xsum_cluster() {
+    static int cs = -1;
+    if (cs < 0) {
+        const char* e = getenv("B2_XSUM_CLUSTER");
+        const int v = e ? atoi(e) : 8;
+        cs = v >= 1 && v <= 8 ? v : 8;
+    }
+    return cs;
+}
+
 template <int R, int BT, int XM, int OM, int U>
 static int launch_vec(const GemvParams& p, cudaStream_t s, bool pdl) {
     auto kern = gemv_vec_kernel<R, BT, XM, OM, U>;
-    const size_t smem = (size_t)BT * p.K * sizeof(__half);
+    const int cs = XM == X_SUM ? xsum_cluster() : 1;
+    // X_SUM also keeps its slice of the residual (fp32) after x
+    const size_t smem = (size_t)BT * p.K * sizeof(__half) +
+                        (XM == X_SUM ? (size_t)BT * (((p.K >> 3) + cs - 1) / cs) * 8 * sizeof(float) : 0);
     // per-device occupancy cache, keyed on the shared-memory footprint
     static thread_local int last_dev = -1;
     static thread_local size_t last_smem = (size_t)-1;
@@ -200,22 +218,45 @@ static int launch_vec(const GemvParams& p, cudaStream_t s, bool pdl) {
     if (dev != last_dev || smem != last_smem) {
         B2_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)(smem > 0 ? smem : 1)));
         int occ = 0;
-        B2_TRY(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, kern, kGemvThreads, smem));
-        last_occ = occ > 0 ? occ : 1;
+        if (XM == X_SUM) {
+            // co-resident CTAs in whole clusters (a cluster sits in one GPC)
+            cudaLaunchConfig_t cfg = {};
+            cfg.gridDim = dim3((unsigned)(cs * sm_count()));
+            cfg.blockDim = dim3(kGemvThreads);
+            cfg.dynamicSmemBytes = smem;
+            cudaLaunchAttribute attr[1];
+            attr[0].id = cudaLaunchAttributeClusterDimension;
+            attr[0].val.clusterDim.x = (unsigned)cs;
+            attr[0].val.clusterDim.y = 1;
+            attr[0].val.clusterDim.z = 1;
+            cfg.attrs = attr;
+            cfg.numAttrs = 1;
+            int clusters = 0;
+            B2_TRY(cudaOccupancyMaxActiveClusters(&clusters, kern, &cfg));
+            occ = clusters * cs;  // CTAs device-wide
+        } else {
+            B2_TRY(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, kern, kGemvThreads, smem));
+            occ *= sm_count();
+        }
+        last_occ = occ > 0 ? occ : cs;
         last_dev = dev;
         last_smem = smem;
     }
-    const int max_warps = sm_count() * last_occ * kGemvWarps;
+    const int max_warps = last_occ * kGemvWarps;
     const int rounds = (p.tasks + max_warps - 1) / max_warps;
     const int warps = (p.tasks + rounds - 1) / rounds;
     int ctas = (warps + kGemvWarps - 1) / kGemvWarps;
+    if (cs > 1) ctas = (ctas + cs - 1) / cs * cs;
     GemvParams q = p;
     if (OM == OUT_PUSH) {
         q.rows_per_cta = kGemvWarps * rounds;
         if (q.rows_per_cta > kPushRows || (p.tasks & 7)) return B2_ERR_UNSUPPORTED;
         ctas = (p.tasks + q.rows_per_cta - 1) / q.rows_per_cta;
     }
-    B2_TRY(launch(kern, dim3(ctas), dim3(kGemvThreads), smem, s, pdl, q));
+    if (XM == X_SUM)
+        B2_TRY(launch_cluster(kern, dim3(ctas), dim3(kGemvThreads), smem, s, pdl, (unsigned)cs, q));
+    else
+        B2_TRY(launch(kern, dim3(ctas), dim3(kGemvThreads), smem, s, pdl, q));
     return B2_OK;
 }
 
