@@ -288,6 +288,17 @@ int b2_model_init_random(b2_model* m, uint64_t seed, float stddev);
 int b2_model_set_tensor(b2_model* m, const char* name, const uint16_t* host_f16, int64_t rows,
                         int64_t cols);
 
+/* b2_model_set_tensor for a bf16 checkpoint tensor (host bf16 [rows, cols],
+ * e.g. straight from a memory-mapped safetensors file): the rank's block is
+ * copied to the device and converted there to fp16 by the loader's rule
+ * (exponent rebased; values below the fp16 normal range become signed zero,
+ * values above it signed infinity; the mantissa bits carry over exactly).
+ * Synchronises.  Replaces the host-side conversion of
+ * ModelWeightsGPU::init_from_weights (src/model/forward_gpu.cu:18-28,
+ * src/loader/safetensors.cpp:307-328). */
+int b2_model_set_tensor_bf16(b2_model* m, const char* name, const uint16_t* host_bf16, int64_t rows,
+                             int64_t cols);
+
 /* Clears the KV cache positions of all sequences (sets lengths to 0). */
 int b2_model_reset(b2_model* m);
 
@@ -307,6 +318,26 @@ int b2_model_prefill(b2_model* m, const int64_t* host_ids, int batch, int seq_le
  * first call. */
 int b2_model_decode_step(b2_model* m, const int64_t* host_tokens, const int* host_positions, int batch,
                          float* host_logits, int64_t* host_next);
+
+/* Full forward over one sequence of `seq_len` host ids: fp32 logits of every
+ * position into host_logits ([seq_len, vocab]).  Runs the batched prefill
+ * (tensor-core projections and flash prefill), then the final RMSNorm and the
+ * lm_head over all positions as one tensor-core GEMM; sequence 0's KV cache
+ * holds the sequence afterwards.  Allocates its logits workspace on first use
+ * (grown as needed); synchronises; tp_size 1 only.
+ * Replaces forward_gpu (src/model/forward_gpu.h:76-84). */
+int b2_model_forward_logits(b2_model* m, const int64_t* host_ids, int seq_len, float* host_logits);
+
+/* b2_model_decode_step without synchronising: the host tokens and positions
+ * go to the device as launch parameters (the host arrays are free once the
+ * call returns), the step's graph is launched on the model's stream, and
+ * when d_logits is not NULL the fp32 logits [batch, vocab] are copied to that
+ * device buffer on the same stream (tp_size 1 only).  Order other work
+ * against it through b2_model_stream.  Replaces decode_step_gpu's
+ * d_last_logits form, which skips the host copy for an asynchronous
+ * pipeline (src/model/forward_gpu.h:98-113, forward_gpu.cu:694-707). */
+int b2_model_decode_enqueue(b2_model* m, const int64_t* host_tokens, const int* host_positions, int batch,
+                            float* d_logits);
 
 /* Device-resident greedy generation: `steps` decode steps replayed back to
  * back without host round trips, each consuming the argmax of the previous

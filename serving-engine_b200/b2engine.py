@@ -81,9 +81,12 @@ _SIGS = {
     "b2_model_p2p_open": (i32, [vp, vp]),
     "b2_model_trace_step": (i32, [vp, i32, vp, i32, C.POINTER(i32)]),
     "b2_model_set_tensor": (i32, [vp, C.c_char_p, vp, i64, i64]),
+    "b2_model_set_tensor_bf16": (i32, [vp, C.c_char_p, vp, i64, i64]),
+    "b2_model_forward_logits": (i32, [vp, vp, i32, vp]),
     "b2_model_reset": (i32, [vp]),
     "b2_model_prefill": (i32, [vp, vp, i32, i32, vp]),
     "b2_model_decode_step": (i32, [vp, vp, vp, i32, vp, vp]),
+    "b2_model_decode_enqueue": (i32, [vp, vp, vp, i32, vp]),
     "b2_model_generate_greedy": (i32, [vp, i32, vp]),
     "b2_model_sync": (i32, [vp]),
     "b2_model_stream": (vp, [vp]),
@@ -268,6 +271,24 @@ class Model:
         a = np.ascontiguousarray(arr16, dtype=np.float16)
         rows, cols = (a.shape[0], a.shape[1]) if a.ndim == 2 else (1, a.size)
         call("b2_model_set_tensor", self.h, name.encode(), a.ctypes.data, rows, cols)
+
+    def set_tensor_bf16(self, name: str, bits):
+        """Upload a bf16 tensor given as its raw 16-bit patterns (uint16);
+        the library converts it to fp16 on the device."""
+        import numpy as np
+        a = np.ascontiguousarray(bits, dtype=np.uint16)
+        rows, cols = (a.shape[0], a.shape[1]) if a.ndim == 2 else (1, a.size)
+        call("b2_model_set_tensor_bf16", self.h, name.encode(), a.ctypes.data, rows, cols)
+
+    def forward_logits(self, ids):
+        """fp32 logits of every position of one sequence [S, vocab] (full
+        forward through the batched prefill and an all-rows lm_head)."""
+        import numpy as np
+        a = np.ascontiguousarray(np.asarray(ids, dtype=np.int64).reshape(-1))
+        out = np.empty((a.size, self.vocab), np.float32)
+        call("b2_model_forward_logits", self.h, a.ctypes.data, a.size, out.ctypes.data)
+        self._B = 1
+        return out
 
     def reset(self):
         call("b2_model_reset", self.h)

@@ -113,6 +113,40 @@ __global__ void fill_half_kernel(__half* dst, int64_t n, float v) {
 // ---------------------------------------------------------------------------
 // step boundary kernels
 // ---------------------------------------------------------------------------
+// bf16 -> fp16 in place, by the checkpoint loader's bit rule
+// (src/loader/safetensors.cpp:307-328): the 8-bit exponent is rebased to 5
+// bits, values below the fp16 normal range become signed zero, values above
+// it (and inf / NaN) signed infinity, and the 7 mantissa bits move up
+// unchanged (bf16's mantissa fits fp16's, so normal values convert exactly).
+__global__ void bf16_to_f16_kernel(uint16_t* __restrict__ p, int64_t n) {
+    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
+        const uint32_t u = p[i];
+        const uint32_t sign = u & 0x8000u;
+        const int e = (int)((u >> 7) & 0xFFu) - 127 + 15;
+        const uint32_t mant = (u & 0x7Fu) << 3;
+        uint32_t o;
+        if (e <= 0) o = sign;
+        else if (e >= 31) o = sign | 0x7C00u;
+        else o = sign | ((uint32_t)e << 10) | mant;
+        p[i] = (uint16_t)o;
+    }
+}
+
+// Step inputs passed by value (kernel parameters are captured at launch, so
+// the caller's host memory is free as soon as the launch returns).
+struct StepInputs {
+    int64_t tokens[kMaxBatch];
+    int positions[kMaxBatch];
+};
+
+__global__ void set_step_inputs_kernel(const StepInputs in, int B, int64_t* __restrict__ tokens,
+                                       int* __restrict__ positions) {
+    for (int b = threadIdx.x; b < B; b += blockDim.x) {
+        tokens[b] = in.tokens[b];
+        positions[b] = in.positions[b];
+    }
+}
+
 __global__ void step_begin_kernel(const int64_t* __restrict__ tokens, const int* __restrict__ positions,
                                   const __half* __restrict__ embed, float* __restrict__ hidden, int H,
                                   int* __restrict__ seq_lens, unsigned long long* __restrict__ argmax,
@@ -574,6 +608,8 @@ struct b2_model {
     __half* pf_gate = nullptr;   // [T, inter] (SwiGLU output in place)
     __half* pf_up = nullptr;     // [T, inter]
     int64_t* pf_ids = nullptr;   // [T]
+    float* pf_logits = nullptr;  // [rows, vocab] logits of every position (b2_model_forward_logits)
+    int64_t pf_logits_rows = 0;
 
     // tensor-parallel exchange over peer memory (see TpExchange)
     void* p2p_base = nullptr;           // this rank's exchange region (IPC-exported)
@@ -655,7 +691,7 @@ extern "C" int b2_model_destroy(b2_model* m) {
     for (void* p : m->allocs) cudaFree(p);
     cudaFree(m->trace_buf);
     for (void* p : {(void*)m->pf_hidden, (void*)m->pf_xn, (void*)m->pf_qkv, (void*)m->pf_attn, (void*)m->pf_gate,
-                    (void*)m->pf_up, (void*)m->pf_ids})
+                    (void*)m->pf_up, (void*)m->pf_ids, (void*)m->pf_logits})
         cudaFree(p);
     cudaFreeHost(m->h_tokens);
     cudaFreeHost(m->h_pos);
@@ -973,15 +1009,43 @@ extern "C" int b2_model_init_random(b2_model* m, uint64_t seed, float stddev) {
     return B2_OK;
 }
 
-// Copy the [rows, cols] sub-block at (row0, col0) of a host [*, ld] fp16 tensor.
+static int convert_block(b2_model* m, __half* dst, int64_t rows, int64_t cols);
+
+// Copy the [rows, cols] sub-block at (row0, col0) of a host [*, ld] fp16 tensor
+// (bf16: converted to fp16 on the device after the copy).
 static int upload_block(b2_model* m, __half* dst, const uint16_t* src, int64_t rows, int64_t cols, int64_t row0,
-                        int64_t col0, int64_t ld) {
+                        int64_t col0, int64_t ld, bool bf16 = false) {
     B2_TRY(cudaMemcpy2DAsync(dst, cols * 2, src + row0 * ld + col0, ld * 2, cols * 2, rows, cudaMemcpyHostToDevice,
                              m->stream));
+    if (bf16) return convert_block(m, dst, rows, cols);
     return B2_OK;
 }
 
+// Convert the [rows, cols] block just uploaded at dst from bf16 to fp16.
+static int convert_block(b2_model* m, __half* dst, int64_t rows, int64_t cols) {
+    const int64_t n = rows * cols;
+    if (n <= 0) return B2_OK;
+    int64_t blocks = (n + 255) / 256;
+    if (blocks > (int64_t)sm_count() * 16) blocks = (int64_t)sm_count() * 16;
+    bf16_to_f16_kernel<<<(unsigned)blocks, 256, 0, m->stream>>>(reinterpret_cast<uint16_t*>(dst), n);
+    B2_CHECK_LAUNCH();
+    return B2_OK;
+}
+
+static int set_tensor(b2_model* m, const char* name, const uint16_t* src, int64_t rows, int64_t cols, bool bf16);
+
 extern "C" int b2_model_set_tensor(b2_model* m, const char* name, const uint16_t* src, int64_t rows, int64_t cols) {
+    return set_tensor(m, name, src, rows, cols, false);
+}
+
+extern "C" int b2_model_set_tensor_bf16(b2_model* m, const char* name, const uint16_t* src, int64_t rows,
+                                        int64_t cols) {
+    return set_tensor(m, name, src, rows, cols, true);
+}
+
+// Upload (and for bf16 sources convert on the device) this rank's block of a
+// global tensor.
+static int set_tensor(b2_model* m, const char* name, const uint16_t* src, int64_t rows, int64_t cols, bool bf16) {
     B2_REQUIRE(m && name && src);
     const b2_model_config& c = m->cfg;
     const int64_t H = c.hidden_size, D = c.head_dim;
@@ -990,11 +1054,11 @@ extern "C" int b2_model_set_tensor(b2_model* m, const char* name, const uint16_t
     int rc = B2_ERR_INVALID;
     auto shape = [&](int64_t r, int64_t cc) { return rows == r && cols == cc; };
     if (n == "embed" && shape(c.vocab_size, H)) {
-        rc = upload_block(m, m->embed, src, c.vocab_size, H, 0, 0, H);
+        rc = upload_block(m, m->embed, src, c.vocab_size, H, 0, 0, H, bf16);
     } else if (n == "lm_head" && shape(c.vocab_size, H) && !c.tie_word_embeddings) {
-        rc = upload_block(m, m->lm_head, src, m->vocab_l, H, m->vocab_off, 0, H);
+        rc = upload_block(m, m->lm_head, src, m->vocab_l, H, m->vocab_off, 0, H, bf16);
     } else if (n == "final_norm" && rows * cols == H) {
-        rc = upload_block(m, m->final_norm, src, 1, H, 0, 0, H);
+        rc = upload_block(m, m->final_norm, src, 1, H, 0, 0, H, bf16);
     } else {
         const size_t dot = n.find('.');
         if (dot == std::string::npos) return B2_ERR_INVALID;
@@ -1003,24 +1067,24 @@ extern "C" int b2_model_set_tensor(b2_model* m, const char* name, const uint16_t
         if (l < 0 || l >= c.num_layers) return B2_ERR_INVALID;
         LayerW& w = m->layers[l];
         const int64_t I = c.intermediate_size;
-        if (t == "ln1" && rows * cols == H) rc = upload_block(m, w.ln1, src, 1, H, 0, 0, H);
-        else if (t == "ln2" && rows * cols == H) rc = upload_block(m, w.ln2, src, 1, H, 0, 0, H);
-        else if (t == "wq" && shape((int64_t)c.num_q_heads * D, H)) rc = upload_block(m, w.wqkv, src, qd, H, m->rank * qd, 0, H);
+        if (t == "ln1" && rows * cols == H) rc = upload_block(m, w.ln1, src, 1, H, 0, 0, H, bf16);
+        else if (t == "ln2" && rows * cols == H) rc = upload_block(m, w.ln2, src, 1, H, 0, 0, H, bf16);
+        else if (t == "wq" && shape((int64_t)c.num_q_heads * D, H)) rc = upload_block(m, w.wqkv, src, qd, H, m->rank * qd, 0, H, bf16);
         else if (t == "wk" && shape((int64_t)c.num_kv_heads * D, H))
-            rc = upload_block(m, w.wqkv + qd * H, src, kvd, H, m->rank * kvd, 0, H);
+            rc = upload_block(m, w.wqkv + qd * H, src, kvd, H, m->rank * kvd, 0, H, bf16);
         else if (t == "wv" && shape((int64_t)c.num_kv_heads * D, H))
-            rc = upload_block(m, w.wqkv + (qd + kvd) * H, src, kvd, H, m->rank * kvd, 0, H);
+            rc = upload_block(m, w.wqkv + (qd + kvd) * H, src, kvd, H, m->rank * kvd, 0, H, bf16);
         else if (t == "bq" && w.bqkv && rows * cols == (int64_t)c.num_q_heads * D)
-            rc = upload_block(m, w.bqkv, src, 1, qd, 0, m->rank * qd, rows * cols);
+            rc = upload_block(m, w.bqkv, src, 1, qd, 0, m->rank * qd, rows * cols, bf16);
         else if (t == "bk" && w.bqkv && rows * cols == (int64_t)c.num_kv_heads * D)
-            rc = upload_block(m, w.bqkv + qd, src, 1, kvd, 0, m->rank * kvd, rows * cols);
+            rc = upload_block(m, w.bqkv + qd, src, 1, kvd, 0, m->rank * kvd, rows * cols, bf16);
         else if (t == "bv" && w.bqkv && rows * cols == (int64_t)c.num_kv_heads * D)
-            rc = upload_block(m, w.bqkv + qd + kvd, src, 1, kvd, 0, m->rank * kvd, rows * cols);
+            rc = upload_block(m, w.bqkv + qd + kvd, src, 1, kvd, 0, m->rank * kvd, rows * cols, bf16);
         else if (t == "wo" && shape(H, (int64_t)c.num_q_heads * D))
-            rc = upload_block(m, w.wo, src, H, qd, 0, m->rank * qd, (int64_t)c.num_q_heads * D);
-        else if (t == "wg" && shape(I, H)) rc = upload_block(m, w.wg, src, m->inter, H, (int64_t)m->rank * m->inter, 0, H);
-        else if (t == "wu" && shape(I, H)) rc = upload_block(m, w.wu, src, m->inter, H, (int64_t)m->rank * m->inter, 0, H);
-        else if (t == "wd" && shape(H, I)) rc = upload_block(m, w.wd, src, H, m->inter, 0, (int64_t)m->rank * m->inter, I);
+            rc = upload_block(m, w.wo, src, H, qd, 0, m->rank * qd, (int64_t)c.num_q_heads * D, bf16);
+        else if (t == "wg" && shape(I, H)) rc = upload_block(m, w.wg, src, m->inter, H, (int64_t)m->rank * m->inter, 0, H, bf16);
+        else if (t == "wu" && shape(I, H)) rc = upload_block(m, w.wu, src, m->inter, H, (int64_t)m->rank * m->inter, 0, H, bf16);
+        else if (t == "wd" && shape(H, I)) rc = upload_block(m, w.wd, src, H, m->inter, 0, (int64_t)m->rank * m->inter, I, bf16);
     }
     if (rc != B2_OK) return rc;
     B2_TRY(cudaStreamSynchronize(m->stream));
@@ -1454,10 +1518,31 @@ extern "C" int b2_model_decode_step(b2_model* m, const int64_t* host_tokens, con
     return B2_OK;
 }
 
+extern "C" int b2_model_decode_enqueue(b2_model* m, const int64_t* host_tokens, const int* host_positions, int B,
+                                       float* d_logits) {
+    B2_REQUIRE(m && host_tokens && host_positions && B >= 1 && B <= m->cfg.max_batch);
+    if (d_logits && m->tp != 1) return B2_ERR_UNSUPPORTED;
+    StepInputs in;
+    for (int b = 0; b < B; ++b) {
+        if (host_positions[b] < 0 || host_positions[b] >= m->cfg.max_seq) return B2_ERR_INVALID;
+        if (host_tokens[b] < 0 || host_tokens[b] >= m->cfg.vocab_size) return B2_ERR_INVALID;
+        in.tokens[b] = host_tokens[b];
+        in.positions[b] = host_positions[b];
+    }
+    set_step_inputs_kernel<<<1, 32, 0, m->stream>>>(in, B, m->tokens, m->positions);
+    B2_CHECK_LAUNCH();
+    M_TRY(run_step(m, B));
+    m->last_B = B;
+    if (d_logits)
+        B2_TRY(cudaMemcpyAsync(d_logits, m->logits, (size_t)B * m->cfg.vocab_size * sizeof(float),
+                               cudaMemcpyDeviceToDevice, m->stream));
+    return B2_OK;
+}
+
 static int ensure_prefill_ws(b2_model* m, int64_t T) {
     if (T <= m->pf_tokens) return B2_OK;
     for (void* p : {(void*)m->pf_hidden, (void*)m->pf_xn, (void*)m->pf_qkv, (void*)m->pf_attn, (void*)m->pf_gate,
-                    (void*)m->pf_up, (void*)m->pf_ids})
+                    (void*)m->pf_up, (void*)m->pf_ids, (void*)m->pf_logits})
         cudaFree(p);
     m->pf_hidden = nullptr; m->pf_xn = m->pf_qkv = m->pf_attn = m->pf_gate = m->pf_up = nullptr; m->pf_ids = nullptr;
     m->pf_tokens = 0;
@@ -1563,6 +1648,37 @@ extern "C" int b2_model_prefill(b2_model* m, const int64_t* host_ids, int B, int
     m->last_B = B;
     if (host_logits) M_TRY(copy_logits_out(m, B, host_logits));
     B2_TRY(cudaStreamSynchronize(m->stream));
+    return B2_OK;
+}
+
+extern "C" int b2_model_forward_logits(b2_model* m, const int64_t* host_ids, int S, float* host_logits) {
+    B2_REQUIRE(m && host_ids && host_logits && S >= 1 && S <= m->cfg.max_seq);
+    if (m->tp != 1) return B2_ERR_UNSUPPORTED;
+    const b2_model_config& c = m->cfg;
+    for (int64_t i = 0; i < S; ++i)
+        if (host_ids[i] < 0 || host_ids[i] >= c.vocab_size) return B2_ERR_INVALID;
+    M_TRY(ensure_prefill_ws(m, S));
+    if (S > m->pf_logits_rows) {
+        cudaFree(m->pf_logits);
+        m->pf_logits = nullptr;
+        m->pf_logits_rows = 0;
+        B2_TRY(cudaMalloc(&m->pf_logits, (size_t)S * c.vocab_size * sizeof(float)));
+        m->pf_logits_rows = S;
+    }
+    cudaStream_t st = m->stream;
+    B2_TRY(cudaMemcpyAsync(m->pf_ids, host_ids, (size_t)S * sizeof(int64_t), cudaMemcpyHostToDevice, st));
+    B2_TRY(cudaMemsetAsync(m->hist_count, 0, sizeof(int), st));
+    M_TRY(prefill_batched(m, 1, S));
+    m->last_B = 1;
+    // every position through the final norm and the lm_head (tensor cores)
+    const int H = c.hidden_size;
+    rmsnorm_rows_kernel<<<(unsigned)S, H >= 1024 ? 256 : 128, 0, st>>>(m->pf_hidden, m->final_norm, m->pf_xn, H,
+                                                                      c.rms_norm_eps);
+    B2_CHECK_LAUNCH();
+    M_TRY(gemm_tc(m->pf_xn, m->lm_head, m->pf_logits, S, c.vocab_size, H, TC_F32, st));
+    B2_TRY(cudaMemcpyAsync(host_logits, m->pf_logits, (size_t)S * c.vocab_size * sizeof(float), cudaMemcpyDeviceToHost,
+                           st));
+    B2_TRY(cudaStreamSynchronize(st));
     return B2_OK;
 }
 
