@@ -65,6 +65,23 @@ __device__ __forceinline__ void load_rows(uint4 (&w)[R][U], const uint4* const (
     }
 }
 
+template <int R, int OM>
+__device__ __forceinline__ void task_rows(const GemvParams& p, int t, const uint4* (&rp)[R]) {
+    if constexpr (OM == OUT_QKV) {
+        const int half = p.D >> 1;
+        const int h = t / half, i = t - h * half;
+        const int r0 = h * p.D + i;
+        rp[0] = reinterpret_cast<const uint4*>(p.W + (size_t)r0 * p.K);
+        rp[1] = reinterpret_cast<const uint4*>(p.W + (size_t)(r0 + half) * p.K);
+    } else if constexpr (OM == OUT_SWIGLU) {
+        rp[0] = reinterpret_cast<const uint4*>(p.W + (size_t)t * p.K);
+        rp[1] = reinterpret_cast<const uint4*>(p.W2 + (size_t)t * p.K);
+    } else {
+        rp[0] = reinterpret_cast<const uint4*>(p.W + (size_t)t * p.K);
+    }
+}
+
+
 // ---------------------------------------------------------------------------
 // register-streaming form
 // ---------------------------------------------------------------------------

@@ -121,15 +121,6 @@ struct GemvParams {
     float* hid_out;              // X_SUM: residual stream after it
     int rows_per_cta;            // OUT_PUSH: contiguous block of rows per CTA (set at launch)
     TraceSlot trace;             // step trace (buf null: off)
-
-    // batch-1 weight-ring form (gemv_ring.cu): fp32 partial dot products of
-    // task groups cut between CTAs, [CTAs][2][8 warps][2]; per-group arrival
-    // counters (zero between launches) for up to ring_cnt_cap groups; the
-    // bounded-wait error word
-    float* ring_part;
-    int* ring_cnt;
-    int ring_cnt_cap;
-    int* ring_err;
 };
 
 constexpr int kPushRows = 128;   // OUT_PUSH rows per CTA at most
@@ -167,13 +158,5 @@ int gemv_launch(const GemvParams& p, XMode xm, OutMode om, cudaStream_t s, bool 
 
 // Maximum batch tile handled by one gemv_launch for row length K.
 int gemv_batch_tile(int K);
-
-// Batch-1 form fed by a bulk-copy weight ring (gemv_ring.cu); needs
-// ring_part / ring_cnt / ring_err.  B2_ERR_UNSUPPORTED when it does not apply
-// (batch > 1, tensor-parallel exchange, unaligned, very long rows).
-int gemv_ring_launch(const GemvParams& p, XMode xm, OutMode om, cudaStream_t s, bool pdl);
-// Scratch sizes of the ring form: partial floats, and groups for `tasks` rows.
-size_t ring_part_floats();
-int ring_groups(int tasks);
 
 }  // namespace b2

@@ -44,17 +44,6 @@ __device__ __forceinline__ int xsum_group_lanes(int tp) {
     return g <= 1 ? 1 : (g <= 2 ? 2 : 4);
 }
 
-// Barrier over the NT threads that stage x: the whole block (BAR == 0), or
-// named barrier BAR over the first NT threads (kernels whose other warps do
-// not take part, e.g. a weight-producer warp).
-template <int BAR, int NT>
-__device__ __forceinline__ void cta_sync() {
-    if constexpr (BAR == 0)
-        __syncthreads();
-    else
-        asm volatile("bar.sync %0, %1;" ::"n"(BAR), "n"(NT) : "memory");
-}
-
 // X_SUM staging, shared across the thread-block cluster.  The new residual
 // h = hid_in + (sum of every rank's partial) is needed whole by every CTA
 // (RMSNorm, then the GEMV's x), but each word of the exchange only has to
@@ -203,8 +192,8 @@ __device__ __forceinline__ void stage_x_sum(const GemvParams& p, uint4* __restri
 }
 
 // Stage x for BT sequences into xs[BT][K8] (packed half).  Ends with a
-// barrier (cta_sync<BAR, NT>); every thread taking part must call it.
-template <int BT, int XM, int NT, int BAR = 0>
+// __syncthreads; every thread of the block must call it.
+template <int BT, int XM, int NT>
 __device__ __forceinline__ void stage_x(const GemvParams& p, uint4* __restrict__ xs, float* s_rs,
                                         float (*s_ss)[NT / 32], int lane, int warp) {
     const int K8 = p.K >> 3;
@@ -234,14 +223,14 @@ __device__ __forceinline__ void stage_x(const GemvParams& p, uint4* __restrict__
             const float v = warp_sum(ss[b]);
             if (lane == 0) s_ss[b][warp] = v;
         }
-        cta_sync<BAR, NT>();
+        __syncthreads();
         if (threadIdx.x < BT) {
             float tot = 0.f;
 #pragma unroll
             for (int w = 0; w < (NT / 32); ++w) tot += s_ss[threadIdx.x][w];
             s_rs[threadIdx.x] = rsqrtf(tot / (float)p.K + p.eps);
         }
-        cta_sync<BAR, NT>();
+        __syncthreads();
         for (int i = threadIdx.x; i < BT * K8; i += NT) {
             const int b = i / K8, c = i - b * K8;
             uint4 o = make_uint4(0, 0, 0, 0);
@@ -265,25 +254,8 @@ __device__ __forceinline__ void stage_x(const GemvParams& p, uint4* __restrict__
                             : make_uint4(0, 0, 0, 0);
         }
     }
-    cta_sync<BAR, NT>();
+    __syncthreads();
 
-}
-
-// Weight rows of task t: one row, or the pair its epilogue needs together.
-template <int R, int OM>
-__device__ __forceinline__ void task_rows(const GemvParams& p, int t, const uint4* (&rp)[R]) {
-    if constexpr (OM == OUT_QKV) {
-        const int half = p.D >> 1;
-        const int h = t / half, i = t - h * half;
-        const int r0 = h * p.D + i;
-        rp[0] = reinterpret_cast<const uint4*>(p.W + (size_t)r0 * p.K);
-        rp[1] = reinterpret_cast<const uint4*>(p.W + (size_t)(r0 + half) * p.K);
-    } else if constexpr (OM == OUT_SWIGLU) {
-        rp[0] = reinterpret_cast<const uint4*>(p.W + (size_t)t * p.K);
-        rp[1] = reinterpret_cast<const uint4*>(p.W2 + (size_t)t * p.K);
-    } else {
-        rp[0] = reinterpret_cast<const uint4*>(p.W + (size_t)t * p.K);
-    }
 }
 
 // Epilogue of task t once acc holds its warp-reduced dot products (every

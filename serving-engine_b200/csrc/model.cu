@@ -619,10 +619,6 @@ struct b2_model {
     float* hidden2 = nullptr;           // second residual-stream buffer
     int* step_ctr = nullptr;            // decode steps completed
     int* push_ctr = nullptr;            // arrival counter of pushing kernels
-    // batch-1 weight-ring GEMVs (gemv_ring.cu): partial sums and group counters
-    float* ring_part = nullptr;
-    int* ring_cnt = nullptr;
-    int ring_cnt_cap = 0;
     bool p2p_on = false;
     TpExchange tpx{};
     // batched decode step (B > kGemvMaxBatch): split-K GEMM partial slabs and
@@ -846,14 +842,6 @@ extern "C" int b2_model_create(const b2_model_config* cfg, int tp_rank, int tp_s
     }
     M_ALLOC(m->step_ctr, 256);
     M_ALLOC(m->push_ctr, 256);
-    {   // ring GEMV scratch: one counter per task group of the widest projection
-        const int widest = std::max(std::max(m->qkv_rows / 2, H), std::max(m->inter, m->vocab_l));
-        m->ring_cnt_cap = ring_groups(widest);
-        M_ALLOC(m->ring_part, ring_part_floats() * sizeof(float));
-        M_ALLOC(m->ring_cnt, (size_t)m->ring_cnt_cap * sizeof(int));
-        cudaError_t e = cudaMemset(m->ring_cnt, 0, (size_t)m->ring_cnt_cap * sizeof(int));
-        if (e != cudaSuccess) { b2_model_destroy(m); return (int)e; }
-    }
     if (tp_size > 1) {
         auto up = [](size_t x) { return (x + 255) & ~size_t(255); };
         m->off_recv = 0;
@@ -1134,18 +1122,6 @@ static void set_exchange(b2_model* m, GemvParams& p, int slot, const float* hin,
     p.hid_out = hout;
 }
 
-// One decode GEMV without the tensor-parallel exchange: the batch-1
-// weight-ring form where it applies, else the register-streaming form.
-static int run_gemv(b2_model* m, GemvParams& p, XMode xm, OutMode om, bool pdl) {
-    p.ring_part = m->ring_part;
-    p.ring_cnt = m->ring_cnt;
-    p.ring_cnt_cap = m->ring_cnt_cap;
-    p.ring_err = wait_error_word();
-    const int rc = gemv_ring_launch(p, xm, om, m->stream, pdl);
-    if (rc != B2_ERR_UNSUPPORTED) return rc;
-    return gemv_launch(p, xm, om, m->stream, pdl);
-}
-
 static int launch_qkv(b2_model* m, int l, int B, bool pdl, bool xch = false) {
     const b2_model_config& c = m->cfg;
     LayerW& w = m->layers[l];
@@ -1177,7 +1153,7 @@ static int launch_qkv(b2_model* m, int l, int B, bool pdl, bool xch = false) {
         p.x = m->hidden2;
         return gemv_launch(p, X_SUM, OUT_QKV, m->stream, pdl);
     }
-    return run_gemv(m, p, X_NORM, OUT_QKV, pdl);
+    return gemv_launch(p, X_NORM, OUT_QKV, m->stream, pdl);
 }
 
 static int launch_attn(b2_model* m, int l, int B, bool pdl) {
@@ -1210,7 +1186,7 @@ static int launch_o(b2_model* m, int l, int B, bool pdl, bool xch = false) {
         set_exchange(m, p, 2 * l, nullptr, nullptr);
         return gemv_launch(p, X_HALF, OUT_PUSH, m->stream, pdl);
     }
-    return run_gemv(m, p, X_HALF, OUT_RESID, pdl);
+    return gemv_launch(p, X_HALF, OUT_RESID, m->stream, pdl);
 }
 
 static int launch_gateup(b2_model* m, int l, int B, bool pdl, bool xch = false) {
@@ -1233,7 +1209,7 @@ static int launch_gateup(b2_model* m, int l, int B, bool pdl, bool xch = false) 
         set_exchange(m, p, 2 * l, m->hidden, m->hidden2);
         return gemv_launch(p, X_SUM, OUT_SWIGLU, m->stream, pdl);
     }
-    return run_gemv(m, p, X_NORM, OUT_SWIGLU, pdl);
+    return gemv_launch(p, X_NORM, OUT_SWIGLU, m->stream, pdl);
 }
 
 static int launch_down(b2_model* m, int l, int B, bool pdl, bool xch = false) {
@@ -1253,7 +1229,7 @@ static int launch_down(b2_model* m, int l, int B, bool pdl, bool xch = false) {
         set_exchange(m, p, 2 * l + 1, nullptr, nullptr);
         return gemv_launch(p, X_HALF, OUT_PUSH, m->stream, pdl);
     }
-    return run_gemv(m, p, X_HALF, OUT_RESID, pdl);
+    return gemv_launch(p, X_HALF, OUT_RESID, m->stream, pdl);
 }
 
 static int launch_lm_head(b2_model* m, int B, bool pdl, bool xch = false) {
@@ -1278,7 +1254,7 @@ static int launch_lm_head(b2_model* m, int B, bool pdl, bool xch = false) {
         p.x = m->hidden2;
         return gemv_launch(p, X_SUM, OUT_LOGITS, m->stream, pdl);
     }
-    return run_gemv(m, p, X_NORM, OUT_LOGITS, pdl);
+    return gemv_launch(p, X_NORM, OUT_LOGITS, m->stream, pdl);
 }
 
 
