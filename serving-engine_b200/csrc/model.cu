@@ -1542,7 +1542,7 @@ extern "C" int b2_model_decode_enqueue(b2_model* m, const int64_t* host_tokens, 
 static int ensure_prefill_ws(b2_model* m, int64_t T) {
     if (T <= m->pf_tokens) return B2_OK;
     for (void* p : {(void*)m->pf_hidden, (void*)m->pf_xn, (void*)m->pf_qkv, (void*)m->pf_attn, (void*)m->pf_gate,
-                    (void*)m->pf_up, (void*)m->pf_ids, (void*)m->pf_logits})
+                    (void*)m->pf_up, (void*)m->pf_ids})
         cudaFree(p);
     m->pf_hidden = nullptr; m->pf_xn = m->pf_qkv = m->pf_attn = m->pf_gate = m->pf_up = nullptr; m->pf_ids = nullptr;
     m->pf_tokens = 0;

@@ -94,4 +94,8 @@ def test_forward_logits_from_bf16_checkpoint_matches_oracle(cuda, tmp_path):
     m.reset()
     last = m.prefill(ids[None, :])[0]
     assert float(np.max(np.abs(last - got[-1]))) <= 2e-3
+    # longer sequences grow the workspaces: every call gives the prefix's rows
+    for S in (41, 57):
+        ids2 = np.random.default_rng(S).integers(0, V, S)
+        assert float(np.max(np.abs(m.forward_logits(ids2)[-1] - m.prefill(ids2[None, :])[0]))) <= 2e-3
     m.close()
