@@ -157,13 +157,38 @@ int b2_flash_prefill_gqa(const void* q, const void* k, const void* v, void* out,
  * rope_theta > 0: q rotated inside the attention kernel, k once per key by a
  * pre-pass kernel of the same call into a per-device scratch copy
  * (batch*S*nkv*head_dim*2 bytes, allocated on first use and grown as
- * needed; RoPE calls on one device must not overlap in time).  q, k in
+ * needed; RoPE calls on one device must not overlap in time; see
+ * b2_flash_prefill_gqa_ws for the form that allocates nothing).  q, k in
  * memory are left unrotated.  head_dim 64 or 128 only.  New API (the
  * reference applies RoPE as a separate apply_rope launch,
  * src/model/forward_gpu.cu:419-421). */
 int b2_flash_prefill_gqa_ex(const void* q, const void* k, const void* v, void* out, int64_t seq_len,
                             int num_q_heads, int num_kv_heads, int head_dim, int batch_size, int bf16,
                             float rope_theta, int64_t start_pos, void* stream);
+
+/* Device scratch owned by the caller and lent to the entry points that take
+ * one, so that those never allocate (SURVEY's explicit-workspace boundary; no
+ * counterpart in the reference, whose only internal workspaces are the
+ * sampler's).  b2_workspace_create allocates `bytes` of device memory on the
+ * current device; the handle may be reused by any number of calls on that
+ * device that do not overlap in time. */
+typedef struct b2_workspace b2_workspace;
+int b2_workspace_create(size_t bytes, b2_workspace** out);
+int b2_workspace_destroy(b2_workspace* ws);
+size_t b2_workspace_bytes(const b2_workspace* ws);
+
+/* Workspace bytes b2_flash_prefill_gqa_ws needs for the RoPE form
+ * (batch * S * nkv * head_dim * 2: the rotated keys). */
+size_t b2_flash_prefill_workspace_bytes(int64_t seq_len, int num_kv_heads, int head_dim, int batch_size);
+
+/* b2_flash_prefill_gqa_ex with the rotated-key scratch taken from `ws`
+ * (B2_ERR_WORKSPACE when it is smaller than
+ * b2_flash_prefill_workspace_bytes): allocates nothing, so it is
+ * graph-capturable from its first call.  ws == NULL behaves as _ex.  New API
+ * (see b2_flash_prefill_gqa_ex). */
+int b2_flash_prefill_gqa_ws(const void* q, const void* k, const void* v, void* out, int64_t seq_len,
+                            int num_q_heads, int num_kv_heads, int head_dim, int batch_size, int bf16,
+                            float rope_theta, int64_t start_pos, b2_workspace* ws, void* stream);
 
 /* out = silu(gate) * up, half. Replaces engine::cuda::swiglu (src/cuda/kernels.h:151-157). */
 int b2_swiglu(const void* gate, const void* up, void* out, int64_t count, void* stream);
@@ -223,6 +248,14 @@ int b2_sampler_destroy(b2_sampler* s);
  * Replaces SamplerGPU::sample (src/runtime/sampler.h:28-33, sampler.cu:202-340). */
 int b2_sampler_sample(b2_sampler* s, const float* d_logits, const int64_t* history, int history_len,
                       const b2_sampler_config* cfg, void* stream, int* token_out);
+/* b2_sampler_sample without a host round trip: history is a device int64
+ * array, the chosen id is written to d_token (device int) on `stream`, and
+ * nothing is allocated or synchronised (the LCG state, kept on the host, is
+ * advanced at enqueue time, so draws follow the order of the calls).  Same
+ * selection, semantics and bit-exact ids as b2_sampler_sample.  New API (the
+ * reference copies the logits to the host, src/runtime/sampler.cu:253-256). */
+int b2_sampler_sample_async(b2_sampler* s, const float* d_logits, const int64_t* d_history, int history_len,
+                            const b2_sampler_config* cfg, void* stream, int* d_token);
 /* Current LCG state (for tests) and explicit set. */
 uint64_t b2_sampler_rng_state(const b2_sampler* s);
 int b2_sampler_set_rng_state(b2_sampler* s, uint64_t state);

@@ -60,6 +60,11 @@ _SIGS = {
     "b2_decode_gqa_split_noalloc": (i32, [vp, KVView, KVView, vp, vp, i32, i32, i32, i32, i32, vp]),
     "b2_flash_prefill_gqa": (i32, [vp, vp, vp, vp, i64, i32, i32, i32, i32, vp]),
     "b2_flash_prefill_gqa_ex": (i32, [vp, vp, vp, vp, i64, i32, i32, i32, i32, i32, f32, i64, vp]),
+    "b2_workspace_create": (i32, [C.c_size_t, C.POINTER(vp)]),
+    "b2_workspace_destroy": (i32, [vp]),
+    "b2_workspace_bytes": (C.c_size_t, [vp]),
+    "b2_flash_prefill_workspace_bytes": (C.c_size_t, [i64, i32, i32, i32]),
+    "b2_flash_prefill_gqa_ws": (i32, [vp, vp, vp, vp, i64, i32, i32, i32, i32, i32, f32, i64, vp, vp]),
     "b2_swiglu": (i32, [vp, vp, vp, i64, vp]),
     "b2_matmul_transB": (i32, [vp, vp, vp, i32, i32, i32, vp]),
     "b2_matmul_transB_f32": (i32, [vp, vp, vp, i32, i32, i32, vp]),
@@ -71,6 +76,7 @@ _SIGS = {
     "b2_sampler_create": (i32, [i32, i32, C.POINTER(vp)]),
     "b2_sampler_destroy": (i32, [vp]),
     "b2_sampler_sample": (i32, [vp, vp, vp, i32, C.POINTER(SamplerConfig), vp, C.POINTER(i32)]),
+    "b2_sampler_sample_async": (i32, [vp, vp, vp, i32, C.POINTER(SamplerConfig), vp, vp]),
     "b2_sampler_rng_state": (u64, [vp]),
     "b2_sampler_set_rng_state": (i32, [vp, u64]),
     "b2_nccl_unique_id": (i32, [vp]),
@@ -205,6 +211,14 @@ class Sampler:
         call("b2_sampler_sample", self.h, ptr(d_logits), hist.ctypes.data if hist.size else None, hist.size,
              C.byref(cfg), stream_ptr(stream), C.byref(tok))
         return tok.value
+
+    def sample_async(self, d_logits, d_history, history_len, d_token, temperature=0.0, top_k=0, top_p=1.0,
+                     repetition_penalty=1.0, seed=42, stream=None) -> None:
+        """Enqueue a draw: device history (int64), chosen id into d_token
+        (device int32); no host round trip."""
+        cfg = SamplerConfig(temperature, top_k, top_p, repetition_penalty, seed)
+        call("b2_sampler_sample_async", self.h, ptr(d_logits), ptr(d_history) if history_len else None, history_len,
+             C.byref(cfg), stream_ptr(stream), ptr(d_token))
 
     @property
     def rng_state(self) -> int:

@@ -35,6 +35,7 @@
 #include <vector>
 
 #include "gemv.cuh"
+#include "prefill.cuh"
 #include "skinny.cuh"
 
 #include <cooperative_groups.h>
@@ -56,20 +57,6 @@ int attn_decode_launch_step(const __half* q, const __half* kbase, const __half* 
                             int64_t ss, const int* seq_lens, __half* out, float* part, int splits, int B, int nq,
                             int nkv, int D, cudaStream_t s, TraceSlot trace);
 
-struct FlashArgs {
-    const void* q;
-    const void* k;
-    const void* v;
-    void* out;
-    int S, nq, nkv, D, batch;
-    int64_t ldq, ldkv, ldo;
-    bool bf16;
-    float rope_theta;
-    int pos0;
-};
-int flash_prefill_tc(const FlashArgs& a, cudaStream_t s);
-int causal_attention_rows_ld(const __half* q, int64_t ldq, const __half* k, const __half* v, int64_t ldkv,
-                             __half* out, int64_t ldo, int64_t S, int nq, int nkv, int D, int batch, cudaStream_t s);
 enum TcEpi : int { TC_HALF = 0, TC_F32 = 1, TC_F32_ADD = 2 };
 int gemm_tc(const __half* A, const __half* B, void* C, int M, int N, int K, int epi, cudaStream_t s);
 int attn_decode_launch_step_q(const __half* q, int64_t q_sb, const __half* kbase, const __half* vbase, int64_t sb,

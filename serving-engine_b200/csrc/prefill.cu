@@ -34,26 +34,16 @@
 // one query row per thread, scalar FMA, head_dim fixed at 64).
 #include <cmath>
 #include <mutex>
+#include <new>
 #include <type_traits>
 
+#include "prefill.cuh"
 #include "tc.cuh"
 
 namespace b2 {
 int causal_attention_rows(const __half* q, const __half* k, const __half* v, __half* out, int64_t S, int nq,
                           int nkv, int D, int batch, cudaStream_t s);
 bool attn_head_dim_supported(int D);
-
-struct FlashArgs {
-    const void* q;
-    const void* k;
-    const void* v;
-    void* out;
-    int S, nq, nkv, D, batch;
-    int64_t ldq, ldkv, ldo;  // elements between consecutive tokens
-    bool bf16;
-    float rope_theta;  // > 0: rotate q and k in-kernel
-    int pos0;
-};
 
 template <int D, bool ROPE>
 struct FlashCfg {
@@ -747,8 +737,14 @@ static int launch_flash(const FlashArgs& a_in, cudaStream_t s) {
     FlashArgs a = a_in;
     if constexpr (ROPE) {  // keys rotated once into a dense copy; K tiles then come from it
         void* rk = nullptr;
-        const int rrc = rotated_key_buffer((size_t)a.batch * a.S * a.nkv * D * 2, &rk);
-        if (rrc != B2_OK) return rrc;
+        const size_t need = (size_t)a.batch * a.S * a.nkv * D * 2;
+        if (a.rk_ws) {  // the caller's workspace: nothing is allocated here
+            if (a.rk_ws_bytes < need || !aligned16(a.rk_ws)) return B2_ERR_WORKSPACE;
+            rk = a.rk_ws;
+        } else {
+            const int rrc = rotated_key_buffer(need, &rk);
+            if (rrc != B2_OK) return rrc;
+        }
         const int64_t work = (int64_t)a.batch * a.S * a.nkv * (D / 16);
         int64_t blocks = (work + 255) / 256;
         if (blocks > (int64_t)sm_count() * 16) blocks = (int64_t)sm_count() * 16;
@@ -817,7 +813,7 @@ int flash_prefill_tc(const FlashArgs& a, cudaStream_t s) {
 
 static b2::FlashArgs dense_args(const void* q, const void* k, const void* v, void* out, int64_t S, int nq, int nkv,
                                 int D, int batch, bool bf16, float theta, int pos0) {
-    b2::FlashArgs a;
+    b2::FlashArgs a = {};
     a.q = q;
     a.k = k;
     a.v = v;
@@ -853,10 +849,53 @@ extern "C" int b2_flash_prefill_gqa(const void* q, const void* k, const void* v,
 extern "C" int b2_flash_prefill_gqa_ex(const void* q, const void* k, const void* v, void* out, int64_t S, int nq,
                                        int nkv, int D, int batch, int bf16, float rope_theta, int64_t start_pos,
                                        void* stream) {
+    return b2_flash_prefill_gqa_ws(q, k, v, out, S, nq, nkv, D, batch, bf16, rope_theta, start_pos, nullptr, stream);
+}
+
+struct b2_workspace {
+    void* ptr = nullptr;
+    size_t bytes = 0;
+};
+
+extern "C" int b2_workspace_create(size_t bytes, b2_workspace** out) {
+    B2_REQUIRE(out && bytes > 0);
+    *out = nullptr;
+    b2_workspace* w = new (std::nothrow) b2_workspace();
+    if (!w) return B2_ERR_INVALID;
+    const cudaError_t e = cudaMalloc(&w->ptr, bytes);
+    if (e != cudaSuccess) {
+        delete w;
+        return (int)e;
+    }
+    w->bytes = bytes;
+    *out = w;
+    return B2_OK;
+}
+
+extern "C" int b2_workspace_destroy(b2_workspace* ws) {
+    if (!ws) return B2_OK;
+    cudaFree(ws->ptr);
+    delete ws;
+    return B2_OK;
+}
+
+extern "C" size_t b2_workspace_bytes(const b2_workspace* ws) { return ws ? ws->bytes : 0; }
+
+extern "C" size_t b2_flash_prefill_workspace_bytes(int64_t S, int num_kv_heads, int head_dim, int batch) {
+    return S > 0 && num_kv_heads > 0 && head_dim > 0 && batch > 0 ? (size_t)batch * S * num_kv_heads * head_dim * 2 : 0;
+}
+
+extern "C" int b2_flash_prefill_gqa_ws(const void* q, const void* k, const void* v, void* out, int64_t S, int nq,
+                                       int nkv, int D, int batch, int bf16, float rope_theta, int64_t start_pos,
+                                       b2_workspace* ws, void* stream) {
     using namespace b2;
     if (S <= 0 || batch <= 0) return B2_OK;
     B2_REQUIRE(q && k && v && out && nq > 0 && nkv > 0 && nq % nkv == 0 && rope_theta >= 0.f && start_pos >= 0);
     B2_REQUIRE(start_pos + S < (int64_t)1 << 24);  // positions stay exact in float
-    return flash_prefill_tc(dense_args(q, k, v, out, S, nq, nkv, D, batch, bf16 != 0, rope_theta, (int)start_pos),
-                            as_stream(stream));
+    FlashArgs a = dense_args(q, k, v, out, S, nq, nkv, D, batch, bf16 != 0, rope_theta, (int)start_pos);
+    if (ws) {
+        a.rk_ws = ws->ptr;
+        a.rk_ws_bytes = ws->bytes;
+    }
+    return flash_prefill_tc(a, as_stream(stream));
 }

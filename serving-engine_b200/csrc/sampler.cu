@@ -66,6 +66,13 @@ __global__ void argmax_kernel(const float* __restrict__ logits, int active, unsi
     }
 }
 
+// Token id of the packed argmax key (0 when no candidate) into *token.
+__global__ void key_to_token_kernel(const unsigned long long* __restrict__ key, int* __restrict__ token) {
+    griddep_wait();
+    const unsigned long long k = *key;
+    *token = k ? (int)(~static_cast<uint32_t>(k & 0xffffffffull)) : 0;
+}
+
 __device__ __forceinline__ float masked_logit(const float* logits, int i, int V) {
     return (V > kRealVocab && i >= kRealVocab) ? -1e9f : logits[i];
 }
@@ -246,6 +253,12 @@ __global__ void __launch_bounds__(kTopkThreads) topk_sample_kernel(const float* 
 
 using namespace b2;
 
+#define M_TRY_S(expr)                 \
+    do {                              \
+        const int rc_ = (expr);       \
+        if (rc_ != B2_OK) return rc_; \
+    } while (0)
+
 struct b2_sampler {
     int device = 0;
     int vocab = 0;
@@ -303,35 +316,24 @@ extern "C" int b2_sampler_set_rng_state(b2_sampler* s, uint64_t state) {
     return B2_OK;
 }
 
-extern "C" int b2_sampler_sample(b2_sampler* s, const float* d_logits, const int64_t* history, int history_len,
-                                 const b2_sampler_config* cfg, void* stream, int* token_out) {
-    B2_REQUIRE(s && d_logits && cfg && token_out && history_len >= 0 && (history_len == 0 || history));
-    cudaStream_t st = as_stream(stream);
+// Enqueue the selection for logits `d_logits` with a device-side history;
+// the chosen id goes to d_token (device).  Host-side state: the LCG.
+static int sample_enqueue(b2_sampler* s, const float* d_logits, const int64_t* d_hist, int history_len,
+                          const b2_sampler_config* cfg, cudaStream_t st, int* d_token) {
     const int V = s->vocab;
     const float* lg = d_logits;
     const int blocks = sm_count() * 2;
     if (cfg->repetition_penalty != 1.0f && history_len > 0) {
-        if (history_len > s->hist_cap) {
-            cudaFree(s->d_hist);
-            s->d_hist = nullptr;
-            s->hist_cap = 0;
-            B2_TRY(cudaMalloc(&s->d_hist, sizeof(int64_t) * (size_t)history_len * 2));
-            s->hist_cap = history_len * 2;
-        }
-        B2_TRY(cudaMemcpyAsync(s->d_hist, history, sizeof(int64_t) * (size_t)history_len, cudaMemcpyHostToDevice, st));
         B2_TRY(launch(copy_logits_kernel, dim3(blocks), dim3(256), 0, st, false, d_logits, s->d_work, V, s->d_key));
-        B2_TRY(launch(penalty_kernel, dim3((history_len + 127) / 128), dim3(128), 0, st, false, s->d_work,
-                      (const int64_t*)s->d_hist, history_len, V, cfg->repetition_penalty));
+        B2_TRY(launch(penalty_kernel, dim3((history_len + 127) / 128), dim3(128), 0, st, false, s->d_work, d_hist,
+                      history_len, V, cfg->repetition_penalty));
         lg = s->d_work;
     }
     if (cfg->temperature <= 1e-6f) {
         const int active = V > kRealVocab ? kRealVocab : V;
         B2_TRY(cudaMemsetAsync(s->d_key, 0, sizeof(unsigned long long), st));
         B2_TRY(launch(argmax_kernel, dim3(blocks), dim3(256), 0, st, false, lg, active, s->d_key));
-        B2_TRY(cudaMemcpyAsync(s->h_key, s->d_key, sizeof(unsigned long long), cudaMemcpyDeviceToHost, st));
-        B2_TRY(cudaStreamSynchronize(st));
-        const unsigned long long k = *s->h_key;
-        *token_out = k ? (int)(~static_cast<uint32_t>(k & 0xffffffffull)) : 0;
+        B2_TRY(launch(key_to_token_kernel, dim3(1), dim3(1), 0, st, false, (const unsigned long long*)s->d_key, d_token));
         return B2_OK;
     }
     int K = cfg->top_k;
@@ -342,7 +344,32 @@ extern "C" int b2_sampler_sample(b2_sampler* s, const float* d_logits, const int
     s->rng = s->rng * 6364136223846793005ull + 1442695040888963407ull;
     const float u = static_cast<float>(static_cast<double>(s->rng >> 40) * (1.0 / 16777216.0));
     B2_TRY(launch(topk_sample_kernel, dim3(1), dim3(kTopkThreads), 0, st, false, lg, V, K, cfg->temperature,
-                  cfg->top_p, u, s->d_token));
+                  cfg->top_p, u, d_token));
+    return B2_OK;
+}
+
+extern "C" int b2_sampler_sample_async(b2_sampler* s, const float* d_logits, const int64_t* d_history,
+                                       int history_len, const b2_sampler_config* cfg, void* stream, int* d_token) {
+    B2_REQUIRE(s && d_logits && cfg && d_token && history_len >= 0 && (history_len == 0 || d_history));
+    return sample_enqueue(s, d_logits, d_history, history_len, cfg, as_stream(stream), d_token);
+}
+
+extern "C" int b2_sampler_sample(b2_sampler* s, const float* d_logits, const int64_t* history, int history_len,
+                                 const b2_sampler_config* cfg, void* stream, int* token_out) {
+    B2_REQUIRE(s && d_logits && cfg && token_out && history_len >= 0 && (history_len == 0 || history));
+    cudaStream_t st = as_stream(stream);
+    const bool pen = cfg->repetition_penalty != 1.0f && history_len > 0;
+    if (pen) {
+        if (history_len > s->hist_cap) {  // grown here; b2_sampler_sample_async never allocates
+            cudaFree(s->d_hist);
+            s->d_hist = nullptr;
+            s->hist_cap = 0;
+            B2_TRY(cudaMalloc(&s->d_hist, sizeof(int64_t) * (size_t)history_len * 2));
+            s->hist_cap = history_len * 2;
+        }
+        B2_TRY(cudaMemcpyAsync(s->d_hist, history, sizeof(int64_t) * (size_t)history_len, cudaMemcpyHostToDevice, st));
+    }
+    M_TRY_S(sample_enqueue(s, d_logits, s->d_hist, pen ? history_len : 0, cfg, st, s->d_token));
     B2_TRY(cudaMemcpyAsync(s->h_token, s->d_token, sizeof(int), cudaMemcpyDeviceToHost, st));
     B2_TRY(cudaStreamSynchronize(st));
     *token_out = *s->h_token;

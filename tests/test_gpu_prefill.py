@@ -136,3 +136,33 @@ def test_flash_prefill_fp16_rope_matches_separate_rope(cuda):
             b2.stream_ptr())
     assert b2.device_status() == 0
     assert float((out_a.float() - out_b.float()).abs().max()) < 4e-3
+
+
+def test_flash_prefill_workspace_form(cuda):
+    """b2_flash_prefill_gqa_ws takes the rotated-key scratch from a caller's
+    b2_workspace (no allocation): same bytes as b2_flash_prefill_gqa_ex, and
+    B2_ERR_WORKSPACE when the workspace is one byte short."""
+    import ctypes
+    import torch
+    S, nq, nkv, D = 700, 32, 8, 128
+    g = torch.Generator(device="cuda").manual_seed(9)
+    q = torch.randn(S, nq * D, generator=g, device="cuda").bfloat16()
+    k = torch.randn(S, nkv * D, generator=g, device="cuda").bfloat16()
+    v = torch.randn(S, nkv * D, generator=g, device="cuda").bfloat16()
+    out_a, out_b = torch.empty_like(q), torch.empty_like(q)
+    st = b2.stream_ptr()
+    b2.call("b2_flash_prefill_gqa_ex", q.data_ptr(), k.data_ptr(), v.data_ptr(), out_a.data_ptr(), S, nq, nkv, D, 1,
+            1, 500000.0, 3, st)
+    need = b2.lib().b2_flash_prefill_workspace_bytes(S, nkv, D, 1)
+    assert need == S * nkv * D * 2
+    for nbytes, want in ((need, 0), (need - 16, -3)):
+        ws = ctypes.c_void_p()
+        b2.call("b2_workspace_create", nbytes, ctypes.byref(ws))
+        assert b2.lib().b2_workspace_bytes(ws) == nbytes
+        rc = b2.lib().b2_flash_prefill_gqa_ws(q.data_ptr(), k.data_ptr(), v.data_ptr(), out_b.data_ptr(), S, nq, nkv,
+                                              D, 1, 1, 500000.0, 3, ws, st)
+        assert rc == want
+        torch.cuda.synchronize()
+        b2.call("b2_workspace_destroy", ws)
+    assert b2.device_status() == 0
+    assert torch.equal(out_a.view(torch.int16), out_b.view(torch.int16))

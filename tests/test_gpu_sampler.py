@@ -118,3 +118,33 @@ def test_token_ids_bit_exact_vs_oracle(cuda, V):
         lg = rng.standard_normal(V).astype(np.float32)
         lg[[7, 9, 11]] = lg.max() + 1.0
         assert dev_s.sample(dlog(lg), temperature=0.0) == O.argmax(lg) == 7
+
+
+def test_async_form_matches_synchronous(cuda):
+    """b2_sampler_sample_async (device history, device token, no host round
+    trip) draws the same ids as b2_sampler_sample from the same LCG sequence:
+    greedy, top-k / top-p with a fixed and a changing seed, and with the
+    repetition penalty."""
+    import torch
+    V = 32000
+    rng = np.random.default_rng(77)
+    a, b = b2.Sampler(V), b2.Sampler(V)
+    tok = torch.zeros(64, dtype=torch.int32, device="cuda")
+    hist = rng.integers(0, V, 40)
+    d_hist = torch.from_numpy(hist).cuda()
+    cases = [dict(temperature=0.0), dict(temperature=0.8, top_k=50, top_p=0.9, seed=7),
+             dict(temperature=1.0, top_k=0, top_p=0.95, seed=0), dict(temperature=0.7, top_k=20, top_p=1.0,
+                                                                       repetition_penalty=1.3, seed=11)]
+    want, slot = [], 0
+    for i in range(16):
+        cfg = dict(cases[i % len(cases)])
+        if cfg.get("seed") == 7:
+            cfg["seed"] = 7 + i  # a new seed every call: reseeds
+        d = dlog(rng.standard_normal(V).astype(np.float32) * 3)
+        n = 40 if cfg.get("repetition_penalty", 1.0) != 1.0 else 0
+        want.append(a.sample(d, history=hist[:n] if n else (), **cfg))
+        b.sample_async(d, d_hist, n, tok[slot:slot + 1], **cfg)
+        slot += 1
+        torch.cuda.synchronize()
+    assert tok[:slot].cpu().tolist() == want
+    assert a.rng_state == b.rng_state
