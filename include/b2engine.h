@@ -296,6 +296,25 @@ int b2_model_create(const b2_model_config* cfg, int tp_rank, int tp_size, const 
                     b2_model** out);
 int b2_model_destroy(b2_model* m);
 
+/* A model shard whose KV cache is a paged block pool instead of one
+ * max_seq slab per sequence: per layer, K and V pools
+ * [num_blocks][block_size][kv heads of this rank][head_dim] half -- the
+ * physical block pool of the reference's paged runner contract
+ * (docs/runner_interface.md:18-84, block size 16 there) -- read through
+ * per-sequence block tables of physical block ids that the caller (the
+ * scheduler, sole owner of block allocation) passes with every call.
+ * head_dim 128 only (the tensor-core decode attention reads the pool; a
+ * 128-position tile is 128/block_size block boxes), block_size a multiple
+ * of 8 dividing 128.  A paged model takes b2_model_prefill_paged and
+ * b2_model_decode_step_paged; b2_model_prefill / _decode_step /
+ * _decode_enqueue / _forward_logits / _kv_layout return B2_ERR_STATE on it.
+ * cfg->max_seq bounds sequence lengths (block-table width
+ * ceil(max_seq / block_size)), cfg->max_batch the decode batch.  Allocates
+ * like b2_model_create.  New API (the reference runner is Python and not
+ * part of its C++ tree). */
+int b2_model_create_paged(const b2_model_config* cfg, int num_blocks, int block_size, int tp_rank, int tp_size,
+                          const void* nccl_id, b2_model** out);
+
 /* Tensor-parallel exchange over peer memory (one node, tp_size > 1).  Each
  * rank exports the 64-byte CUDA IPC handle of its exchange buffer; the
  * caller all-gathers the tp handles (rank order) with its own launcher and
@@ -351,6 +370,31 @@ int b2_model_prefill(b2_model* m, const int64_t* host_ids, int batch, int seq_le
  * first call. */
 int b2_model_decode_step(b2_model* m, const int64_t* host_tokens, const int* host_positions, int batch,
                          float* host_logits, int64_t* host_next);
+
+/* Paged prefill of one sequence (the runner's prefill(seq)): all seq_len
+ * prompt tokens at once; K/V of position p land in block
+ * host_block_table[p / block_size] (n_blocks entries, host int32), except
+ * positions below skip_blocks * block_size, whose blocks are shared and kept
+ * (prefix "share" mode: the prompt is recomputed, shared blocks are not
+ * overwritten).  first_token (may be NULL) receives the argmax of the last
+ * position, host_logits (may be NULL) its fp32 logits [vocab].  Synchronises.
+ * New API (docs/runner_interface.md:33-46). */
+int b2_model_prefill_paged(b2_model* m, const int64_t* host_ids, int seq_len, const int* host_block_table,
+                           int n_blocks, int skip_blocks, float* host_logits, int64_t* first_token);
+
+/* Paged decode step of `batch` sequences (the runner's decode_step(seqs)):
+ * sequence b consumes host_tokens[b] at position host_seq_lens[b] - 1 (the
+ * runner has already bumped its length to include this token), its K/V row
+ * goes to block host_block_tables[b * max_blocks + pos / block_size], and it
+ * attends over all host_seq_lens[b] positions through its table row (int32,
+ * unused slots padded with any valid id, e.g. 0).  host_logits ([batch,
+ * vocab]) and host_next (argmax ids) may be NULL.  The step runs as the
+ * captured graph of the batch size; the tables travel with each call, so
+ * sequences may join, leave and change blocks between steps.
+ * Synchronises.  New API (docs/runner_interface.md:48-72). */
+int b2_model_decode_step_paged(b2_model* m, const int64_t* host_tokens, const int* host_seq_lens,
+                               const int* host_block_tables, int max_blocks, int batch, float* host_logits,
+                               int64_t* host_next);
 
 /* Full forward over one sequence of `seq_len` host ids: fp32 logits of every
  * position into host_logits ([seq_len, vocab]).  Runs the batched prefill

@@ -81,6 +81,9 @@ _SIGS = {
     "b2_sampler_set_rng_state": (i32, [vp, u64]),
     "b2_nccl_unique_id": (i32, [vp]),
     "b2_model_create": (i32, [C.POINTER(ModelConfig), i32, i32, vp, C.POINTER(vp)]),
+    "b2_model_create_paged": (i32, [C.POINTER(ModelConfig), i32, i32, i32, i32, vp, C.POINTER(vp)]),
+    "b2_model_prefill_paged": (i32, [vp, vp, i32, vp, i32, i32, vp, vp]),
+    "b2_model_decode_step_paged": (i32, [vp, vp, vp, vp, i32, i32, vp, vp]),
     "b2_model_destroy": (i32, [vp]),
     "b2_model_init_random": (i32, [vp, u64, f32]),
     "b2_model_p2p_handle": (i32, [vp, vp]),
@@ -242,15 +245,23 @@ class Model:
     """A decode-path model shard (b2_model_*)."""
 
     def __init__(self, vocab, hidden, inter, layers, nq, nkv, head_dim, eps=1e-5, theta=10000.0, tied=False,
-                 bias=False, max_batch=1, max_seq=4096, tp_rank=0, tp_size=1, nccl_id: bytes | None = None):
+                 bias=False, max_batch=1, max_seq=4096, tp_rank=0, tp_size=1, nccl_id: bytes | None = None,
+                 kv_blocks: int = 0, block_size: int = 16):
+        """kv_blocks > 0 makes the KV cache a paged pool of kv_blocks blocks
+        of block_size positions (b2_model_create_paged)."""
         self.cfg = ModelConfig(vocab, hidden, inter, layers, nq, nkv, head_dim, eps, theta, int(tied), int(bias),
                                max_batch, max_seq)
         h = vp()
         idbuf = None
         if nccl_id is not None:
             idbuf = (C.c_char * 128).from_buffer_copy(nccl_id)
-        call("b2_model_create", C.byref(self.cfg), tp_rank, tp_size, C.cast(idbuf, vp) if idbuf else None, C.byref(h))
+        nid = C.cast(idbuf, vp) if idbuf else None
+        if kv_blocks > 0:
+            call("b2_model_create_paged", C.byref(self.cfg), kv_blocks, block_size, tp_rank, tp_size, nid, C.byref(h))
+        else:
+            call("b2_model_create", C.byref(self.cfg), tp_rank, tp_size, nid, C.byref(h))
         self.h = h
+        self.block_size = block_size if kv_blocks > 0 else 0
         self.vocab = vocab
         self._B = max_batch
 
@@ -351,6 +362,33 @@ class Model:
              nx.ctypes.data if nx is not None else None)
         return lg, nx
 
+    def prefill_paged(self, ids, block_table, skip_blocks=0, want_logits=False):
+        """One sequence's prompt into its blocks; returns (first token, logits or None)."""
+        import numpy as np
+        a = np.ascontiguousarray(np.asarray(ids, dtype=np.int64).reshape(-1))
+        bt = np.ascontiguousarray(np.asarray(block_table, dtype=np.int32).reshape(-1))
+        lg = np.empty(self.vocab, np.float32) if want_logits else None
+        nx = np.empty(1, np.int64)
+        call("b2_model_prefill_paged", self.h, a.ctypes.data, a.size, bt.ctypes.data, bt.size, skip_blocks,
+             lg.ctypes.data if lg is not None else None, nx.ctypes.data)
+        self._B = 1
+        return int(nx[0]), lg
+
+    def decode_step_paged(self, tokens, seq_lens, block_tables, want_logits=False):
+        """One step of len(tokens) sequences over the pool; block_tables is
+        [batch, max_blocks] int32.  Returns (next ids, logits [batch, vocab] or None)."""
+        import numpy as np
+        t = np.ascontiguousarray(np.asarray(tokens, dtype=np.int64).reshape(-1))
+        L = np.ascontiguousarray(np.asarray(seq_lens, dtype=np.int32).reshape(-1))
+        bt = np.ascontiguousarray(np.atleast_2d(np.asarray(block_tables, dtype=np.int32)))
+        B = t.size
+        lg = np.empty((B, self.vocab), np.float32) if want_logits else None
+        nx = np.empty(B, np.int64)
+        call("b2_model_decode_step_paged", self.h, t.ctypes.data, L.ctypes.data, bt.ctypes.data, bt.shape[1], B,
+             lg.ctypes.data if lg is not None else None, nx.ctypes.data)
+        self._B = B
+        return nx, lg
+
     def generate_greedy(self, steps: int, fetch=True):
         """Device-resident greedy loop continuing from the last prefill / step.
         fetch=True returns the ids [steps, batch] (synchronises); fetch=False
@@ -406,3 +444,73 @@ class Model:
             self.h = None
 
     __del__ = close
+
+
+# ---------------------------------------------------------------------------
+# paged-KV model runner
+# ---------------------------------------------------------------------------
+
+class PagedRunner:
+    """Model runner over a paged KV pool, with the contract of the reference
+    engine's runner (docs/runner_interface.md:18-84): the scheduler owns
+    block allocation and sequence bookkeeping; the runner never allocates or
+    frees blocks and only
+
+      prefill(seq)        runs the prompt, writes its K/V into the blocks of
+                          seq.block_table.physical_block_ids (skipping the
+                          first seq.num_cached_tokens // block_size blocks,
+                          which are shared), returns the first token id;
+      decode_step(seqs)   bumps seq.block_table.num_tokens by one for each
+                          sequence (the new K/V row goes to position
+                          num_tokens - 1), runs one step of the batch on
+                          seq.last_token_id, returns the next ids;
+      step(batch)         PREFILL (one sequence) or DECODE by batch.batch_type.
+
+    Sequences are duck-typed: .prompt_ids, .block_table (.physical_block_ids,
+    .num_tokens), .last_token_id, optional .num_cached_tokens; the runner
+    sets .last_logits and .last_logit_margin (top-1 minus top-2).  The
+    scheduler must have allocated a sequence's next block before a step that
+    crosses into it, and never hand a block shared with another sequence to a
+    decode write (both as in the contract)."""
+
+    PREFILL, DECODE = "prefill", "decode"
+
+    def __init__(self, model: Model):
+        if not model.block_size:
+            raise ValueError("PagedRunner needs a model created with kv_blocks > 0")
+        self.m = model
+        self.bs = model.block_size
+
+    @staticmethod
+    def _diag(seq, logits):
+        import numpy as np
+        seq.last_logits = logits
+        top = np.partition(logits, -2)[-2:]
+        seq.last_logit_margin = float(top[1] - top[0])
+
+    def prefill(self, seq, allocator=None) -> int:
+        bt = seq.block_table
+        skip = getattr(seq, "num_cached_tokens", 0) // self.bs
+        tok, lg = self.m.prefill_paged(seq.prompt_ids, bt.physical_block_ids, skip_blocks=skip, want_logits=True)
+        self._diag(seq, lg)
+        return tok
+
+    def decode_step(self, seqs, allocator=None) -> list:
+        import numpy as np
+        for s in seqs:
+            s.block_table.num_tokens += 1
+        width = max(len(s.block_table.physical_block_ids) for s in seqs)
+        tables = np.zeros((len(seqs), width), np.int32)
+        for i, s in enumerate(seqs):
+            ids = s.block_table.physical_block_ids
+            tables[i, :len(ids)] = ids
+        nx, lg = self.m.decode_step_paged([s.last_token_id for s in seqs],
+                                          [s.block_table.num_tokens for s in seqs], tables, want_logits=True)
+        for i, s in enumerate(seqs):
+            self._diag(s, lg[i])
+        return [int(x) for x in nx]
+
+    def step(self, batch) -> list:
+        if batch.batch_type == self.PREFILL:
+            return [self.prefill(batch.sequences[0])]
+        return self.decode_step(batch.sequences)

@@ -53,6 +53,10 @@ struct AttnTcParams {
     const __half* kp;  // the cache views as pointers (the newest row is copied in directly)
     const __half* vp;
     int64_t sb, sh, ss;
+    // paged cache (bt != null): block tables [B][maxb] of bs-position blocks,
+    // pools [num_blocks][bs][nkv][128]; the tensor maps then cover one block
+    const int* bt;
+    int maxb, bs;
     int* err;
     TraceSlot trace;
 };
@@ -188,6 +192,24 @@ __global__ void __launch_bounds__(192, 1) attn_tc_kernel(const __grid_constant__
                 const int pos0 = start + i * kAtP;
                 uint8_t* st = ring + (size_t)s * kAtStage;
                 tc::mbar_arrive_expect_tx(&kv_full[s], kAtStage);
+                if (p.bt) {
+                    // one box per (block, 64-column atom): rows of block j of
+                    // the tile land at row 16j.. of the swizzled tile (a
+                    // block is a whole number of 8-row swizzle atoms); table
+                    // slots past the sequence's blocks read block 0 (masked)
+                    const int nblk = kAtP / p.bs;
+                    for (int j = 0; j < nblk; ++j) {
+                        const int lb = pos0 / p.bs + j;
+                        const int phys = lb < p.maxb ? p.bt[(int64_t)b * p.maxb + lb] : 0;
+#pragma unroll
+                        for (int a = 0; a < 2; ++a) {
+                            const uint32_t off = a * kAtAtom + (uint32_t)(j * p.bs) * 128u;
+                            tc::tma_load_4d(st + off, &tmK, &kv_full[s], a * 64, kvh, 0, phys);
+                            tc::tma_load_4d(st + kAtKV + off, &tmV, &kv_full[s], a * 64, kvh, 0, phys);
+                        }
+                    }
+                    continue;
+                }
 #pragma unroll
                 for (int a = 0; a < 2; ++a) {
                     if (p.head_inner) {
@@ -208,8 +230,10 @@ __global__ void __launch_bounds__(192, 1) attn_tc_kernel(const __grid_constant__
             const bool ok = __all_sync(0xffffffffu, tc::mbar_wait(&kv_full[s], (uint32_t)(i / kAtStages) & 1u, p.err, 79));
             if (ok) {
                 const int c = lane & 15;  // 16-byte chunk of the K (lanes 0-15) or V (16-31) row
-                const __half* src = (lane < 16 ? p.kp : p.vp) + (int64_t)b * p.sb + (int64_t)kvh * p.sh +
-                                    (int64_t)(L - 1) * p.ss + c * 8;
+                const int64_t at = p.bt ? (((int64_t)p.bt[(int64_t)b * p.maxb + (L - 1) / p.bs] * p.bs + (L - 1) % p.bs) *
+                                               p.nkv + kvh) * kAtD
+                                        : (int64_t)b * p.sb + (int64_t)kvh * p.sh + (int64_t)(L - 1) * p.ss;
+                const __half* src = (lane < 16 ? p.kp : p.vp) + at + c * 8;
                 uint8_t* dst = ring + (size_t)s * kAtStage + (lane < 16 ? 0u : kAtKV) + (uint32_t)(c >> 3) * kAtAtom +
                                (uint32_t)row * 128u + ((((uint32_t)c & 7u) ^ ((uint32_t)row & 7u)) << 4);
                 *reinterpret_cast<uint4*>(dst) = __ldcg(reinterpret_cast<const uint4*>(src));
@@ -539,6 +563,63 @@ int attn_tc_launch(const __half* q, int64_t q_sb, __half* out, int64_t o_sb, con
     // one wave instead of 1.7 waves of one CTA per SM (batch 32, ctx 512:
     // 24.6 vs 28.7 us).  Long contexts keep the deeper ring (ctx 32K: 638
     // vs 692 us).
+    const long ctas = (long)cs * B * nkv * p.hg;
+    const bool many = ctas > sm_count() && max_len <= 8192;
+    const int stages = many ? 1 : (!lean ? 3 : ((max_len + cs - 1) / cs <= kAtP ? 1 : 2));
+    if (G == 4) {
+        if (stages == 1) return launch_tc_g<4, 1>(tk, tv, p, cs, B, s, pdl);
+        if (stages == 2) return launch_tc_g<4, 2>(tk, tv, p, cs, B, s, pdl);
+        return launch_tc_g<4, 3>(tk, tv, p, cs, B, s, pdl);
+    }
+    if (stages == 1) return launch_tc_g<8, 1>(tk, tv, p, cs, B, s, pdl);
+    if (stages == 2) return launch_tc_g<8, 2>(tk, tv, p, cs, B, s, pdl);
+    return launch_tc_g<8, 3>(tk, tv, p, cs, B, s, pdl);
+}
+
+// Paged form: K / V pools [num_blocks][bs][nkv][128], block tables [B][maxb]
+// (bs a multiple of 8 dividing 128), sequence lengths seq_lens[B] <=
+// max_len.  Same kernel; the producer fetches each 128-position tile as
+// 128/bs block boxes.
+int attn_tc_launch_paged(const __half* q, int64_t q_sb, __half* out, int64_t o_sb, const __half* kpool,
+                         const __half* vpool, int num_blocks, int bs, const int* bt, int maxb, int max_len,
+                         const int* seq_lens, int B, int nq, int nkv, int D, int early_kv, int lean, TraceSlot trace,
+                         cudaStream_t s, bool pdl) {
+    if (D != kAtD || max_len < 1 || B < 1 || B > 65535 || num_blocks < 1 || maxb < 1 || !bt) return B2_ERR_UNSUPPORTED;
+    if (bs < 8 || (bs & 7) || kAtP % bs) return B2_ERR_UNSUPPORTED;
+    if (!aligned16(kpool) || !aligned16(vpool) || !aligned16(q) || (q_sb & 7)) return B2_ERR_UNSUPPORTED;
+    int* err = wait_error_word();
+    if (!err) return B2_ERR_STATE;
+    const int group = nq / nkv;
+    const int G = group <= 4 ? 4 : 8;
+    AttnTcParams p = {};
+    p.q = q;
+    p.q_sb = q_sb;
+    p.out = out;
+    p.o_sb = o_sb;
+    p.seq_lens = seq_lens;
+    p.nq = nq;
+    p.nkv = nkv;
+    p.group = group;
+    p.hg = (group + G - 1) / G;
+    p.scale_log2 = 1.4426950408889634f / sqrtf((float)D);
+    p.early_kv = early_kv;
+    p.kp = kpool;
+    p.vp = vpool;
+    p.bt = bt;
+    p.maxb = maxb;
+    p.bs = bs;
+    p.err = err;
+    p.trace = trace;
+    // (128 columns, head, slot, block): box 64 x 1 x bs x 1
+    const uint64_t dims[4] = {(uint64_t)D, (uint64_t)nkv, (uint64_t)bs, (uint64_t)num_blocks};
+    const uint64_t st[3] = {(uint64_t)D * 2, (uint64_t)nkv * D * 2, (uint64_t)bs * nkv * D * 2};
+    const uint32_t box[4] = {64u, 1u, (uint32_t)bs, 1u};
+    CUtensorMap tk, tv;
+    int rc = make_tensor_map(&tk, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 4, kpool, dims, st, box);
+    if (rc != B2_OK) return rc;
+    rc = make_tensor_map(&tv, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 4, vpool, dims, st, box);
+    if (rc != B2_OK) return rc;
+    const int cs = attn_tc_splits(B, nkv, p.hg, max_len);
     const long ctas = (long)cs * B * nkv * p.hg;
     const bool many = ctas > sm_count() && max_len <= 8192;
     const int stages = many ? 1 : (!lean ? 3 : ((max_len + cs - 1) / cs <= kAtP ? 1 : 2));

@@ -129,6 +129,29 @@ __device__ __forceinline__ void trace_end(const TraceSlot& tr) {
     if (tr.buf && threadIdx.x == 0) atomicMax(tr.buf + 2 * tr.slot + 1, globaltimer_ns());
 }
 
+// Where one layer's K and V rows live.  Contiguous: element d of (sequence
+// b, kv head h, position pos) at base + b*sb + h*sh + pos*D + d (the model's
+// [batch][K|V][head][max_seq][D] cache).  Paged (bt != null): block tables
+// [B][maxb] of physical blocks of `bs` positions, a block's rows stored
+// [slot][head][D], so the row is at base + ((bt[b][pos/bs]*bs + pos%bs)*nkv
+// + h)*D -- the pool layout [num_blocks][block_size][kv_heads][head_dim] of
+// the reference's paged runner contract.
+struct KvLayout {
+    __half* k;
+    __half* v;
+    int64_t sb, sh;
+    const int* bt;
+    int maxb, bs, nkv;
+};
+
+__device__ __forceinline__ int64_t kv_row(const KvLayout& L, int b, int h, int pos, int D) {
+    if (L.bt) {
+        const int blk = L.bt[(int64_t)b * L.maxb + pos / L.bs];
+        return (((int64_t)blk * L.bs + pos % L.bs) * L.nkv + h) * D;
+    }
+    return (int64_t)b * L.sb + (int64_t)h * L.sh + (int64_t)pos * D;
+}
+
 // 16-byte streaming load that bypasses L1 allocation (weights are read once).
 __device__ __forceinline__ uint4 ldg_stream(const void* p) {
     uint4 r;

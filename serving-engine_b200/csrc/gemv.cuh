@@ -104,9 +104,7 @@ struct GemvParams {
     int nq, nkv, D;
     const float2* rope;  // [max_pos, D/2] (cos, sin)
     const int* pos;      // [B] positions of the new token
-    __half* kcache;      // this layer's K base: + b*kv_sb + h*kv_sh + pos*D
-    __half* vcache;
-    int64_t kv_sb, kv_sh;
+    KvLayout kv;         // this layer's K / V rows
 
     // OUT_LOGITS
     unsigned long long* argmax;  // [B] packed (value, id), 0 before the launch

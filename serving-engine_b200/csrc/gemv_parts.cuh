@@ -314,12 +314,12 @@ __device__ __forceinline__ void task_epilogue(const GemvParams& p, int t, const 
                     q[i] = __float2half_rn(o1);
                     q[i + half] = __float2half_rn(o2);
                 } else {
-                    __half* k = p.kcache + b * p.kv_sb + (int64_t)(h - p.nq) * p.kv_sh + (int64_t)pos * p.D;
+                    __half* k = p.kv.k + kv_row(p.kv, b, h - p.nq, pos, p.D);
                     k[i] = __float2half_rn(o1);
                     k[i + half] = __float2half_rn(o2);
                 }
             } else {
-                __half* v = p.vcache + b * p.kv_sb + (int64_t)(h - p.nq - p.nkv) * p.kv_sh + (int64_t)pos * p.D;
+                __half* v = p.kv.v + kv_row(p.kv, b, h - p.nq - p.nkv, pos, p.D);
                 v[i] = __float2half_rn(x1);
                 v[i + half] = __float2half_rn(x2);
             }

@@ -63,6 +63,10 @@ int attn_decode_launch_step_q(const __half* q, int64_t q_sb, const __half* kbase
                               int64_t sh, int64_t ss, const int* seq_lens, __half* out, float* part, int splits,
                               int B, int nq, int nkv, int D, cudaStream_t s);
 int* wait_error_word();
+int attn_tc_launch_paged(const __half* q, int64_t q_sb, __half* out, int64_t o_sb, const __half* kpool,
+                         const __half* vpool, int num_blocks, int bs, const int* bt, int maxb, int max_len,
+                         const int* seq_lens, int B, int nq, int nkv, int D, int early_kv, int lean, TraceSlot trace,
+                         cudaStream_t s, bool pdl);
 int attn_cl_launch(const __half* q, int64_t q_sb, __half* out, int64_t o_sb, const __half* k, const __half* v,
                    int64_t sb, int64_t sh, int64_t ss, int max_len, const int* seq_lens, int len_const, int B,
                    int nq, int nkv, int D, int early_kv, int lean, TraceSlot trace, cudaStream_t s, bool pdl);
@@ -246,8 +250,8 @@ __global__ void rmsnorm_rows_kernel(const float* __restrict__ hidden, const __ha
 // in place, and K / V of every token written into this layer's cache.
 // grid (T, nq + 2 nkv), D/2 threads.
 __global__ void rope_append_kernel(__half* __restrict__ qkv, int64_t ld, const float2* __restrict__ rope, int S,
-                                   int nq, int nkv, int D, __half* __restrict__ kcache, __half* __restrict__ vcache,
-                                   int64_t kv_sb, int64_t kv_sh, const int* __restrict__ positions) {
+                                   int nq, int nkv, int D, const KvLayout kv, int skip_pos,
+                                   const int* __restrict__ positions) {
     griddep_wait();
     const int64_t t = blockIdx.x;
     // prefill: row t is position t % S of sequence t / S; decode (positions
@@ -263,13 +267,13 @@ __global__ void rope_append_kernel(__half* __restrict__ qkv, int64_t ld, const f
         const float o2 = x2 * cs.x + x1 * cs.y;
         row[i] = __float2half_rn(o1);
         row[i + half] = __float2half_rn(o2);
-        if (head >= nq) {
-            __half* k = kcache + b * kv_sb + (int64_t)(head - nq) * kv_sh + (int64_t)pos * D;
+        if (head >= nq && pos >= skip_pos) {
+            __half* k = kv.k + kv_row(kv, b, head - nq, pos, D);
             k[i] = __float2half_rn(o1);
             k[i + half] = __float2half_rn(o2);
         }
-    } else {
-        __half* v = vcache + b * kv_sb + (int64_t)(head - nq - nkv) * kv_sh + (int64_t)pos * D;
+    } else if (pos >= skip_pos) {
+        __half* v = kv.v + kv_row(kv, b, head - nq - nkv, pos, D);
         v[i] = row[i];
         v[i + half] = row[i + half];
     }
@@ -335,8 +339,7 @@ __device__ __forceinline__ float sk_sum(const SkSlabs& a, int B, int b, int n) {
 // i+D/2..); grid (B, ceil((nq + 2 nkv) D/8 / 256)), 256 threads.
 __global__ void sk_qkv_rope_kernel(SkSlabs a, int B, const __half* __restrict__ bias, __half* __restrict__ qkv,
                                    int64_t ld, const float2* __restrict__ rope, int nq, int nkv, int D,
-                                   __half* __restrict__ kcache, __half* __restrict__ vcache, int64_t kv_sb,
-                                   int64_t kv_sh, const int* __restrict__ positions) {
+                                   const KvLayout kv, const int* __restrict__ positions) {
     griddep_wait();
     griddep_launch_dependents();
     const int b = blockIdx.x, half = D >> 1, per_head = D >> 3;
@@ -367,8 +370,8 @@ __global__ void sk_qkv_rope_kernel(SkSlabs a, int B, const __half* __restrict__ 
     }
     __half* dst;
     if (head < nq) dst = qkv + (int64_t)b * ld + (int64_t)head * D;
-    else if (head < nq + nkv) dst = kcache + b * kv_sb + (int64_t)(head - nq) * kv_sh + (int64_t)pos * D;
-    else dst = vcache + b * kv_sb + (int64_t)(head - nq - nkv) * kv_sh + (int64_t)pos * D;
+    else if (head < nq + nkv) dst = kv.k + kv_row(kv, b, head - nq, pos, D);
+    else dst = kv.v + kv_row(kv, b, head - nq - nkv, pos, D);
     __half2 p0 = __halves2half2(o1[0], o1[1]), p1 = __halves2half2(o1[2], o1[3]);
     __half2 q0 = __halves2half2(o2[0], o2[1]), q1 = __halves2half2(o2[2], o2[3]);
     uint2 w1, w2;
@@ -562,6 +565,11 @@ struct b2_model {
 
     __half* kv = nullptr;
     int64_t kv_s_layer = 0, kv_s_batch = 0, kv_s_kv = 0, kv_s_head = 0;
+    // paged KV (b2_model_create_paged): pool [layer][K|V][block][slot][kv head][D]
+    // and device block tables [max_batch][kv_maxb]
+    int paged = 0, kv_blocks = 0, kv_bs = 0, kv_maxb = 0;
+    int* block_tables = nullptr;
+    int* h_bt = nullptr;  // pinned staging of the block tables
     float2* rope = nullptr;
 
     float* hidden = nullptr;
@@ -684,13 +692,28 @@ extern "C" int b2_model_destroy(b2_model* m) {
     cudaFreeHost(m->h_pos);
     cudaFreeHost(m->h_argmax);
     cudaFreeHost(m->h_logits);
+    cudaFreeHost(m->h_bt);
     if (m->stream) cudaStreamDestroy(m->stream);
     delete m;
     return B2_OK;
 }
 
+static int model_create(const b2_model_config* cfg, int tp_rank, int tp_size, const void* nccl_id, int num_blocks,
+                        int block_size, b2_model** out);
+
 extern "C" int b2_model_create(const b2_model_config* cfg, int tp_rank, int tp_size, const void* nccl_id,
                                b2_model** out) {
+    return model_create(cfg, tp_rank, tp_size, nccl_id, 0, 0, out);
+}
+
+extern "C" int b2_model_create_paged(const b2_model_config* cfg, int num_blocks, int block_size, int tp_rank,
+                                     int tp_size, const void* nccl_id, b2_model** out) {
+    B2_REQUIRE(num_blocks >= 1 && block_size >= 1);
+    return model_create(cfg, tp_rank, tp_size, nccl_id, num_blocks, block_size, out);
+}
+
+static int model_create(const b2_model_config* cfg, int tp_rank, int tp_size, const void* nccl_id, int num_blocks,
+                        int block_size, b2_model** out) {
     B2_REQUIRE(cfg && out && tp_size >= 1 && tp_rank >= 0 && tp_rank < tp_size);
     *out = nullptr;
     const b2_model_config& c = *cfg;
@@ -702,6 +725,10 @@ extern "C" int b2_model_create(const b2_model_config* cfg, int tp_rank, int tp_s
         (c.num_q_heads / tp_size * c.head_dim) % 8)
         return B2_ERR_UNSUPPORTED;
     if (tp_size > 1 && !nccl_id) return B2_ERR_INVALID;
+    // the paged cache is read by the tensor-core attention (head_dim 128), one
+    // 128-position tile as whole blocks of whole 8-row swizzle atoms
+    if (num_blocks > 0 && (c.head_dim != 128 || block_size < 8 || (block_size & 7) || 128 % block_size))
+        return B2_ERR_UNSUPPORTED;
 
     b2_model* m = new (std::nothrow) b2_model();
     if (!m) return B2_ERR_INVALID;
@@ -763,11 +790,26 @@ extern "C" int b2_model_create(const b2_model_config* cfg, int tp_rank, int tp_s
         M_ALLOC(w.ln1, (size_t)H * hs);
         M_ALLOC(w.ln2, (size_t)H * hs);
     }
-    // KV cache [layer][batch][K/V][kv head][max_seq][D]
-    m->kv_s_head = (int64_t)c.max_seq * D;
-    m->kv_s_kv = m->kv_s_head * m->nkv;
-    m->kv_s_batch = m->kv_s_kv * 2;
-    m->kv_s_layer = m->kv_s_batch * B;
+    if (num_blocks > 0) {
+        // paged: pool [layer][K/V][block][slot][kv head][D], block tables
+        // [max_batch][blocks per sequence at max_seq]
+        m->paged = 1;
+        m->kv_blocks = num_blocks;
+        m->kv_bs = block_size;
+        m->kv_maxb = (c.max_seq + block_size - 1) / block_size;
+        m->kv_s_kv = (int64_t)num_blocks * block_size * m->nkv * D;
+        m->kv_s_layer = 2 * m->kv_s_kv;
+        M_ALLOC(m->block_tables, (size_t)B * m->kv_maxb * sizeof(int));
+        cudaError_t e = cudaMemset(m->block_tables, 0, (size_t)B * m->kv_maxb * sizeof(int));
+        if (e == cudaSuccess) e = cudaMallocHost(&m->h_bt, (size_t)B * m->kv_maxb * sizeof(int));
+        if (e != cudaSuccess) { b2_model_destroy(m); return (int)e; }
+    } else {
+        // KV cache [layer][batch][K/V][kv head][max_seq][D]
+        m->kv_s_head = (int64_t)c.max_seq * D;
+        m->kv_s_kv = m->kv_s_head * m->nkv;
+        m->kv_s_batch = m->kv_s_kv * 2;
+        m->kv_s_layer = m->kv_s_batch * B;
+    }
     M_ALLOC(m->kv, (size_t)m->kv_s_layer * L * hs);
     {
         cudaError_t e = cudaMemset(m->kv, 0, (size_t)m->kv_s_layer * L * hs);
@@ -1109,10 +1151,26 @@ static void set_exchange(b2_model* m, GemvParams& p, int slot, const float* hin,
     p.hid_out = hout;
 }
 
+// Layer l's K / V rows: the contiguous cache or the paged pool.
+static KvLayout layer_kv(const b2_model* m, int l) {
+    KvLayout k = {};
+    k.k = m->kv + (int64_t)l * m->kv_s_layer;
+    k.v = k.k + m->kv_s_kv;
+    if (m->paged) {
+        k.bt = m->block_tables;
+        k.maxb = m->kv_maxb;
+        k.bs = m->kv_bs;
+        k.nkv = m->nkv;
+    } else {
+        k.sb = m->kv_s_batch;
+        k.sh = m->kv_s_head;
+    }
+    return k;
+}
+
 static int launch_qkv(b2_model* m, int l, int B, bool pdl, bool xch = false) {
     const b2_model_config& c = m->cfg;
     LayerW& w = m->layers[l];
-    __half* kbase = m->kv + (int64_t)l * m->kv_s_layer;
     GemvParams p = {};
     p.trace = next_trace(m);
     p.W = w.wqkv;
@@ -1131,10 +1189,7 @@ static int launch_qkv(b2_model* m, int l, int B, bool pdl, bool xch = false) {
     p.D = c.head_dim;
     p.rope = m->rope;
     p.pos = m->positions;
-    p.kcache = kbase;
-    p.vcache = kbase + m->kv_s_kv;
-    p.kv_sb = m->kv_s_batch;
-    p.kv_sh = m->kv_s_head;
+    p.kv = layer_kv(m, l);
     if (xch && l > 0) {
         set_exchange(m, p, 2 * (l - 1) + 1, m->hidden2, m->hidden);
         p.x = m->hidden2;
@@ -1143,12 +1198,21 @@ static int launch_qkv(b2_model* m, int l, int B, bool pdl, bool xch = false) {
     return gemv_launch(p, X_NORM, OUT_QKV, m->stream, pdl);
 }
 
+// Decode attention of layer l over the paged pool (q rows q_sb apart).
+static int launch_attn_paged(b2_model* m, int l, const __half* q, int64_t q_sb, int B, int lean, TraceSlot tr) {
+    const KvLayout kv = layer_kv(m, l);
+    const int D = m->cfg.head_dim, qd = m->nq * D;
+    return attn_tc_launch_paged(q, q_sb, m->attn, qd, kv.k, kv.v, m->kv_blocks, m->kv_bs, m->block_tables, m->kv_maxb,
+                                m->cfg.max_seq, m->seq_lens, B, m->nq, m->nkv, D, 1, lean, tr, m->stream, true);
+}
+
 static int launch_attn(b2_model* m, int l, int B, bool pdl) {
     (void)pdl;  // the step form always uses programmatic launch
     const int D = m->cfg.head_dim;
     __half* kbase = m->kv + (int64_t)l * m->kv_s_layer;
     const TraceSlot tr = next_trace(m);
     const int qd = m->nq * D;
+    if (m->paged) return launch_attn_paged(m, l, m->q, qd, B, 1, tr);
     const int rc = attn_cl_launch(m->q, qd, m->attn, qd, kbase, kbase + m->kv_s_kv, m->kv_s_batch, m->kv_s_head, D,
                                   m->cfg.max_seq, m->seq_lens, 0, B, m->nq, m->nkv, D, 1, 1, tr, m->stream, true);
     if (rc != B2_ERR_UNSUPPORTED) return rc;
@@ -1324,8 +1388,10 @@ static int enqueue_step_batched(b2_model* m, int B) {
         const unsigned qkv_threads = (unsigned)((m->nq + 2 * m->nkv) * (D / 8));
         B2_TRY(launch(sk_qkv_rope_kernel, dim3((unsigned)B, (qkv_threads + 255) / 256), dim3(256), 0, s, true,
                       qkv, B, (const __half*)w.bqkv, m->bqkv, (int64_t)R, (const float2*)m->rope, m->nq, m->nkv, D,
-                      kbase, kbase + m->kv_s_kv, m->kv_s_batch, m->kv_s_head, (const int*)m->positions));
-        {
+                      layer_kv(m, l), (const int*)m->positions));
+        if (m->paged) {
+            M_TRY(launch_attn_paged(m, l, m->bqkv, R, B, 0, TraceSlot{nullptr, 0}));
+        } else {
             const int rc = attn_cl_launch(m->bqkv, R, m->attn, qd, kbase, kbase + m->kv_s_kv, m->kv_s_batch,
                                           m->kv_s_head, D, c.max_seq, m->seq_lens, 0, B, m->nq, m->nkv, D, 1, 0,
                                           TraceSlot{nullptr, 0}, s, true);
@@ -1489,6 +1555,7 @@ static int read_next(b2_model* m, int B, int64_t* host_next) {
 extern "C" int b2_model_decode_step(b2_model* m, const int64_t* host_tokens, const int* host_positions, int B,
                                     float* host_logits, int64_t* host_next) {
     B2_REQUIRE(m && host_tokens && host_positions && B >= 1 && B <= m->cfg.max_batch);
+    if (m->paged) return B2_ERR_STATE;
     for (int b = 0; b < B; ++b) {
         if (host_positions[b] < 0 || host_positions[b] >= m->cfg.max_seq) return B2_ERR_INVALID;
         if (host_tokens[b] < 0 || host_tokens[b] >= m->cfg.vocab_size) return B2_ERR_INVALID;
@@ -1508,6 +1575,7 @@ extern "C" int b2_model_decode_step(b2_model* m, const int64_t* host_tokens, con
 extern "C" int b2_model_decode_enqueue(b2_model* m, const int64_t* host_tokens, const int* host_positions, int B,
                                        float* d_logits) {
     B2_REQUIRE(m && host_tokens && host_positions && B >= 1 && B <= m->cfg.max_batch);
+    if (m->paged) return B2_ERR_STATE;
     if (d_logits && m->tp != 1) return B2_ERR_UNSUPPORTED;
     StepInputs in;
     for (int b = 0; b < B; ++b) {
@@ -1558,7 +1626,7 @@ static int nccl_sum_rows(b2_model* m, float* buf, int64_t rows) {
 // GEMMs for every projection, the tensor-core flash prefill for attention,
 // K/V written into the cache, then the lm_head (with argmax) of each
 // sequence's last position through the decode GEMV.
-static int prefill_batched(b2_model* m, int B, int S) {
+static int prefill_batched(b2_model* m, int B, int S, int skip_pos = 0) {
     const b2_model_config& c = m->cfg;
     cudaStream_t st = m->stream;
     const int64_t T = (int64_t)B * S;
@@ -1569,14 +1637,12 @@ static int prefill_batched(b2_model* m, int B, int S) {
     const int norm_threads = H >= 1024 ? 256 : 128;
     for (int l = 0; l < c.num_layers; ++l) {
         LayerW& w = m->layers[l];
-        __half* kbase = m->kv + (int64_t)l * m->kv_s_layer;
         rmsnorm_rows_kernel<<<(unsigned)T, norm_threads, 0, st>>>(m->pf_hidden, w.ln1, m->pf_xn, H, c.rms_norm_eps);
         B2_CHECK_LAUNCH();
         M_TRY(gemm_tc(m->pf_xn, w.wqkv, m->pf_qkv, rows, m->qkv_rows, H, TC_HALF, st));
         if (w.bqkv) M_TRY(b2_bias_add(m->pf_qkv, w.bqkv, m->pf_qkv, T, m->qkv_rows, st));
         rope_append_kernel<<<dim3((unsigned)T, (unsigned)(m->nq + 2 * m->nkv)), D / 2, 0, st>>>(
-            m->pf_qkv, m->qkv_rows, m->rope, S, m->nq, m->nkv, D, kbase, kbase + m->kv_s_kv, m->kv_s_batch,
-            m->kv_s_head, nullptr);
+            m->pf_qkv, m->qkv_rows, m->rope, S, m->nq, m->nkv, D, layer_kv(m, l), skip_pos, nullptr);
         B2_CHECK_LAUNCH();
         FlashArgs fa = {};
         fa.q = m->pf_qkv;
@@ -1626,6 +1692,7 @@ static int prefill_batched(b2_model* m, int B, int S) {
 
 extern "C" int b2_model_prefill(b2_model* m, const int64_t* host_ids, int B, int S, float* host_logits) {
     B2_REQUIRE(m && host_ids && B >= 1 && B <= m->cfg.max_batch && S >= 1 && S <= m->cfg.max_seq);
+    if (m->paged) return B2_ERR_STATE;
     for (int64_t i = 0; i < (int64_t)B * S; ++i)
         if (host_ids[i] < 0 || host_ids[i] >= m->cfg.vocab_size) return B2_ERR_INVALID;
     M_TRY(ensure_prefill_ws(m, (int64_t)B * S));
@@ -1638,8 +1705,74 @@ extern "C" int b2_model_prefill(b2_model* m, const int64_t* host_ids, int B, int
     return B2_OK;
 }
 
+// Copy B block-table rows (host, max_blocks wide) into the device tables
+// (kv_maxb wide, zero-padded), checking the entries every sequence of
+// lens[b] positions uses.
+static int upload_block_tables(b2_model* m, const int* host_bt, int max_blocks, int B, const int* lens) {
+    for (int b = 0; b < B; ++b) {
+        const int used = (lens[b] + m->kv_bs - 1) / m->kv_bs;
+        if (used > max_blocks || used > m->kv_maxb) return B2_ERR_INVALID;
+        for (int j = 0; j < used; ++j) {
+            const int blk = host_bt[(int64_t)b * max_blocks + j];
+            if (blk < 0 || blk >= m->kv_blocks) return B2_ERR_INVALID;
+        }
+        int* row = m->h_bt + (int64_t)b * m->kv_maxb;
+        const int w = max_blocks < m->kv_maxb ? max_blocks : m->kv_maxb;
+        for (int j = 0; j < m->kv_maxb; ++j) {
+            int v = j < w ? host_bt[(int64_t)b * max_blocks + j] : 0;
+            row[j] = (v >= 0 && v < m->kv_blocks) ? v : 0;  // padding slots read a valid block, masked
+        }
+    }
+    B2_TRY(cudaMemcpyAsync(m->block_tables, m->h_bt, (size_t)B * m->kv_maxb * sizeof(int), cudaMemcpyHostToDevice,
+                           m->stream));
+    return B2_OK;
+}
+
+extern "C" int b2_model_prefill_paged(b2_model* m, const int64_t* host_ids, int S, const int* host_block_table,
+                                      int n_blocks, int skip_blocks, float* host_logits, int64_t* first_token) {
+    B2_REQUIRE(m && host_ids && host_block_table && S >= 1 && S <= m->cfg.max_seq && n_blocks >= 1 &&
+               skip_blocks >= 0);
+    if (!m->paged) return B2_ERR_STATE;
+    for (int64_t i = 0; i < S; ++i)
+        if (host_ids[i] < 0 || host_ids[i] >= m->cfg.vocab_size) return B2_ERR_INVALID;
+    M_TRY(upload_block_tables(m, host_block_table, n_blocks, 1, &S));
+    M_TRY(ensure_prefill_ws(m, S));
+    B2_TRY(cudaMemcpyAsync(m->pf_ids, host_ids, (size_t)S * sizeof(int64_t), cudaMemcpyHostToDevice, m->stream));
+    B2_TRY(cudaMemsetAsync(m->hist_count, 0, sizeof(int), m->stream));
+    M_TRY(prefill_batched(m, 1, S, skip_blocks * m->kv_bs));
+    m->last_B = 1;
+    if (host_logits) M_TRY(copy_logits_out(m, 1, host_logits));
+    if (first_token) M_TRY(read_next(m, 1, first_token));
+    B2_TRY(cudaStreamSynchronize(m->stream));
+    return B2_OK;
+}
+
+extern "C" int b2_model_decode_step_paged(b2_model* m, const int64_t* host_tokens, const int* host_seq_lens,
+                                          const int* host_block_tables, int max_blocks, int B, float* host_logits,
+                                          int64_t* host_next) {
+    B2_REQUIRE(m && host_tokens && host_seq_lens && host_block_tables && max_blocks >= 1 && B >= 1 &&
+               B <= m->cfg.max_batch);
+    if (!m->paged) return B2_ERR_STATE;
+    for (int b = 0; b < B; ++b) {
+        if (host_seq_lens[b] < 1 || host_seq_lens[b] > m->cfg.max_seq) return B2_ERR_INVALID;
+        if (host_tokens[b] < 0 || host_tokens[b] >= m->cfg.vocab_size) return B2_ERR_INVALID;
+    }
+    M_TRY(upload_block_tables(m, host_block_tables, max_blocks, B, host_seq_lens));
+    memcpy(m->h_tokens, host_tokens, (size_t)B * sizeof(int64_t));
+    for (int b = 0; b < B; ++b) m->h_pos[b] = host_seq_lens[b] - 1;  // the new token's position
+    B2_TRY(cudaMemcpyAsync(m->tokens, m->h_tokens, (size_t)B * sizeof(int64_t), cudaMemcpyHostToDevice, m->stream));
+    B2_TRY(cudaMemcpyAsync(m->positions, m->h_pos, (size_t)B * sizeof(int), cudaMemcpyHostToDevice, m->stream));
+    M_TRY(run_step(m, B));
+    m->last_B = B;
+    if (host_logits) M_TRY(copy_logits_out(m, B, host_logits));
+    if (host_next) M_TRY(read_next(m, B, host_next));
+    B2_TRY(cudaStreamSynchronize(m->stream));
+    return B2_OK;
+}
+
 extern "C" int b2_model_forward_logits(b2_model* m, const int64_t* host_ids, int S, float* host_logits) {
     B2_REQUIRE(m && host_ids && host_logits && S >= 1 && S <= m->cfg.max_seq);
+    if (m->paged) return B2_ERR_STATE;
     if (m->tp != 1) return B2_ERR_UNSUPPORTED;
     const b2_model_config& c = m->cfg;
     for (int64_t i = 0; i < S; ++i)
@@ -1716,6 +1849,7 @@ extern "C" int b2_model_read(b2_model* m, const char* name, void* dst, size_t of
 
 extern "C" int b2_model_kv_layout(const b2_model* m, int64_t* sl, int64_t* sb, int64_t* skv, int64_t* sh, int64_t* sp) {
     B2_REQUIRE(m && sl && sb && skv && sh && sp);
+    if (m->paged) return B2_ERR_STATE;
     *sl = m->kv_s_layer;
     *sb = m->kv_s_batch;
     *skv = m->kv_s_kv;
