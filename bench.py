@@ -66,6 +66,7 @@ def model_cfg(args):
         c["layers"] = args.layers
     return c
 PROMPT = 512
+PAGE = 16  # KV block size of the paged mode (the reference runner's default)
 SEED_W, SEED_P = 1234, 42
 FALLBACK_HBM = 6650.0
 
@@ -246,8 +247,14 @@ def run_reference(args, rank, world):
 
 def config_dict(args, world):
     c = model_cfg(args)
-    return {"workload": f"{args.model}-shaped decode, batch {args.batch}, {args.prompt}-token prompt then "
-                        f"{args.warmup}+{args.steps} decode steps",
+    if args.paged:
+        wl = (f"{args.model}-shaped decode over a paged KV cache ({PAGE}-position blocks scattered over a pool), "
+              f"batch {args.batch}, prompts of {args.prompt // 2}..{args.prompt * 3 // 2} tokens (mixed), then "
+              f"{args.warmup}+{args.steps} decode steps")
+    else:
+        wl = (f"{args.model}-shaped decode, batch {args.batch}, {args.prompt}-token prompt then "
+              f"{args.warmup}+{args.steps} decode steps")
+    return {"workload": wl,
             "model": f"{args.model}-shape random-init (H{c['hidden']} L{c['layers']} {c['nq']}/{c['nkv']} heads "
                      f"D{c['head_dim']} FFN{c['inter']} V{c['vocab']}, theta {c['theta']:g})",
             "global_batch": args.batch, "prompt_len": args.prompt,
@@ -347,11 +354,14 @@ def run_b2(args, rank, world, local):
         dist.broadcast_object_list(obj, src=0)
         nccl_id = obj[0]
     B, K, W = args.batch, args.steps, args.warmup
-    max_seq = max(4096, args.prompt + 2 * (W + K) + 8)
+    max_seq = max(4096, 2 * args.prompt + 2 * (W + K) + 8)
     c = model_cfg(args)
+    kv_blocks = 0
+    if args.paged:  # pool with room for every sequence's blocks, scattered
+        kv_blocks = B * ((args.prompt * 3 // 2 + 2 * (W + K) + 8 + PAGE - 1) // PAGE)
     m = b2.Model(c["vocab"], c["hidden"], c["inter"], c["layers"], c["nq"], c["nkv"], c["head_dim"], eps=c["eps"],
                  theta=c["theta"], tied=False, max_batch=B, max_seq=max_seq, tp_rank=rank, tp_size=world,
-                 nccl_id=nccl_id)
+                 nccl_id=nccl_id, kv_blocks=kv_blocks, block_size=PAGE)
     m.init_random(SEED_W, 0.02)
     if world > 1 and args.exchange == "p2p":
         # decode-step partial sums over NVLink peer memory (fused into the
@@ -360,13 +370,33 @@ def run_b2(args, rank, world, local):
         dist.all_gather_object(handles, m.p2p_handle())
         m.p2p_open(handles)
     prompt = np.random.default_rng(SEED_P).integers(0, c["vocab"], (B, args.prompt))
-    m.prefill(prompt, want_logits=False)  # first call: workspace allocation, module load
-    m.reset()
-    torch.cuda.synchronize()
-    t = time.time()
-    m.prefill(prompt, want_logits=False)
-    prefill_s = time.time() - t
-    log(f"[rank {rank}] prefill {B}x{args.prompt} tokens in {prefill_s * 1e3:.1f} ms")
+    if args.paged:
+        # mixed lengths: sequence b's prompt is lens[b] tokens, its blocks a
+        # random scatter over the pool; prefilled one sequence at a time
+        prng = np.random.default_rng(SEED_P + 7)
+        lens = [int(x) for x in prng.integers(args.prompt // 2, args.prompt * 3 // 2 + 1, B)]
+        perm = list(prng.permutation(kv_blocks))
+        per_seq = kv_blocks // B
+        tables = np.array([perm[b * per_seq:(b + 1) * per_seq] for b in range(B)], np.int32)
+        firsts = np.zeros(B, np.int64)
+        m.prefill_paged(prompt[0, :lens[0]], tables[0])  # first call: workspace allocation, module load
+        torch.cuda.synchronize()
+        t = time.time()
+        for b in range(B):
+            firsts[b] = m.prefill_paged(prompt[b, :lens[b]], tables[b])[0]
+        prefill_s = time.time() - t
+        # the device loop continues every sequence from its own position
+        m.decode_step_paged(firsts, [n + 1 for n in lens], tables)
+        log(f"[rank {rank}] paged prefill of {B} prompts of {min(lens)}..{max(lens)} tokens in "
+            f"{prefill_s * 1e3:.1f} ms")
+    else:
+        m.prefill(prompt, want_logits=False)  # first call: workspace allocation, module load
+        m.reset()
+        torch.cuda.synchronize()
+        t = time.time()
+        m.prefill(prompt, want_logits=False)
+        prefill_s = time.time() - t
+        log(f"[rank {rank}] prefill {B}x{args.prompt} tokens in {prefill_s * 1e3:.1f} ms")
     stream = torch.cuda.ExternalStream(m.stream, device=dev)
 
     def barrier():
@@ -388,6 +418,8 @@ def run_b2(args, rank, world, local):
     m.generate_greedy(W, fetch=False)
     m.sync()
     pos0 = args.prompt + W
+    if args.paged:  # next position of each sequence after the warm-up and timed loops
+        pos_b = np.array([n + 1 + W + K for n in lens])
 
     # value: K device-resident steps, CUDA events on the model's stream
     barrier()
@@ -424,7 +456,10 @@ def run_b2(args, rank, world, local):
     w2 = time.time()
     e2.record(stream)
     for i in range(K):
-        _, tok = m.decode_step(tok, [pos0 + i] * B, want_logits=True, want_next=True, logits_out=lg_host)
+        if args.paged:
+            tok, _ = m.decode_step_paged(tok, pos_b + i + 1, tables)
+        else:
+            _, tok = m.decode_step(tok, [pos0 + i] * B, want_logits=True, want_next=True, logits_out=lg_host)
     e3.record(stream)
     e3.synchronize()
     w3 = time.time()
@@ -471,9 +506,15 @@ def run_b2(args, rank, world, local):
             "vs_baseline": None, "dtype": "f16",
             "data": "synthetic: seeded random-init fp16 weights ~N(0,0.02), uniform random prompt ids",
             "config": config_dict(args, world),
-            "e2e": {"value": B * K / (ms_e2e * 1e-3), "unit": "tok/s", "h2d_bytes_per_step": 12 * B,
-                    "d2h_bytes_per_step": 4 * B * c["vocab"] + 8 * B, "ms_per_step": ms_e2e / K,
-                    "api": "b2_model_decode_step (host token + position in, fp32 logits into a reused page-locked host buffer + next id out)"},
+            "e2e": ({"value": B * K / (ms_e2e * 1e-3), "unit": "tok/s",
+                     "h2d_bytes_per_step": 12 * B + 4 * int(tables.size), "d2h_bytes_per_step": 8 * B,
+                     "ms_per_step": ms_e2e / K,
+                     "api": "b2_model_decode_step_paged (host tokens, sequence lengths and block tables in, "
+                            "next ids out)"} if args.paged else
+                    {"value": B * K / (ms_e2e * 1e-3), "unit": "tok/s", "h2d_bytes_per_step": 12 * B,
+                     "d2h_bytes_per_step": 4 * B * c["vocab"] + 8 * B, "ms_per_step": ms_e2e / K,
+                     "api": "b2_model_decode_step (host token + position in, fp32 logits into a reused page-locked "
+                            "host buffer + next id out)"}),
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                          "frac": achieved / peak, "traffic": ncu_traffic("gate_up") if ktimes else None,
                          "kernel": dom_name, "bytes_per_launch": dom_bytes, "launch_ms": dom_ms,
@@ -647,6 +688,9 @@ def main():
     ap.add_argument("--prompt", type=int, default=PROMPT, help="prompt length (512 for the metric)")
     ap.add_argument("--layers", type=int, default=0,
                     help="decoder depth override (reduced only for small profiler captures; 0 = the model's)")
+    ap.add_argument("--paged", action="store_true",
+                    help="paged KV cache (16-position blocks scattered over a pool), mixed prompt lengths "
+                         "prompt/2 .. 3*prompt/2, prefilled one sequence at a time")
     ap.add_argument("--model", default="llama3-8b", choices=sorted(MODELS),
                     help="model shape (the metric is quoted on llama3-8b)")
     args = ap.parse_args()

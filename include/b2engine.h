@@ -351,6 +351,19 @@ int b2_model_set_tensor(b2_model* m, const char* name, const uint16_t* host_f16,
 int b2_model_set_tensor_bf16(b2_model* m, const char* name, const uint16_t* host_bf16, int64_t rows,
                              int64_t cols);
 
+/* How the model picks each next token from here on (prefill, decode steps
+ * and the device-resident loop): cfg->temperature <= 1e-6 is greedy argmax
+ * (the default); otherwise every sequence draws from top-k / temperature /
+ * top-p inside the captured step -- the selection of b2_sampler_sample, with
+ * one LCG state per sequence, reset by this call to a fresh sampler's state
+ * (13374269) -- so a sampled decode keeps its logits on the device.  The
+ * configuration lives in device memory: changing temperature / top-k /
+ * top-p / seed needs no recapture (switching greedy <-> sampling recaptures
+ * the step).  B2_ERR_UNSUPPORTED for a repetition penalty != 1 or tp_size >
+ * 1 when sampling.  Synchronises.  New API (the reference samples on the
+ * host, src/runtime/sampler.cu:253-339, apps/generate.cpp:884-898). */
+int b2_model_set_sampling(b2_model* m, const b2_sampler_config* cfg);
+
 /* Clears the KV cache positions of all sequences (sets lengths to 0). */
 int b2_model_reset(b2_model* m);
 
@@ -416,9 +429,9 @@ int b2_model_forward_logits(b2_model* m, const int64_t* host_ids, int seq_len, f
 int b2_model_decode_enqueue(b2_model* m, const int64_t* host_tokens, const int* host_positions, int batch,
                             float* d_logits);
 
-/* Device-resident greedy generation: `steps` decode steps replayed back to
- * back without host round trips, each consuming the argmax of the previous
- * one.  It continues from the last prefill / decode step: the first step
+/* Device-resident generation: `steps` decode steps replayed back to back
+ * without host round trips, each consuming the token the previous one chose
+ * (the argmax, or the draw of b2_model_set_sampling's configuration).  It continues from the last prefill / decode step: the first step
  * consumes that step's argmax.  host_tokens_out ([steps, batch]) receives the
  * token each step consumed (so row 0 is the argmax of the last processed
  * position); when it is NULL the call only enqueues the steps on the model's

@@ -93,6 +93,7 @@ _SIGS = {
     "b2_model_set_tensor_bf16": (i32, [vp, C.c_char_p, vp, i64, i64]),
     "b2_model_forward_logits": (i32, [vp, vp, i32, vp]),
     "b2_model_reset": (i32, [vp]),
+    "b2_model_set_sampling": (i32, [vp, C.POINTER(SamplerConfig)]),
     "b2_model_prefill": (i32, [vp, vp, i32, i32, vp]),
     "b2_model_decode_step": (i32, [vp, vp, vp, i32, vp, vp]),
     "b2_model_decode_enqueue": (i32, [vp, vp, vp, i32, vp]),
@@ -317,6 +318,12 @@ class Model:
 
     def reset(self):
         call("b2_model_reset", self.h)
+
+    def set_sampling(self, temperature=0.0, top_k=0, top_p=1.0, seed=42):
+        """Token choice of prefill, decode steps and the device loop
+        (temperature 0: greedy); resets every sequence's LCG state."""
+        cfg = SamplerConfig(temperature, top_k, top_p, 1.0, seed)
+        call("b2_model_set_sampling", self.h, C.byref(cfg))
 
     def prefill(self, ids, want_logits=True):
         import numpy as np

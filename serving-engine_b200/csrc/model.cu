@@ -63,6 +63,8 @@ int attn_decode_launch_step_q(const __half* q, int64_t q_sb, const __half* kbase
                               int64_t sh, int64_t ss, const int* seq_lens, __half* out, float* part, int splits,
                               int B, int nq, int nkv, int D, cudaStream_t s);
 int* wait_error_word();
+int step_sample_launch(const float* logits, int64_t ld, int V, int B, const b2_sampler_config* d_cfg,
+                       uint64_t* d_rng, unsigned long long* d_argmax, cudaStream_t s);
 int attn_tc_launch_paged(const __half* q, int64_t q_sb, __half* out, int64_t o_sb, const __half* kpool,
                          const __half* vpool, int num_blocks, int bs, const int* bt, int maxb, int max_len,
                          const int* seq_lens, int B, int nq, int nkv, int D, int early_kv, int lean, TraceSlot trace,
@@ -570,6 +572,11 @@ struct b2_model {
     int paged = 0, kv_blocks = 0, kv_bs = 0, kv_maxb = 0;
     int* block_tables = nullptr;
     int* h_bt = nullptr;  // pinned staging of the block tables
+    // sampling inside the step (b2_model_set_sampling): configuration in
+    // device memory, one LCG state per sequence
+    int sampling = 0;
+    b2_sampler_config* d_samp_cfg = nullptr;
+    uint64_t* d_rng = nullptr;
     float2* rope = nullptr;
 
     float* hidden = nullptr;
@@ -886,6 +893,8 @@ static int model_create(const b2_model_config* cfg, int tp_rank, int tp_size, co
         if (e == cudaSuccess) e = cudaMemset(m->push_ctr, 0, 256);
         if (e != cudaSuccess) { b2_model_destroy(m); return (int)e; }
     }
+    M_ALLOC(m->d_samp_cfg, sizeof(b2_sampler_config));
+    M_ALLOC(m->d_rng, (size_t)B * sizeof(uint64_t));
     m->hist_cap = 4096;
     M_ALLOC(m->hist, (size_t)m->hist_cap * B * sizeof(int64_t));
     M_ALLOC(m->hist_count, sizeof(int));
@@ -1420,6 +1429,8 @@ static int enqueue_step_batched(b2_model* m, int B) {
         M_TRY(add_and_norm(m, d, B, l + 1 < c.num_layers ? m->layers[l + 1].ln1 : m->final_norm));
     }
     M_TRY(lm_head_rows(m, B));
+    if (m->sampling)
+        M_TRY(step_sample_launch(m->logits, m->vocab_l, m->vocab_l, B, m->d_samp_cfg, m->d_rng, m->argmax, s));
     if (m->tp > 1) {
         if (nccl().AllReduce(m->argmax, m->argmax, (size_t)B, ncclUint64, ncclMax, m->comm, s) != ncclSuccess)
             return B2_ERR_NCCL;
@@ -1450,6 +1461,8 @@ static int enqueue_step(b2_model* m, int B) {
         if (!xch) M_TRY(nccl_sum_hidden(m, B));
     }
     M_TRY(launch_lm_head(m, B, pdl, xch));
+    if (m->sampling)
+        M_TRY(step_sample_launch(m->logits, m->vocab_l, m->vocab_l, B, m->d_samp_cfg, m->d_rng, m->argmax, s));
     if (m->tp > 1 && !xch) {
         if (nccl().AllReduce(m->argmax, m->argmax, (size_t)B, ncclUint64, ncclMax, m->comm, s) != ncclSuccess)
             return B2_ERR_NCCL;
@@ -1492,6 +1505,21 @@ static int run_step(b2_model* m, int B) {
     if (!use_graph) return enqueue_step(m, B);
     M_TRY(ensure_graph(m, B));
     B2_TRY(cudaGraphLaunch(m->graphs[B], m->stream));
+    return B2_OK;
+}
+
+extern "C" int b2_model_set_sampling(b2_model* m, const b2_sampler_config* cfg) {
+    B2_REQUIRE(m && cfg);
+    const int on = cfg->temperature > 1e-6f ? 1 : 0;
+    if (on && (m->tp != 1 || cfg->repetition_penalty != 1.0f || !(cfg->top_p > 0.f))) return B2_ERR_UNSUPPORTED;
+    B2_TRY(cudaMemcpyAsync(m->d_samp_cfg, cfg, sizeof(*cfg), cudaMemcpyHostToDevice, m->stream));
+    std::vector<uint64_t> st((size_t)m->cfg.max_batch, 13374269ull);  // a fresh sampler's state
+    B2_TRY(cudaMemcpyAsync(m->d_rng, st.data(), st.size() * sizeof(uint64_t), cudaMemcpyHostToDevice, m->stream));
+    B2_TRY(cudaStreamSynchronize(m->stream));
+    if (on != m->sampling) {
+        m->sampling = on;
+        invalidate_graphs(m);  // the step gains or loses its sampling kernel
+    }
     return B2_OK;
 }
 
@@ -1681,6 +1709,8 @@ static int prefill_batched(b2_model* m, int B, int S, int skip_pos = 0) {
         B2_CHECK_LAUNCH();
         M_TRY(lm_head_rows(m, B));
     }
+    if (m->sampling)
+        M_TRY(step_sample_launch(m->logits, m->vocab_l, m->vocab_l, B, m->d_samp_cfg, m->d_rng, m->argmax, st));
     if (m->tp > 1) {
         if (nccl().AllReduce(m->argmax, m->argmax, (size_t)B, ncclUint64, ncclMax, m->comm, st) != ncclSuccess)
             return B2_ERR_NCCL;

@@ -104,10 +104,10 @@ __device__ int block_exclusive_scan(int v, int* s_warp, int* total) {
     return before + x - v;
 }
 
-// Single CTA: top-k selection, sort, sequential tail.  K <= 1024.
-__global__ void __launch_bounds__(kTopkThreads) topk_sample_kernel(const float* __restrict__ logits, int V, int K,
-                                                                   float temperature, float top_p, float u,
-                                                                   int* __restrict__ token_out) {
+// One CTA of 1024 threads: top-k selection, sort, sequential tail; the id
+// goes to *token_out (thread 0).  K <= 1024.
+__device__ __forceinline__ int topk_select(const float* __restrict__ logits, int V, int K, float temperature,
+                                           float top_p, float u) {
     __shared__ unsigned int s_hist[256];
     __shared__ unsigned int s_prefix, s_remaining;
     __shared__ int s_warp[32];
@@ -115,7 +115,7 @@ __global__ void __launch_bounds__(kTopkThreads) topk_sample_kernel(const float* 
     __shared__ float s_val[kTopkThreads];
     __shared__ int s_id[kTopkThreads];
     __shared__ float s_prob[kTopkThreads];
-    griddep_wait();
+    __shared__ int s_token;
 
     const int tid = threadIdx.x;
     unsigned int prefix = 0, pmask = 0;
@@ -245,8 +245,56 @@ __global__ void __launch_bounds__(kTopkThreads) topk_sample_kernel(const float* 
             cdf += s_prob[i];
             if (u <= cdf) { sel = i; break; }
         }
-        *token_out = s_id[sel];
+        s_token = s_id[sel];
     }
+    __syncthreads();
+    return s_token;
+}
+
+__global__ void __launch_bounds__(kTopkThreads) topk_sample_kernel(const float* __restrict__ logits, int V, int K,
+                                                                   float temperature, float top_p, float u,
+                                                                   int* __restrict__ token_out) {
+    griddep_wait();
+    const int t = topk_select(logits, V, K, temperature, top_p, u);
+    if (threadIdx.x == 0) *token_out = t;
+}
+
+// The reference's LCG draw (src/runtime/sampler.cu:321-328): reseed iff
+// seed != 0 and seed != state, advance, u = (state >> 40) * 2^-24.
+__device__ __forceinline__ float lcg_draw(uint64_t* state, uint64_t seed) {
+    uint64_t st = *state;
+    if (seed != 0 && seed != st) st = seed;
+    st = st * 6364136223846793005ull + 1442695040888963407ull;
+    *state = st;
+    return static_cast<float>(static_cast<double>(st >> 40) * (1.0 / 16777216.0));
+}
+
+// Decode-step sampling: CTA b draws sequence b's token from its logits row
+// with its own LCG state (cfg in device memory, so a captured step picks up
+// a new configuration without recapture) and stores it as a packed argmax
+// key, which the step's end kernel turns into the next token.
+__global__ void __launch_bounds__(kTopkThreads) step_sample_kernel(const float* __restrict__ logits, int64_t ld,
+                                                                   int V, const b2_sampler_config* __restrict__ cfg,
+                                                                   int max_top_k, uint64_t* __restrict__ rng,
+                                                                   unsigned long long* __restrict__ argmax) {
+    griddep_wait();
+    const int b = blockIdx.x;
+    __shared__ float s_u;
+    const b2_sampler_config c = *cfg;
+    if (threadIdx.x == 0) s_u = lcg_draw(rng + b, c.seed);
+    __syncthreads();
+    int K = c.top_k;
+    if (K <= 0 || K > max_top_k) K = max_top_k < 64 ? max_top_k : 64;
+    if (K > V) K = V;
+    const int t = topk_select(logits + (int64_t)b * ld, V, K, c.temperature, c.top_p, s_u);
+    if (threadIdx.x == 0) argmax[b] = argmax_key(0.f, (uint32_t)t);
+}
+
+int step_sample_launch(const float* logits, int64_t ld, int V, int B, const b2_sampler_config* d_cfg,
+                       uint64_t* d_rng, unsigned long long* d_argmax, cudaStream_t s) {
+    B2_TRY(launch(step_sample_kernel, dim3((unsigned)B), dim3(kTopkThreads), 0, s, true, logits, ld, V, d_cfg,
+                  kTopkThreads, d_rng, d_argmax));
+    return B2_OK;
 }
 
 }  // namespace b2

@@ -335,3 +335,35 @@ def test_batched_tensor_core_step_llama8b_width(cuda, B):
     2, so the tensor-core step runs."""
     O.set_threads(os.cpu_count() or 1)
     _batched_teacher_forced(LLAMA8B_2L, 405 + B, B=B, S0=6, n_dec=3)
+
+
+@pytest.mark.parametrize("B", [1, 3])
+def test_device_sampling_matches_host_sampler(cuda, B):
+    """b2_model_set_sampling: with top-k / temperature / top-p on, the
+    captured step draws each sequence's token on the device (one LCG state
+    per sequence).  The ids equal those of b2_sampler_sample -- one fresh
+    sampler per sequence -- applied on the host side to the logits of the
+    same positions (decode steps fed those ids), so the device loop samples
+    bit-exactly as the reference's sampler would."""
+    import torch
+    cfg = SMALL
+    n = 12
+    rng = np.random.default_rng(31 + B)
+    prompts = rng.integers(0, cfg.vocab, (B, 9))
+    samp = dict(temperature=0.9, top_k=30, top_p=0.92, seed=0)
+    a = make_model(cfg, 515, max_batch=B)
+    a.set_sampling(**samp)
+    a.prefill(prompts, want_logits=False)
+    got = a.generate_greedy(n)
+    a.close()
+    host = make_model(cfg, 515, max_batch=B)
+    lg = host.prefill(prompts)
+    samplers = [b2.Sampler(cfg.vocab) for _ in range(B)]
+    want = np.zeros((n, B), np.int64)
+    for i in range(n):
+        for b in range(B):
+            want[i, b] = samplers[b].sample(torch.from_numpy(np.ascontiguousarray(lg[b])).cuda(), **samp)
+        if i + 1 < n:
+            lg, _ = host.decode_step(want[i], [9 + i] * B)
+    host.close()
+    assert np.array_equal(got, want), (got.T, want.T)
