@@ -197,8 +197,10 @@ __global__ void __launch_bounds__(FlashCfg<D, ROPE>::THREADS, 1)
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bar + 18);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int qt = (int)gridDim.x - 1 - (int)blockIdx.x;  // heaviest tiles first
-    const int h = blockIdx.y, b = blockIdx.z;
+    // grid (heads, tiles, batch): CTAs are dispatched x fastest, so every
+    // head's heaviest tile goes out before any lighter one (longest first)
+    const int qt = (int)gridDim.y - 1 - (int)blockIdx.y;
+    const int h = blockIdx.x, b = blockIdx.z;
     const int kvh = h / (nq / nkv);
     const int q0 = qt * 128;
     const int nt = qt + 1;
@@ -466,8 +468,10 @@ __global__ void __launch_bounds__(F2Cfg::THREADS, 1)
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bar + 16);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int pt = (int)gridDim.x - 1 - (int)blockIdx.x;  // heaviest pairs first
-    const int h = blockIdx.y, b = blockIdx.z;
+    // grid (heads, pairs, batch): every head's heaviest pair is dispatched
+    // before any lighter one (longest first across the whole grid)
+    const int pt = (int)gridDim.y - 1 - (int)blockIdx.y;
+    const int h = blockIdx.x, b = blockIdx.z;
     const int kvh = h / (nq / nkv);
     const int q0 = pt * 256;
     const bool hasB = q0 + 128 < S;
@@ -776,14 +780,14 @@ static int launch_flash(const FlashArgs& a_in, cudaStream_t s) {
     if (D == 128 && flash2_enabled()) {
         auto kern2 = flash2_tc_kernel<BF16, ROPE>;
         B2_TRY(cudaFuncSetAttribute(kern2, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)F2Cfg::SMEM));
-        dim3 grid2((unsigned)((a.S + 255) / 256), (unsigned)a.nq, (unsigned)a.batch);
+        dim3 grid2((unsigned)a.nq, (unsigned)((a.S + 255) / 256), (unsigned)a.batch);
         B2_TRY(launch(kern2, grid2, dim3(F2Cfg::THREADS), F2Cfg::SMEM, s, true, tq, tk, tv, a.out, a.ldo, a.S, a.nq,
                       a.nkv, scale_log2, a.rope_theta, a.pos0, err));
         return B2_OK;
     }
     auto kern = flash_tc_kernel<D, BF16, ROPE>;
     B2_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)Cfg::SMEM));
-    dim3 grid((unsigned)((a.S + 127) / 128), (unsigned)a.nq, (unsigned)a.batch);
+    dim3 grid((unsigned)a.nq, (unsigned)((a.S + 127) / 128), (unsigned)a.batch);
     B2_TRY(launch(kern, grid, dim3(Cfg::THREADS), Cfg::SMEM, s, true, tq, tk, tv, a.out, a.ldo, a.S, a.nq, a.nkv,
                   scale_log2, a.rope_theta, a.pos0, err));
     return B2_OK;
