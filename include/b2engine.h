@@ -154,10 +154,10 @@ int b2_flash_prefill_gqa(const void* q, const void* k, const void* v, void* out,
 
 /* b2_flash_prefill_gqa with a choice of element type (bf16 != 0: bf16
  * q/k/v/out, else half) and rotate-half RoPE at positions start_pos + s when
- * rope_theta > 0: q rotated inside the attention kernel, k once per key by a
- * pre-pass kernel of the same call into a per-device scratch copy
- * (batch*S*nkv*head_dim*2 bytes, allocated on first use and grown as
- * needed; RoPE calls on one device must not overlap in time; see
+ * rope_theta > 0: q and k rotated once by a pre-pass kernel of the same
+ * call into per-device scratch copies (batch*S*(nq+nkv)*head_dim*2 bytes,
+ * allocated on first use and grown as needed; RoPE calls on one device
+ * must not overlap in time; see
  * b2_flash_prefill_gqa_ws for the form that allocates nothing).  q, k in
  * memory are left unrotated.  head_dim 64 or 128 only.  New API (the
  * reference applies RoPE as a separate apply_rope launch,
@@ -167,21 +167,23 @@ int b2_flash_prefill_gqa_ex(const void* q, const void* k, const void* v, void* o
                             float rope_theta, int64_t start_pos, void* stream);
 
 /* Device scratch owned by the caller and lent to the entry points that take
- * one, so that those never allocate (SURVEY's explicit-workspace boundary; no
- * counterpart in the reference, whose only internal workspaces are the
- * sampler's).  b2_workspace_create allocates `bytes` of device memory on the
- * current device; the handle may be reused by any number of calls on that
- * device that do not overlap in time. */
+ * one, so that those never allocate (no counterpart in the reference, whose
+ * only internal workspaces are the sampler's).  b2_workspace_create
+ * allocates `bytes` of device memory on the current device; the handle may
+ * be reused by any number of calls on that device that do not overlap in
+ * time. */
 typedef struct b2_workspace b2_workspace;
 int b2_workspace_create(size_t bytes, b2_workspace** out);
 int b2_workspace_destroy(b2_workspace* ws);
 size_t b2_workspace_bytes(const b2_workspace* ws);
 
-/* Workspace bytes b2_flash_prefill_gqa_ws needs for the RoPE form
- * (batch * S * nkv * head_dim * 2: the rotated keys). */
-size_t b2_flash_prefill_workspace_bytes(int64_t seq_len, int num_kv_heads, int head_dim, int batch_size);
+/* Workspace bytes b2_flash_prefill_gqa_ws needs for the RoPE form:
+ * batch * S * (num_q_heads + num_kv_heads) * head_dim * 2 (the rotated q
+ * and k copies). */
+size_t b2_flash_prefill_workspace_bytes(int64_t seq_len, int num_q_heads, int num_kv_heads, int head_dim,
+                                        int batch_size);
 
-/* b2_flash_prefill_gqa_ex with the rotated-key scratch taken from `ws`
+/* b2_flash_prefill_gqa_ex with the rotated q / k scratch taken from `ws`
  * (B2_ERR_WORKSPACE when it is smaller than
  * b2_flash_prefill_workspace_bytes): allocates nothing, so it is
  * graph-capturable from its first call.  ws == NULL behaves as _ex.  New API

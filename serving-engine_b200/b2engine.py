@@ -63,7 +63,7 @@ _SIGS = {
     "b2_workspace_create": (i32, [C.c_size_t, C.POINTER(vp)]),
     "b2_workspace_destroy": (i32, [vp]),
     "b2_workspace_bytes": (C.c_size_t, [vp]),
-    "b2_flash_prefill_workspace_bytes": (C.c_size_t, [i64, i32, i32, i32]),
+    "b2_flash_prefill_workspace_bytes": (C.c_size_t, [i64, i32, i32, i32, i32]),
     "b2_flash_prefill_gqa_ws": (i32, [vp, vp, vp, vp, i64, i32, i32, i32, i32, i32, f32, i64, vp, vp]),
     "b2_swiglu": (i32, [vp, vp, vp, i64, vp]),
     "b2_matmul_transB": (i32, [vp, vp, vp, i32, i32, i32, vp]),

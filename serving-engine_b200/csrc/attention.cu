@@ -34,6 +34,7 @@
 // src/cuda/decode_attention.cu:15-141 (serial per-token loop).
 #include <cmath>
 
+#include "attention.cuh"
 #include "common.cuh"
 
 namespace b2 {
@@ -452,9 +453,6 @@ static bool view_ok(const b2_kv_view& v) {
 }  // namespace b2
 
 namespace b2 {
-int attn_cl_launch(const __half* q, int64_t q_sb, __half* out, int64_t o_sb, const __half* k, const __half* v,
-                   int64_t sb, int64_t sh, int64_t ss, int max_len, const int* seq_lens, int len_const, int B,
-                   int nq, int nkv, int D, int early_kv, int lean, TraceSlot trace, cudaStream_t s, bool pdl);
 }
 
 using namespace b2;

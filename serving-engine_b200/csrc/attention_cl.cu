@@ -29,6 +29,7 @@
 
 #include <cooperative_groups.h>
 
+#include "attention.cuh"
 #include "tc.cuh"
 
 namespace cg = cooperative_groups;
@@ -404,10 +405,6 @@ int attn_cl_splits(int batch, int nq, int nkv, int D, int max_len) {
 // cores (attention_tc.cu), other head dims on this file's kernel.
 // B2_ERR_UNSUPPORTED when the shape fits neither (the caller then uses
 // attn_decode_launch).
-int attn_tc_launch(const __half* q, int64_t q_sb, __half* out, int64_t o_sb, const __half* k, const __half* v,
-                   int64_t sb, int64_t sh, int64_t ss, int max_len, const int* seq_lens, int len_const, int B,
-                   int nq, int nkv, int D, int early_kv, int lean, TraceSlot trace, cudaStream_t s, bool pdl);
-
 int attn_cl_launch(const __half* q, int64_t q_sb, __half* out, int64_t o_sb, const __half* k, const __half* v,
                    int64_t sb, int64_t sh, int64_t ss, int max_len, const int* seq_lens, int len_const, int B,
                    int nq, int nkv, int D, int early_kv, int lean, TraceSlot trace, cudaStream_t s, bool pdl) {

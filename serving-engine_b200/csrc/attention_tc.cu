@@ -33,6 +33,7 @@
 
 #include <cooperative_groups.h>
 
+#include "attention.cuh"
 #include "tc.cuh"
 
 namespace cg = cooperative_groups;

@@ -34,6 +34,7 @@
 #include <string>
 #include <vector>
 
+#include "attention.cuh"
 #include "gemv.cuh"
 #include "prefill.cuh"
 #include "skinny.cuh"
@@ -65,13 +66,6 @@ int attn_decode_launch_step_q(const __half* q, int64_t q_sb, const __half* kbase
 int* wait_error_word();
 int step_sample_launch(const float* logits, int64_t ld, int V, int B, const b2_sampler_config* d_cfg,
                        uint64_t* d_rng, unsigned long long* d_argmax, cudaStream_t s);
-int attn_tc_launch_paged(const __half* q, int64_t q_sb, __half* out, int64_t o_sb, const __half* kpool,
-                         const __half* vpool, int num_blocks, int bs, const int* bt, int maxb, int max_len,
-                         const int* seq_lens, int B, int nq, int nkv, int D, int early_kv, int lean, TraceSlot trace,
-                         cudaStream_t s, bool pdl);
-int attn_cl_launch(const __half* q, int64_t q_sb, __half* out, int64_t o_sb, const __half* k, const __half* v,
-                   int64_t sb, int64_t sh, int64_t ss, int max_len, const int* seq_lens, int len_const, int B,
-                   int nq, int nkv, int D, int early_kv, int lean, TraceSlot trace, cudaStream_t s, bool pdl);
 
 // ---------------------------------------------------------------------------
 // seeded initialisation (bit-identical to oracle/b2oracle.c ora_init_value)

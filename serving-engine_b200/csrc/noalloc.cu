@@ -26,6 +26,7 @@
 // partial results are overwritten before they are read.
 #include <mutex>
 
+#include "attention.cuh"
 #include "common.cuh"
 
 namespace b2 {
@@ -37,9 +38,6 @@ bool attn_head_dim_supported(int D);
 int attn_decode_launch_model(const __half* q, const __half* kbase, const __half* vbase, int64_t sb, int64_t sh,
                              int64_t ss, const int* seq_lens, __half* out, float* part, int splits, int B, int nq,
                              int nkv, int D, cudaStream_t s, bool pdl);
-int attn_cl_launch(const __half* q, int64_t q_sb, __half* out, int64_t o_sb, const __half* k, const __half* v,
-                   int64_t sb, int64_t sh, int64_t ss, int max_len, const int* seq_lens, int len_const, int B,
-                   int nq, int nkv, int D, int early_kv, int lean, TraceSlot trace, cudaStream_t s, bool pdl);
 
 // 4 MiB of partial results (1,048,576 floats).
 constexpr size_t kNoAllocScratchBytes = 4u << 20;

@@ -12,14 +12,13 @@
 // Warp roles (192 threads):
 //   warp 4      TMA producer: Q once, then K_j / V_j into 2-stage rings;
 //   warp 5      MMA issuer (one thread): S_j, then P_{j-1} V_{j-1};
-//   warps 0..3  softmax, one query row per thread: (RoPE form) the row of
-//               Q rotated in shared memory first; then per key tile the row
+//   warps 0..3  softmax, one query row per thread: per key tile the row
 //               of S_j read from TMEM once into registers, causal mask, row
 //               max, P_j = exp2(S scale - m) as half/bf16 into one of two
 //               swizzled shared-memory P buffers (P_j is written while
 //               P_{j-1} V_{j-1} runs), running row sum; O / l at the end.
-// RoPE form: keys are rotated once by a pre-pass kernel of the same call
-// into a dense copy that the K tiles are loaded from.
+// RoPE form: queries and keys are rotated once by a pre-pass kernel of the
+// same call into dense copies that the Q and K tiles are loaded from.
 // Online softmax without a rescale per tile: the reference max m of a row
 // only moves when the tile max exceeds it by more than 8 (log2 units); P
 // values stay <= 2^8 otherwise, and when m moves the O row in TMEM is scaled
@@ -45,7 +44,7 @@ int causal_attention_rows(const __half* q, const __half* k, const __half* v, __h
                           int nkv, int D, int batch, cudaStream_t s);
 bool attn_head_dim_supported(int D);
 
-template <int D, bool ROPE>
+template <int D>
 struct FlashCfg {
     static constexpr int ATOMS = D / 64;                    // 128-byte swizzle atoms per row
     static constexpr uint32_t ATOM = 128 * 128;             // bytes of one 128-row atom
@@ -98,67 +97,53 @@ __device__ __forceinline__ uint32_t sw128_off(int row, int e) {
 // (c, s) = (cos, sin)(float(pos) * inv_freq[i]), inv_freq[i] =
 // 1 / theta^(2i/D) -- the same float product per element as the reference.
 //
-// Q: row r of the tile (position p) rotated in shared memory by thread r.
-template <int D, bool BF16>
-__device__ __forceinline__ void rope_row(uint8_t* tile, int r, int p, const float* invf) {
-    constexpr int H = D / 2;
-#pragma unroll 1
-    for (int c = 0; c < H; c += 8) {
-        uint4* p1 = reinterpret_cast<uint4*>(tile + sw128_off(r, c));
-        uint4* p2 = reinterpret_cast<uint4*>(tile + sw128_off(r, c + H));
-        uint4 a = *p1, b = *p2;
-        uint32_t* aw = reinterpret_cast<uint32_t*>(&a);
-        uint32_t* bw = reinterpret_cast<uint32_t*>(&b);
-#pragma unroll
-        for (int q = 0; q < 4; ++q) {
-            const float2 x1 = unpack2<BF16>(aw[q]), x2 = unpack2<BF16>(bw[q]);
-            float s0, c0, s1, c1;
-            sincosf((float)p * invf[c + 2 * q], &s0, &c0);
-            sincosf((float)p * invf[c + 2 * q + 1], &s1, &c1);
-            aw[q] = pack2<BF16>(x1.x * c0 - x2.x * s0, x1.y * c1 - x2.y * s1);
-            bw[q] = pack2<BF16>(x2.x * c0 + x1.x * s0, x2.y * c1 + x1.y * s1);
-        }
-        *p1 = a;
-        *p2 = b;
-    }
-}
-
-// K: every key row rotated once, into a dense [batch][S][nkv][D] copy, before
-// the attention kernel runs (each key tile is read by every query tile and
-// query head of its group, so rotating it inside each CTA would repeat the
-// work S/128 * nq/nkv times).  One thread per 8 frequencies of a row.
+// Queries and keys are rotated once, by a pre-pass of the same call, into
+// dense [batch][S][heads][D] copies that the attention kernel's Q and K tiles
+// are loaded from: rotating inside the attention CTAs would put the rotation
+// on each CTA's path to its first S = Q K^T and repeat the keys' rotation
+// S/128 * nq/nkv times.  One thread per (token, 8 frequencies, group of 8
+// heads of the q|k head list): its 8 (cos, sin) pairs are computed once and
+// applied to each head of the group.
 template <bool BF16>
-__global__ void rope_keys_kernel(const uint16_t* __restrict__ k, int64_t ldk, uint16_t* __restrict__ out, int S,
-                                 int nkv, int D, int batch, float theta, int pos0) {
+__global__ void rope_qk_kernel(const uint16_t* __restrict__ q, int64_t ldq, const uint16_t* __restrict__ k,
+                               int64_t ldk, uint16_t* __restrict__ qo, uint16_t* __restrict__ ko, int S, int nq,
+                               int nkv, int D, int batch, float theta, int pos0) {
+    constexpr int kHeads = 8;
     __shared__ float invf[64];
     const int H = D / 2;
     if ((int)threadIdx.x < H) invf[threadIdx.x] = 1.0f / powf(theta, (float)(2 * threadIdx.x) / (float)D);
     __syncthreads();
     griddep_wait();
     const int chunks = H / 8;
-    const int64_t n = (int64_t)batch * S * nkv * chunks;
+    const int groups = (nq + nkv + kHeads - 1) / kHeads;
+    const int64_t n = (int64_t)batch * S * groups * chunks;
     for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
         const int c = (int)(i % chunks) * 8;
-        const int64_t row = i / chunks;  // (b, s, head)
-        const int hd = (int)(row % nkv);
-        const int64_t bs = row / nkv;
+        const int g = (int)((i / chunks) % groups);
+        const int64_t bs = i / ((int64_t)chunks * groups);  // (b, s)
         const int pos = pos0 + (int)(bs % S);
-        const uint16_t* src = k + bs * ldk + (int64_t)hd * D;
-        uint16_t* dst = out + row * D;
-        uint4 a = *reinterpret_cast<const uint4*>(src + c), b = *reinterpret_cast<const uint4*>(src + c + H);
-        uint32_t* aw = reinterpret_cast<uint32_t*>(&a);
-        uint32_t* bw = reinterpret_cast<uint32_t*>(&b);
+        float cs[8], sn[8];
 #pragma unroll
-        for (int q = 0; q < 4; ++q) {
-            const float2 x1 = unpack2<BF16>(aw[q]), x2 = unpack2<BF16>(bw[q]);
-            float s0, c0, s1, c1;
-            sincosf((float)pos * invf[c + 2 * q], &s0, &c0);
-            sincosf((float)pos * invf[c + 2 * q + 1], &s1, &c1);
-            aw[q] = pack2<BF16>(x1.x * c0 - x2.x * s0, x1.y * c1 - x2.y * s1);
-            bw[q] = pack2<BF16>(x2.x * c0 + x1.x * s0, x2.y * c1 + x1.y * s1);
+        for (int e = 0; e < 8; ++e) sincosf((float)pos * invf[c + e], &sn[e], &cs[e]);
+        const int h_end = min(nq + nkv, (g + 1) * kHeads);
+#pragma unroll 4
+        for (int hd = g * kHeads; hd < h_end; ++hd) {
+            const bool isq = hd < nq;
+            const uint16_t* src = isq ? q + bs * ldq + (int64_t)hd * D : k + bs * ldk + (int64_t)(hd - nq) * D;
+            uint16_t* dst = isq ? qo + (bs * nq + hd) * D : ko + (bs * nkv + (hd - nq)) * D;
+            uint4 a = *reinterpret_cast<const uint4*>(src + c), b = *reinterpret_cast<const uint4*>(src + c + H);
+            uint32_t* aw = reinterpret_cast<uint32_t*>(&a);
+            uint32_t* bw = reinterpret_cast<uint32_t*>(&b);
+#pragma unroll
+            for (int w = 0; w < 4; ++w) {
+                const float2 x1 = unpack2<BF16>(aw[w]), x2 = unpack2<BF16>(bw[w]);
+                const float c0 = cs[2 * w], s0 = sn[2 * w], c1 = cs[2 * w + 1], s1 = sn[2 * w + 1];
+                aw[w] = pack2<BF16>(x1.x * c0 - x2.x * s0, x1.y * c1 - x2.y * s1);
+                bw[w] = pack2<BF16>(x2.x * c0 + x1.x * s0, x2.y * c1 + x1.y * s1);
+            }
+            *reinterpret_cast<uint4*>(dst + c) = a;
+            *reinterpret_cast<uint4*>(dst + c + H) = b;
         }
-        *reinterpret_cast<uint4*>(dst + c) = a;
-        *reinterpret_cast<uint4*>(dst + c + H) = b;
     }
 }
 
@@ -170,23 +155,21 @@ __device__ __forceinline__ float fast_exp2(float x) {
     return y;
 }
 
-template <int D, bool BF16, bool ROPE>
-__global__ void __launch_bounds__(FlashCfg<D, ROPE>::THREADS, 1)
+template <int D, bool BF16>
+__global__ void __launch_bounds__(FlashCfg<D>::THREADS, 1)
     flash_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                     const __grid_constant__ CUtensorMap tmV, void* __restrict__ out, int64_t ldo, int S, int nq,
-                    int nkv, float scale_log2, float rope_theta, int pos0, int* err) {
-    using Cfg = FlashCfg<D, ROPE>;
+                    int nkv, float scale_log2, int* err) {
+    using Cfg = FlashCfg<D>;
     constexpr uint32_t TILE = Cfg::TILE;
     extern __shared__ uint8_t smem_raw[];
-    __shared__ float s_invf[64];
     uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint8_t* sQ = sm + Cfg::OFF_Q;
     uint8_t* sK = sm + Cfg::OFF_K;
     uint8_t* sV = sm + Cfg::OFF_V;
     uint8_t* sP = sm + Cfg::OFF_P;
     uint64_t* bar = reinterpret_cast<uint64_t*>(sm + Cfg::OFF_BAR);
-    uint64_t* q_full = bar + 0;
-    uint64_t* q_ready = bar + 1;
+    uint64_t* q_full = bar + 0;   // (bar + 1 spare)
     uint64_t* k_full = bar + 2;   // [2] (bar + 4, + 5 spare)
     uint64_t* k_empty = bar + 6;  // [2]
     uint64_t* v_full = bar + 8;   // [2]
@@ -207,7 +190,6 @@ __global__ void __launch_bounds__(FlashCfg<D, ROPE>::THREADS, 1)
 
     if (threadIdx.x == 0) {
         tc::mbar_init(q_full, 1);
-        tc::mbar_init(q_ready, 128);
         for (int s = 0; s < 2; ++s) {
             tc::mbar_init(&k_full[s], 1);
             tc::mbar_init(&k_empty[s], 1);
@@ -221,7 +203,6 @@ __global__ void __launch_bounds__(FlashCfg<D, ROPE>::THREADS, 1)
         }
         tc::fence_barrier_init();
     }
-    if (ROPE && threadIdx.x < D / 2) s_invf[threadIdx.x] = 1.0f / powf(rope_theta, (float)(2 * threadIdx.x) / (float)D);
     if (warp == 0) tc::tmem_alloc(tmem_slot, Cfg::TMEM_COLS);
     tc::fence_before_sync();
     __syncthreads();
@@ -260,7 +241,7 @@ __global__ void __launch_bounds__(FlashCfg<D, ROPE>::THREADS, 1)
             constexpr uint32_t idO = tc::idesc_f16(128, D, BF16, true);
             const uint32_t aQ = tc::smem_u32(sQ), aK = tc::smem_u32(sK), aV = tc::smem_u32(sV),
                            aP = tc::smem_u32(sP);
-            bool ok = tc::mbar_wait(ROPE ? q_ready : q_full, 0, err, 13);
+            bool ok = tc::mbar_wait(q_full, 0, err, 13);
             for (int j = 0; ok && j <= nt; ++j) {
                 if (j < nt) {
                     const int s = j & 1;
@@ -306,14 +287,6 @@ __global__ void __launch_bounds__(FlashCfg<D, ROPE>::THREADS, 1)
         const uint32_t lane_base = (uint32_t)(warp * 32) << 16;
         float m = -1e30f, l = 0.f;  // finite start: a fully masked row keeps P = 0 and l = 0
         bool ok = true;
-        if constexpr (ROPE) {  // rotate this thread's Q row before the first S = Q K^T
-            ok = __all_sync(0xffffffffu, tc::mbar_wait(q_full, 0, err, 17));
-            if (ok) {
-                rope_row<D, BF16>(sQ, r, pos0 + qpos, s_invf);
-                tc::fence_proxy_async_smem();
-                tc::mbar_arrive(q_ready);
-            }
-        }
         for (int j = 0; ok && j < nt; ++j) {
             const int s = j & 1;
             const uint32_t u = (uint32_t)j >> 1;
@@ -442,22 +415,20 @@ struct F2Cfg {
     static constexpr int THREADS = 320;
 };
 
-template <bool BF16, bool ROPE>
+template <bool BF16>
 __global__ void __launch_bounds__(F2Cfg::THREADS, 1)
     flash2_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                      const __grid_constant__ CUtensorMap tmV, void* __restrict__ out, int64_t ldo, int S, int nq,
-                     int nkv, float scale_log2, float rope_theta, int pos0, int* err) {
+                     int nkv, float scale_log2, int* err) {
     constexpr int D = 128;
     constexpr uint32_t TILE = F2Cfg::TILE, ATOM = F2Cfg::ATOM;
     extern __shared__ uint8_t smem_raw[];
-    __shared__ float s_invf[64];
     uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint8_t* sQ = sm + F2Cfg::OFF_Q;
     uint8_t* sK = sm + F2Cfg::OFF_K;
     uint8_t* sV = sm + F2Cfg::OFF_V;
     uint64_t* bar = reinterpret_cast<uint64_t*>(sm + F2Cfg::OFF_BAR);
-    uint64_t* q_full = bar + 0;
-    uint64_t* q_ready = bar + 1;
+    uint64_t* q_full = bar + 0;    // (bar + 1 spare)
     uint64_t* k_full = bar + 2;    // [2]
     uint64_t* k_empty = bar + 4;   // [2]
     uint64_t* v_full = bar + 6;    // [2]
@@ -481,7 +452,6 @@ __global__ void __launch_bounds__(F2Cfg::THREADS, 1)
 
     if (threadIdx.x == 0) {
         tc::mbar_init(q_full, 1);
-        tc::mbar_init(q_ready, 256);
         for (int s = 0; s < 2; ++s) {
             tc::mbar_init(&k_full[s], 1);
             tc::mbar_init(&k_empty[s], 1);
@@ -493,7 +463,6 @@ __global__ void __launch_bounds__(F2Cfg::THREADS, 1)
         }
         tc::fence_barrier_init();
     }
-    if (ROPE && threadIdx.x < D / 2) s_invf[threadIdx.x] = 1.0f / powf(rope_theta, (float)(2 * threadIdx.x) / (float)D);
     if (warp == 0) tc::tmem_alloc(tmem_slot, 512);
     tc::fence_before_sync();
     __syncthreads();
@@ -551,7 +520,7 @@ __global__ void __launch_bounds__(F2Cfg::THREADS, 1)
                                    tc::desc_mn_sw128(vb + (uint32_t)kk * 2048u, ATOM), idO, (j > 0 || kk > 0) ? 1u : 0u);
                 tc::mma_commit(&o_done[t]);
             };
-            bool ok = tc::mbar_wait(ROPE ? q_ready : q_full, 0, err, 33) && tc::mbar_wait(&k_full[0], 0, err, 34);
+            bool ok = tc::mbar_wait(q_full, 0, err, 33) && tc::mbar_wait(&k_full[0], 0, err, 34);
             if (ok) {
                 tc::fence_after_sync();
                 issue_s(0, 0);
@@ -605,12 +574,6 @@ __global__ void __launch_bounds__(F2Cfg::THREADS, 1)
         const int ntt = t == 0 ? ntA : ntB;
         float m = -1e30f, l = 0.f;
         bool ok = true;
-        if constexpr (ROPE) {
-            ok = __all_sync(0xffffffffu, tc::mbar_wait(q_full, 0, err, 41));
-            if (ok && ntt > 0) rope_row<D, BF16>(sQ + t * TILE, r, pos0 + qpos, s_invf);
-            tc::fence_proxy_async_smem();
-            tc::mbar_arrive(q_ready);
-        }
         for (int j = 0; ok && j < ntt; ++j) {
             ok = __all_sync(0xffffffffu, tc::mbar_wait(&s_full[t], (uint32_t)j & 1u, err, 42));
             if (!ok) break;
@@ -700,14 +663,15 @@ __global__ void __launch_bounds__(F2Cfg::THREADS, 1)
     }
 }
 
-// Rotated-key buffer of the RoPE form: one per device, grown on demand and
-// kept (freed at process exit).  Calls with RoPE on one device that overlap
-// in time (different streams) would share it and must not be issued.
+// Rotated-copy buffer of the RoPE form (q and k): one per device, grown on
+// demand and kept (freed at process exit).  Calls with RoPE on one device
+// that overlap in time (different streams) would share it and must not be
+// issued.
 static std::mutex g_rk_mu;
 static void* g_rk_buf[64];
 static size_t g_rk_bytes[64];
 
-static int rotated_key_buffer(size_t bytes, void** out) {
+static int rotated_copy_buffer(size_t bytes, void** out) {
     int dev = 0;
     B2_TRY(cudaGetDevice(&dev));
     if (dev < 0 || dev >= 64) return B2_ERR_UNSUPPORTED;
@@ -733,31 +697,40 @@ static bool flash2_enabled() {
     return on == 1;
 }
 
-template <int D, bool BF16, bool ROPE>
+// Workspace bytes of the RoPE form: the rotated Q and K copies.
+static size_t rope_copy_bytes(int64_t S, int nq, int nkv, int D, int batch) {
+    return (size_t)batch * S * (nq + nkv) * D * 2;
+}
+
+template <int D, bool BF16>
 static int launch_flash(const FlashArgs& a_in, cudaStream_t s) {
-    using Cfg = FlashCfg<D, ROPE>;
+    using Cfg = FlashCfg<D>;
     int* err = wait_error_word();
     if (!err) return B2_ERR_STATE;
     FlashArgs a = a_in;
-    if constexpr (ROPE) {  // keys rotated once into a dense copy; K tiles then come from it
-        void* rk = nullptr;
-        const size_t need = (size_t)a.batch * a.S * a.nkv * D * 2;
+    if (a.rope_theta > 0.f) {  // q and k rotated once into dense copies; the tiles then come from them
+        void* ws = nullptr;
+        const size_t need = rope_copy_bytes(a.S, a.nq, a.nkv, D, a.batch);
         if (a.rk_ws) {  // the caller's workspace: nothing is allocated here
             if (a.rk_ws_bytes < need || !aligned16(a.rk_ws)) return B2_ERR_WORKSPACE;
-            rk = a.rk_ws;
+            ws = a.rk_ws;
         } else {
-            const int rrc = rotated_key_buffer(need, &rk);
+            const int rrc = rotated_copy_buffer(need, &ws);
             if (rrc != B2_OK) return rrc;
         }
-        const int64_t work = (int64_t)a.batch * a.S * a.nkv * (D / 16);
+        uint16_t* qo = static_cast<uint16_t*>(ws);
+        uint16_t* ko = qo + (size_t)a.batch * a.S * a.nq * D;
+        const int64_t work = (int64_t)a.batch * a.S * ((a.nq + a.nkv + 7) / 8) * (D / 16);
         int64_t blocks = (work + 255) / 256;
         if (blocks > (int64_t)sm_count() * 16) blocks = (int64_t)sm_count() * 16;
-        B2_TRY(launch(rope_keys_kernel<BF16>, dim3((unsigned)blocks), dim3(256), 0, s, true,
-                      static_cast<const uint16_t*>(a.k), a.ldkv, static_cast<uint16_t*>(rk), a.S, a.nkv, D, a.batch,
-                      a.rope_theta, a.pos0));
-        a.k = rk;
+        B2_TRY(launch(rope_qk_kernel<BF16>, dim3((unsigned)blocks), dim3(256), 0, s, true,
+                      static_cast<const uint16_t*>(a.q), a.ldq, static_cast<const uint16_t*>(a.k), a.ldkv, qo, ko,
+                      a.S, a.nq, a.nkv, D, a.batch, a.rope_theta, a.pos0));
+        a.q = qo;
+        a.ldq = (int64_t)a.nq * D;
+        a.k = ko;
     }
-    const int64_t ldk = ROPE ? (int64_t)a.nkv * D : a.ldkv;
+    const int64_t ldk = a.rope_theta > 0.f ? (int64_t)a.nkv * D : a.ldkv;
     const CUtensorMapDataType dt = BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
     CUtensorMap tq, tk, tv;
     const uint32_t box[4] = {64, 1, 128, 1};
@@ -778,25 +751,25 @@ static int launch_flash(const FlashArgs& a_in, cudaStream_t s) {
     }
     const float scale_log2 = 1.4426950408889634f / sqrtf((float)D);
     if (D == 128 && flash2_enabled()) {
-        auto kern2 = flash2_tc_kernel<BF16, ROPE>;
+        auto kern2 = flash2_tc_kernel<BF16>;
         B2_TRY(cudaFuncSetAttribute(kern2, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)F2Cfg::SMEM));
         dim3 grid2((unsigned)a.nq, (unsigned)((a.S + 255) / 256), (unsigned)a.batch);
         B2_TRY(launch(kern2, grid2, dim3(F2Cfg::THREADS), F2Cfg::SMEM, s, true, tq, tk, tv, a.out, a.ldo, a.S, a.nq,
-                      a.nkv, scale_log2, a.rope_theta, a.pos0, err));
+                      a.nkv, scale_log2, err));
         return B2_OK;
     }
-    auto kern = flash_tc_kernel<D, BF16, ROPE>;
+    auto kern = flash_tc_kernel<D, BF16>;
     B2_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)Cfg::SMEM));
     dim3 grid((unsigned)a.nq, (unsigned)((a.S + 127) / 128), (unsigned)a.batch);
     B2_TRY(launch(kern, grid, dim3(Cfg::THREADS), Cfg::SMEM, s, true, tq, tk, tv, a.out, a.ldo, a.S, a.nq, a.nkv,
-                  scale_log2, a.rope_theta, a.pos0, err));
+                  scale_log2, err));
     return B2_OK;
 }
 
-template <bool BF16, bool ROPE>
+template <bool BF16>
 static int flash_dispatch_d(const FlashArgs& a, cudaStream_t s) {
-    if (a.D == 64) return launch_flash<64, BF16, ROPE>(a, s);
-    if (a.D == 128) return launch_flash<128, BF16, ROPE>(a, s);
+    if (a.D == 64) return launch_flash<64, BF16>(a, s);
+    if (a.D == 128) return launch_flash<128, BF16>(a, s);
     return B2_ERR_UNSUPPORTED;
 }
 
@@ -808,9 +781,7 @@ int flash_prefill_tc(const FlashArgs& a, cudaStream_t s) {
         !aligned16(a.v) || !aligned16(a.out) || a.batch > 65535 || a.nq > 65535 || (a.ldq & 7) || (a.ldkv & 7) ||
         (a.ldo & 7))
         return B2_ERR_UNSUPPORTED;
-    const bool rope = a.rope_theta > 0.f;
-    if (a.bf16) return rope ? flash_dispatch_d<true, true>(a, s) : flash_dispatch_d<true, false>(a, s);
-    return rope ? flash_dispatch_d<false, true>(a, s) : flash_dispatch_d<false, false>(a, s);
+    return a.bf16 ? flash_dispatch_d<true>(a, s) : flash_dispatch_d<false>(a, s);
 }
 
 }  // namespace b2
@@ -885,8 +856,11 @@ extern "C" int b2_workspace_destroy(b2_workspace* ws) {
 
 extern "C" size_t b2_workspace_bytes(const b2_workspace* ws) { return ws ? ws->bytes : 0; }
 
-extern "C" size_t b2_flash_prefill_workspace_bytes(int64_t S, int num_kv_heads, int head_dim, int batch) {
-    return S > 0 && num_kv_heads > 0 && head_dim > 0 && batch > 0 ? (size_t)batch * S * num_kv_heads * head_dim * 2 : 0;
+extern "C" size_t b2_flash_prefill_workspace_bytes(int64_t S, int num_q_heads, int num_kv_heads, int head_dim,
+                                                   int batch) {
+    return S > 0 && num_q_heads > 0 && num_kv_heads > 0 && head_dim > 0 && batch > 0
+               ? b2::rope_copy_bytes(S, num_q_heads, num_kv_heads, head_dim, batch)
+               : 0;
 }
 
 extern "C" int b2_flash_prefill_gqa_ws(const void* q, const void* k, const void* v, void* out, int64_t S, int nq,

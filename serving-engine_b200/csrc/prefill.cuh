@@ -14,10 +14,11 @@ struct FlashArgs {
     int S, nq, nkv, D, batch;
     int64_t ldq, ldkv, ldo;  // elements between consecutive tokens
     bool bf16;
-    float rope_theta;  // > 0: rotate q and k in-kernel
+    float rope_theta;  // > 0: q and k rotated (positions pos0..) by a pre-pass
     int pos0;
-    // RoPE form: device scratch for the rotated keys (batch*S*nkv*D*2 bytes);
-    // null: the library's per-device buffer, grown on demand
+    // RoPE form: device scratch for the rotated q and k copies
+    // (batch*S*(nq+nkv)*D*2 bytes); null: the library's per-device buffer,
+    // grown on demand
     void* rk_ws;
     size_t rk_ws_bytes;
 };

@@ -60,7 +60,7 @@ def _bf16(a):
 @pytest.mark.parametrize("S,rope", [(2048, 500000.0), (640, 0.0)])
 def test_flash_prefill_bf16_rope(cuda, S, rope):
     """BASELINE's causal-prefill shape: bf16 Q [1,S,32,128], K/V [1,S,8,128]
-    ~N(0,1), RoPE theta 5e5 in-kernel (rope = 0: no rotation)."""
+    ~N(0,1), RoPE theta 5e5 inside the call (rope = 0: no rotation)."""
     import torch
     nq, nkv, D = 32, 8, 128
     rng = np.random.default_rng(S)
@@ -139,7 +139,7 @@ def test_flash_prefill_fp16_rope_matches_separate_rope(cuda):
 
 
 def test_flash_prefill_workspace_form(cuda):
-    """b2_flash_prefill_gqa_ws takes the rotated-key scratch from a caller's
+    """b2_flash_prefill_gqa_ws takes the rotated q and k copies from a caller's
     b2_workspace (no allocation): same bytes as b2_flash_prefill_gqa_ex, and
     B2_ERR_WORKSPACE when the workspace is one byte short."""
     import ctypes
@@ -153,8 +153,8 @@ def test_flash_prefill_workspace_form(cuda):
     st = b2.stream_ptr()
     b2.call("b2_flash_prefill_gqa_ex", q.data_ptr(), k.data_ptr(), v.data_ptr(), out_a.data_ptr(), S, nq, nkv, D, 1,
             1, 500000.0, 3, st)
-    need = b2.lib().b2_flash_prefill_workspace_bytes(S, nkv, D, 1)
-    assert need == S * nkv * D * 2
+    need = b2.lib().b2_flash_prefill_workspace_bytes(S, nq, nkv, D, 1)
+    assert need == S * (nq + nkv) * D * 2  # rotated q and k copies
     for nbytes, want in ((need, 0), (need - 16, -3)):
         ws = ctypes.c_void_p()
         b2.call("b2_workspace_create", nbytes, ctypes.byref(ws))
