@@ -469,12 +469,19 @@ def run_b2(args, rank, world, local):
     ck = clocks.stop()
 
     trace = None
-    if args.trace and ktimes:  # the fused-GEMV step carries trace points
+    if args.trace:
         # per-launch device timestamps of a few live steps (b2_model_trace_step)
-        names = ["step_begin"] + ["qkv", "attention", "o_proj", "gate_up", "down"] * c["layers"] + ["lm_head",
-                                                                                                   "step_end"]
+        L = c["layers"]
+        layouts = [  # launch sequences of the step forms, in launch order
+            # fused-GEMV step
+            ["step_begin"] + ["qkv", "attention", "o_proj", "gate_up", "down"] * L + ["lm_head", "step_end"],
+            # batched step: skinny projections and the kernels that sum their partials
+            ["step_begin"] + ["qkv", "qkv_sum_rope", "attention", "o_proj", "o_sum_norm", "gate_up", "swiglu",
+                              "down", "down_sum_norm"] * L + ["lm_head", "logits_argmax", "step_end"],
+        ]
         runs = np.stack([m.trace_step(B) for _ in range(5)])
         t = np.median(runs, axis=0)
+        names = next((n for n in layouts if len(n) == len(t)), [f"k{i}" for i in range(len(t))])
         agg, prev = {}, 0
         for i, (a, e) in enumerate(t):
             g = agg.setdefault(names[i] if i < len(names) else f"k{i}", [0, 0.0, 0.0])

@@ -335,13 +335,17 @@ __device__ __forceinline__ float sk_sum(const SkSlabs& a, int B, int b, int n) {
 // i+D/2..); grid (B, ceil((nq + 2 nkv) D/8 / 256)), 256 threads.
 __global__ void sk_qkv_rope_kernel(SkSlabs a, int B, const __half* __restrict__ bias, __half* __restrict__ qkv,
                                    int64_t ld, const float2* __restrict__ rope, int nq, int nkv, int D,
-                                   const KvLayout kv, const int* __restrict__ positions) {
+                                   const KvLayout kv, const int* __restrict__ positions, TraceSlot tr) {
     griddep_wait();
     griddep_launch_dependents();
+    trace_begin(tr);
     const int b = blockIdx.x, half = D >> 1, per_head = D >> 3;
     const int t = blockIdx.y * blockDim.x + threadIdx.x;
     const int head = t / per_head, i = (t - head * per_head) * 4;
-    if (head >= nq + 2 * nkv) return;
+    if (head >= nq + 2 * nkv) {
+        trace_end(tr);
+        return;
+    }
     const int n1 = head * D + i, n2 = n1 + half;
     const float4 s1 = sk_sum4(a, B, b, n1), s2 = sk_sum4(a, B, b, n2);
     float x1[4] = {s1.x, s1.y, s1.z, s1.w}, x2[4] = {s2.x, s2.y, s2.z, s2.w};
@@ -377,33 +381,35 @@ __global__ void sk_qkv_rope_kernel(SkSlabs a, int B, const __half* __restrict__ 
     w2.y = *reinterpret_cast<uint32_t*>(&q1);
     *reinterpret_cast<uint2*>(dst + i) = w1;
     *reinterpret_cast<uint2*>(dst + i + half) = w2;
+    trace_end(tr);
 }
 
 // hidden[b] = (add ? hidden[b] : 0) + projection; then, when norm_w is set,
-// xn[b] = half(hidden[b] * rsqrt(mean(hidden[b]^2) + eps) * norm_w).  A
-// cluster of kAddNormCtas CTAs per row (grid (kAddNormCtas, B)), each over
-// H / kAddNormCtas columns, 4 per thread; the row's sum of squares is the
-// sum of the CTAs' partials read through distributed shared memory in rank
-// order (the same order in every CTA, so deterministic).
-constexpr int kAddNormCtas = 8;
+// xn[b] = half(hidden[b] * rsqrt(mean(hidden[b]^2) + eps) * norm_w).  One
+// 1024-thread CTA per row (grid B), 4 columns per thread and pass; the row's
+// sum of squares is reduced inside the CTA (warp trees, then the 32 warps in
+// order, so deterministic).  (An 8-CTA cluster per row, partials shared
+// through distributed shared memory, took 7.4 us against 5.5 at batch 8.)
+constexpr int kAddNormRowThreads = 1024;
 
-__global__ void __launch_bounds__(128) sk_add_norm_kernel(SkSlabs a, int B, float* __restrict__ hidden, int add,
-                                                          int H, const __half* __restrict__ norm_w,
-                                                          __half* __restrict__ xn, float eps) {
-    __shared__ float red[4];
-    __shared__ float part;
+__global__ void __launch_bounds__(kAddNormRowThreads) sk_add_norm_kernel(SkSlabs a, int B,
+                                                                            float* __restrict__ hidden, int add,
+                                                                            int H, const __half* __restrict__ norm_w,
+                                                                            __half* __restrict__ xn, float eps,
+                                                                            TraceSlot tr) {
+    __shared__ float red[kAddNormRowThreads / 32];
+    __shared__ float s_rs;
     griddep_wait();
     griddep_launch_dependents();
-    const int b = blockIdx.y;
-    const int cols = H / kAddNormCtas;
-    const int c0 = blockIdx.x * cols;
+    trace_begin(tr);
+    const int b = blockIdx.x;
     constexpr int kMaxV = 4;  // float4 groups per thread (H <= 16384)
     float4 hv[kMaxV];
     float ss = 0.f;
 #pragma unroll
     for (int k = 0; k < kMaxV; ++k) {
-        const int n = c0 + 4 * ((int)threadIdx.x + k * (int)blockDim.x);
-        if (n < c0 + cols) {
+        const int n = 4 * ((int)threadIdx.x + k * kAddNormRowThreads);
+        if (n < H) {
             float4 v = sk_sum4(a, B, b, n);
             float4* h = reinterpret_cast<float4*>(hidden + (int64_t)b * H + n);
             if (add) {
@@ -415,39 +421,42 @@ __global__ void __launch_bounds__(128) sk_add_norm_kernel(SkSlabs a, int B, floa
             ss = fmaf(v.x, v.x, ss); ss = fmaf(v.y, v.y, ss); ss = fmaf(v.z, v.z, ss); ss = fmaf(v.w, v.w, ss);
         }
     }
-    if (!norm_w) return;  // uniform over the grid
-    for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
-    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = ss;
-    __syncthreads();
-    if (threadIdx.x == 0) part = (red[0] + red[1]) + (red[2] + red[3]);
-    cg::cluster_group cl = cg::this_cluster();
-    cl.sync();
-    float tot = 0.f;
-    for (int r = 0; r < kAddNormCtas; ++r) tot += *cl.map_shared_rank(&part, r);
-    cl.sync();  // no CTA leaves while another still reads its partial
-    const float rs = rsqrtf(tot / (float)H + eps);
+    if (norm_w) {  // uniform over the grid
+        ss = warp_sum(ss);
+        if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = ss;
+        __syncthreads();
+        if (threadIdx.x == 0) {
+            float tot = 0.f;
+            for (int w = 0; w < kAddNormRowThreads / 32; ++w) tot += red[w];
+            s_rs = rsqrtf(tot / (float)H + eps);
+        }
+        __syncthreads();
+        const float rs = s_rs;
 #pragma unroll
-    for (int k = 0; k < kMaxV; ++k) {
-        const int n = c0 + 4 * ((int)threadIdx.x + k * (int)blockDim.x);
-        if (n < c0 + cols) {
-            const float4 v = hv[k];
-            const uint2 wv = *reinterpret_cast<const uint2*>(norm_w + n);
-            const float2 w01 = __half22float2(*reinterpret_cast<const __half2*>(&wv.x));
-            const float2 w23 = __half22float2(*reinterpret_cast<const __half2*>(&wv.y));
-            __half2 o0 = __floats2half2_rn(v.x * rs * w01.x, v.y * rs * w01.y);
-            __half2 o1 = __floats2half2_rn(v.z * rs * w23.x, v.w * rs * w23.y);
-            uint2 ov;
-            ov.x = *reinterpret_cast<uint32_t*>(&o0);
-            ov.y = *reinterpret_cast<uint32_t*>(&o1);
-            *reinterpret_cast<uint2*>(xn + (int64_t)b * H + n) = ov;
+        for (int k = 0; k < kMaxV; ++k) {
+            const int n = 4 * ((int)threadIdx.x + k * kAddNormRowThreads);
+            if (n < H) {
+                const float4 v = hv[k];
+                const uint2 wv = *reinterpret_cast<const uint2*>(norm_w + n);
+                const float2 w01 = __half22float2(*reinterpret_cast<const __half2*>(&wv.x));
+                const float2 w23 = __half22float2(*reinterpret_cast<const __half2*>(&wv.y));
+                __half2 o0 = __floats2half2_rn(v.x * rs * w01.x, v.y * rs * w01.y);
+                __half2 o1 = __floats2half2_rn(v.z * rs * w23.x, v.w * rs * w23.y);
+                uint2 ov;
+                ov.x = *reinterpret_cast<uint32_t*>(&o0);
+                ov.y = *reinterpret_cast<uint32_t*>(&o1);
+                *reinterpret_cast<uint2*>(xn + (int64_t)b * H + n) = ov;
+            }
         }
     }
+    trace_end(tr);
 }
 
 // act[b][i] = half(silu(gate) * up), silu(x) = x / (1 + exp(-x)) in fp32
-__global__ void sk_swiglu_kernel(SkSlabs g, SkSlabs u, int B, int I, __half* __restrict__ act) {
+__global__ void sk_swiglu_kernel(SkSlabs g, SkSlabs u, int B, int I, __half* __restrict__ act, TraceSlot tr) {
     griddep_wait();
     griddep_launch_dependents();
+    trace_begin(tr);
     const int64_t n = (int64_t)B * I / 4;
     for (int64_t e = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; e < n; e += (int64_t)gridDim.x * blockDim.x) {
         const int b = (int)(4 * e / I), i = (int)(4 * e - (int64_t)b * I);
@@ -459,16 +468,18 @@ __global__ void sk_swiglu_kernel(SkSlabs g, SkSlabs u, int B, int I, __half* __r
         ov.y = *reinterpret_cast<uint32_t*>(&o1);
         *reinterpret_cast<uint2*>(act + 4 * e) = ov;
     }
+    trace_end(tr);
 }
 
 // logits[b][v] = lm_head projection (fp32) and the packed argmax of each row
 // (ties to the lower id, ids >= limit excluded); argmax zeroed before.
 // grid (chunks, B), 256 threads.
 __global__ void sk_logits_argmax_kernel(SkSlabs a, int B, float* __restrict__ logits, int V, int row_offset,
-                                        int limit, unsigned long long* __restrict__ argmax) {
+                                        int limit, unsigned long long* __restrict__ argmax, TraceSlot tr) {
     __shared__ unsigned long long red[32];
     griddep_wait();
     griddep_launch_dependents();
+    trace_begin(tr);
     const int b = blockIdx.y;
     unsigned long long best = 0ull;
     for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < V; i += gridDim.x * blockDim.x) {
@@ -490,6 +501,7 @@ __global__ void sk_logits_argmax_kernel(SkSlabs a, int B, float* __restrict__ lo
         for (int w = 1; w < (int)(blockDim.x >> 5); ++w) best = red[w] > best ? red[w] : best;
         if (best) atomicMax(argmax + b, best);
     }
+    trace_end(tr);
 }
 
 // ---------------------------------------------------------------------------
@@ -850,7 +862,7 @@ static int model_create(const b2_model_config* cfg, int tp_rank, int tp_size, co
     M_ALLOC(m->seq_lens, (size_t)B * sizeof(int));
     M_ALLOC(m->hidden2, (size_t)B * H * sizeof(float));
     if (!gemv_step(m, B)) {  // batched decode step: skinny partial slabs, q|k|v rows, normed rows
-        if (H % (4 * kAddNormCtas) || H > 16 * 128 * kAddNormCtas || m->inter % 4 || D % 8) {
+        if (H % 4 || H > 4 * 4 * kAddNormRowThreads || m->inter % 4 || D % 8) {
             b2_model_destroy(m);
             return B2_ERR_UNSUPPORTED;
         }
@@ -1322,7 +1334,7 @@ static int launch_lm_head(b2_model* m, int B, bool pdl, bool xch = false) {
 static int sk_proj(b2_model* m, const __half* X, int B, const __half* W0, int N0, const __half* W1, int N1, int K,
                    float* ws, SkSlabs* out) {
     SkinnyPlan pl;
-    M_TRY(gemm_skinny(X, B, W0, N0, W1, N1, K, ws, m->bws_floats, &pl, m->stream));
+    M_TRY(gemm_skinny(X, B, W0, N0, W1, N1, K, ws, m->bws_floats, &pl, m->stream, next_trace(m)));
     out->ws = ws;
     out->N = N0 + N1;
     out->nk = pl.nk;
@@ -1340,7 +1352,7 @@ static int lm_head_rows(b2_model* m, int B) {
     const int limit = c.vocab_size > 151665 ? 151665 : c.vocab_size;
     const unsigned chunks = (unsigned)((m->vocab_l + 4095) / 4096);
     B2_TRY(launch(sk_logits_argmax_kernel, dim3(chunks, (unsigned)B), dim3(256), 0, m->stream, true, lg, B,
-                  m->logits, m->vocab_l, m->vocab_off, limit, m->argmax));
+                  m->logits, m->vocab_l, m->vocab_off, limit, m->argmax, next_trace(m)));
     return B2_OK;
 }
 
@@ -1354,13 +1366,12 @@ static int add_and_norm(b2_model* m, const SkSlabs& a, int B, const __half* norm
     const int H = c.hidden_size;
     const int add = m->rank == 0 ? 1 : 0;
     if (m->tp == 1) {
-        B2_TRY(launch_cluster(sk_add_norm_kernel, dim3(kAddNormCtas, (unsigned)B), dim3(128), 0, m->stream, true,
-                              kAddNormCtas, a, B, m->hidden, add, H, norm_w, m->bxn, c.rms_norm_eps));
+        B2_TRY(launch(sk_add_norm_kernel, dim3((unsigned)B), dim3(kAddNormRowThreads), 0, m->stream, true, a, B,
+                      m->hidden, add, H, norm_w, m->bxn, c.rms_norm_eps, next_trace(m)));
         return B2_OK;
     }
-    B2_TRY(launch_cluster(sk_add_norm_kernel, dim3(kAddNormCtas, (unsigned)B), dim3(128), 0, m->stream, true,
-                          kAddNormCtas, a, B, m->hidden, add, H, (const __half*)nullptr, (__half*)nullptr,
-                          c.rms_norm_eps));
+    B2_TRY(launch(sk_add_norm_kernel, dim3((unsigned)B), dim3(kAddNormRowThreads), 0, m->stream, true, a, B,
+                  m->hidden, add, H, (const __half*)nullptr, (__half*)nullptr, c.rms_norm_eps, next_trace(m)));
     M_TRY(nccl_sum_hidden(m, B));
     rmsnorm_rows_kernel<<<B, 256, 0, m->stream>>>(m->hidden, norm_w, m->bxn, H, c.rms_norm_eps);
     B2_CHECK_LAUNCH();
@@ -1380,7 +1391,7 @@ static int enqueue_step_batched(b2_model* m, int B) {
     const bool fuse_gu = (I % 128) == 0;
     B2_TRY(launch(step_begin_kernel, dim3(B), dim3(256), 0, s, true, (const int64_t*)m->tokens,
                   (const int*)m->positions, (const __half*)m->embed, m->hidden, H, m->seq_lens, m->argmax, m->hist,
-                  (const int*)m->hist_count, m->hist_cap, TraceSlot{nullptr, 0}));
+                  (const int*)m->hist_count, m->hist_cap, next_trace(m)));
     rmsnorm_rows_kernel<<<B, 256, 0, s>>>(m->hidden, m->layers[0].ln1, m->bxn, H, c.rms_norm_eps);
     B2_CHECK_LAUNCH();
     for (int l = 0; l < c.num_layers; ++l) {
@@ -1391,19 +1402,21 @@ static int enqueue_step_batched(b2_model* m, int B) {
         const unsigned qkv_threads = (unsigned)((m->nq + 2 * m->nkv) * (D / 8));
         B2_TRY(launch(sk_qkv_rope_kernel, dim3((unsigned)B, (qkv_threads + 255) / 256), dim3(256), 0, s, true,
                       qkv, B, (const __half*)w.bqkv, m->bqkv, (int64_t)R, (const float2*)m->rope, m->nq, m->nkv, D,
-                      layer_kv(m, l), (const int*)m->positions));
+                      layer_kv(m, l), (const int*)m->positions, next_trace(m)));
+        const TraceSlot tr_attn = next_trace(m);
         if (m->paged) {
-            M_TRY(launch_attn_paged(m, l, m->bqkv, R, B, 0, TraceSlot{nullptr, 0}));
+            M_TRY(launch_attn_paged(m, l, m->bqkv, R, B, 0, tr_attn));
         } else {
             const int rc = attn_cl_launch(m->bqkv, R, m->attn, qd, kbase, kbase + m->kv_s_kv, m->kv_s_batch,
                                           m->kv_s_head, D, c.max_seq, m->seq_lens, 0, B, m->nq, m->nkv, D, 1, 0,
-                                          TraceSlot{nullptr, 0}, s, true);
+                                          tr_attn, s, true);
             if (rc == B2_ERR_UNSUPPORTED)
                 M_TRY(attn_decode_launch_step_q(m->bqkv, R, kbase, kbase + m->kv_s_kv, m->kv_s_batch, m->kv_s_head, D,
                                                 m->seq_lens, m->attn, m->part, m->splits, B, m->nq, m->nkv, D, s));
             else
                 M_TRY(rc);
         }
+        const __half* next_ln = l + 1 < c.num_layers ? m->layers[l + 1].ln1 : m->final_norm;
         M_TRY(sk_proj(m, m->attn, B, w.wo, H, nullptr, 0, qd, m->bws_a, &o));
         M_TRY(add_and_norm(m, o, B, w.ln2));
         if (fuse_gu) {
@@ -1417,10 +1430,11 @@ static int enqueue_step_batched(b2_model* m, int B) {
         {
             int64_t blocks = ((int64_t)B * I / 4 + 255) / 256;
             if (blocks > (int64_t)sm_count() * 8) blocks = (int64_t)sm_count() * 8;
-            B2_TRY(launch(sk_swiglu_kernel, dim3((unsigned)blocks), dim3(256), 0, s, true, g, u, B, I, m->act));
+            B2_TRY(launch(sk_swiglu_kernel, dim3((unsigned)blocks), dim3(256), 0, s, true, g, u, B, I, m->act,
+                          next_trace(m)));
         }
         M_TRY(sk_proj(m, m->act, B, w.wd, H, nullptr, 0, I, m->bws_a, &d));
-        M_TRY(add_and_norm(m, d, B, l + 1 < c.num_layers ? m->layers[l + 1].ln1 : m->final_norm));
+        M_TRY(add_and_norm(m, d, B, next_ln));
     }
     M_TRY(lm_head_rows(m, B));
     if (m->sampling)
@@ -1431,7 +1445,7 @@ static int enqueue_step_batched(b2_model* m, int B) {
     }
     B2_TRY(launch(step_end_kernel, dim3(1), dim3(end_threads(B)), 0, s, true, (const unsigned long long*)m->argmax,
                   m->tokens, m->positions, B, m->hist_count, m->hist_cap, 0, (const unsigned long long*)nullptr,
-                  (const unsigned*)nullptr, m->tp, c.max_batch, m->step_ctr, (int*)nullptr, TraceSlot{nullptr, 0}));
+                  (const unsigned*)nullptr, m->tp, c.max_batch, m->step_ctr, (int*)nullptr, next_trace(m)));
     return B2_OK;
 }
 

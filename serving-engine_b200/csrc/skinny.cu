@@ -42,7 +42,7 @@ template <int NB>
 __global__ void __launch_bounds__(192, 1)
     skinny_kernel(const __grid_constant__ CUtensorMap tmW0, const __grid_constant__ CUtensorMap tmW1,
                   const __grid_constant__ CUtensorMap tmX, float* __restrict__ ws, int B, int N, int T0, int nk,
-                  int per, int total, int* err) {
+                  int per, int total, int* err, TraceSlot tr) {
     using Cfg = SkCfg<NB>;
     constexpr int STAGES = Cfg::STAGES;
     extern __shared__ uint8_t smem_raw[];
@@ -135,6 +135,7 @@ __global__ void __launch_bounds__(192, 1)
         }
     } else {
         griddep_wait();  // ws may still be read by the previous kernel
+        trace_begin(tr);
         const uint32_t lane_base = (uint32_t)(warp * 32) << 16;
         int seg = 0;
         for (int it = it0; it < it1; ++seg) {
@@ -169,6 +170,7 @@ __global__ void __launch_bounds__(192, 1)
         tc::fence_after_sync();
         tc::tmem_dealloc(tmem, Cfg::TMEM_COLS);
     }
+    trace_end(tr);
 }
 
 SkinnyPlan skinny_plan(int N, int K) {
@@ -189,7 +191,7 @@ SkinnyPlan skinny_plan(int N, int K) {
 
 template <int NB>
 static int launch_skinny(const CUtensorMap& w0, const CUtensorMap& w1, const __half* X, int B, int N, int T0, int K,
-                         float* ws, const SkinnyPlan& pl, int* err, cudaStream_t s) {
+                         float* ws, const SkinnyPlan& pl, int* err, cudaStream_t s, TraceSlot tr) {
     using Cfg = SkCfg<NB>;
     CUtensorMap tx;
     const uint64_t dx[2] = {(uint64_t)K, (uint64_t)B}, sx[1] = {(uint64_t)K * 2};
@@ -200,12 +202,12 @@ static int launch_skinny(const CUtensorMap& w0, const CUtensorMap& w1, const __h
     B2_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)Cfg::SMEM));
     const int total = ((N + 127) / 128) * pl.nk;
     B2_TRY(launch(kern, dim3((unsigned)pl.ctas), dim3(192), Cfg::SMEM, s, true, w0, w1, tx, ws, B, N, T0, pl.nk,
-                  pl.per, total, err));
+                  pl.per, total, err, tr));
     return B2_OK;
 }
 
 int gemm_skinny(const __half* X, int B, const __half* W0, int N0, const __half* W1, int N1, int K, float* ws,
-                size_t ws_floats, SkinnyPlan* plan, cudaStream_t s) {
+                size_t ws_floats, SkinnyPlan* plan, cudaStream_t s, TraceSlot tr) {
     if (B < 1 || B > 256 || N0 < 1 || K < 8 || (K & 7) || N1 < 0 || (N1 > 0 && (!W1 || (N0 & 127)))) return B2_ERR_INVALID;
     if (!aligned16(X) || !aligned16(W0) || (W1 && !aligned16(W1))) return B2_ERR_UNSUPPORTED;
     int* err = wait_error_word();
@@ -229,10 +231,10 @@ int gemm_skinny(const __half* X, int B, const __half* W0, int N0, const __half* 
         w1 = w0;
     }
     const int T0 = N1 > 0 ? N0 / 128 : (N0 + 127) / 128;
-    if (B <= 32) return launch_skinny<32>(w0, w1, X, B, N, T0, K, ws, pl, err, s);
-    if (B <= 64) return launch_skinny<64>(w0, w1, X, B, N, T0, K, ws, pl, err, s);
-    if (B <= 128) return launch_skinny<128>(w0, w1, X, B, N, T0, K, ws, pl, err, s);
-    return launch_skinny<256>(w0, w1, X, B, N, T0, K, ws, pl, err, s);
+    if (B <= 32) return launch_skinny<32>(w0, w1, X, B, N, T0, K, ws, pl, err, s, tr);
+    if (B <= 64) return launch_skinny<64>(w0, w1, X, B, N, T0, K, ws, pl, err, s, tr);
+    if (B <= 128) return launch_skinny<128>(w0, w1, X, B, N, T0, K, ws, pl, err, s, tr);
+    return launch_skinny<256>(w0, w1, X, B, N, T0, K, ws, pl, err, s, tr);
 }
 
 }  // namespace b2

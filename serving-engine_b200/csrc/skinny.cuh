@@ -30,7 +30,8 @@ SkinnyPlan skinny_plan(int N, int K);
 // else N0 % 128 == 0).  X [B][K] half, rows K apart; W row-major [rows][K].
 // B <= 256, K % 8 == 0, 16-byte aligned bases.  ws must hold
 // plan.max_slabs * B * (N0 + N1) floats (B2_ERR_INVALID otherwise).
+// tr: the step trace's slot for this launch (buf null: off).
 int gemm_skinny(const __half* X, int B, const __half* W0, int N0, const __half* W1, int N1, int K, float* ws,
-                size_t ws_floats, SkinnyPlan* plan, cudaStream_t s);
+                size_t ws_floats, SkinnyPlan* plan, cudaStream_t s, TraceSlot tr = TraceSlot{nullptr, 0});
 
 }  // namespace b2
