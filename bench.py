@@ -552,21 +552,28 @@ def run_b2(args, rank, world, local):
 # kernel microbenchmarks (BASELINE configs 2 and 3, prefill projections)
 # ---------------------------------------------------------------------------
 
-def _events_time(fn, iters, flush=None):
-    """Median per-call milliseconds over `iters` calls timed with CUDA events on
-    the current stream; `flush` (if given) runs before each call, outside the
-    timed interval."""
+def _events_time(fn, iters, flush=None, back_to_back=10):
+    """Median per-call milliseconds over `iters` samples timed with CUDA
+    events on the current stream.  With `flush`, one call per sample, the
+    flush (an L2-sized memset) enqueued first: the call is queued behind it,
+    so the host's launch work never leaves the device idle inside the timed
+    interval.  Without, `back_to_back` calls per sample (the device time of
+    a call, not the host's time to issue it)."""
     import torch
     times = []
     for _ in range(iters):
+        reps = 1
         if flush is not None:
             flush()
+        else:
+            reps = back_to_back
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         e0.record()
-        fn()
+        for _ in range(reps):
+            fn()
         e1.record()
         e1.synchronize()
-        times.append(e0.elapsed_time(e1))
+        times.append(e0.elapsed_time(e1) / reps)
     return statistics.median(times)
 
 

@@ -67,7 +67,17 @@ __global__ void __launch_bounds__(192, 1)
     griddep_wait();  // A may be the previous kernel's output
     griddep_launch_dependents();
 
-    const int m0 = blockIdx.y * kTcBM, n0 = blockIdx.x * BN;
+    // Tile of this CTA: tiles in groups of up to kGroupM M-tiles, the M index
+    // fastest inside a group, so the CTAs in flight together share each B
+    // (weight) tile and B streams through L2 once per group instead of once
+    // per row of M-tiles (2048 x 4096 x 28672: 235 MB of B read once rather
+    // than 16 times).
+    constexpr int kGroupM = 16;
+    const int tilesM = (M + kTcBM - 1) / kTcBM, tilesN = (N + BN - 1) / BN;
+    const int grp = (int)blockIdx.x / (kGroupM * tilesN);
+    const int gm = min(kGroupM, tilesM - grp * kGroupM);
+    const int local = (int)blockIdx.x - grp * kGroupM * tilesN;
+    const int m0 = (grp * kGroupM + local % gm) * kTcBM, n0 = (local / gm) * BN;
     // split-K: this CTA's k blocks [kb0, kb1); split z writes slab z of C
     const int nk_all = (K + kTcBK - 1) / kTcBK;
     const int kb0 = blockIdx.z * kb_per_split;
@@ -180,7 +190,7 @@ static int launch_tc(const CUtensorMap& ta, const CUtensorMap& tb, void* C, int 
     const int nk = (K + kTcBK - 1) / kTcBK;
     const int kbps = (nk + ksplit - 1) / ksplit;
     ksplit = (nk + kbps - 1) / kbps;  // no empty split
-    dim3 grid((unsigned)((N + BN - 1) / BN), (unsigned)((M + kTcBM - 1) / kTcBM), (unsigned)ksplit);
+    dim3 grid((unsigned)(((N + BN - 1) / BN) * ((M + kTcBM - 1) / kTcBM)), 1u, (unsigned)ksplit);
     B2_TRY(launch(kern, grid, dim3(192), smem, s, true, ta, tb, C, M, N, K, kbps, err));
     return B2_OK;
 }
