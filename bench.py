@@ -261,8 +261,10 @@ def config_dict(args, world):
             "ctx_range": [args.prompt + args.warmup, args.prompt + args.warmup + args.steps],
             "parallelism": f"tp{world}",
             "tp_exchange": (args.exchange if world > 1 else None),
+            "weights": ("fp16" if args.weights == "fp16" else
+                        "fp8 e4m3 per-row copies for the decode GEMVs (b2_model_quantize_weights)"),
             "l2": f"inputs larger than L2: every step streams the model's {weight_gb(c):.1f} GB of fp16 weights "
-                  f"(divided over the tensor-parallel ranks; L2 126 MB)"}
+                  f"(half that as fp8; divided over the tensor-parallel ranks; L2 126 MB)"}
 
 
 # ---------------------------------------------------------------------------
@@ -363,6 +365,8 @@ def run_b2(args, rank, world, local):
                  theta=c["theta"], tied=False, max_batch=B, max_seq=max_seq, tp_rank=rank, tp_size=world,
                  nccl_id=nccl_id, kv_blocks=kv_blocks, block_size=PAGE)
     m.init_random(SEED_W, 0.02)
+    if args.weights == "fp8":  # decode GEMVs on per-row FP8 copies (prefill stays fp16)
+        m.quantize_weights("fp8")
     if world > 1 and args.exchange == "p2p":
         # decode-step partial sums over NVLink peer memory (fused into the
         # GEMVs) instead of NCCL all-reduces
@@ -510,7 +514,8 @@ def run_b2(args, rank, world, local):
         out = {
             "metric": METRIC, "value": B * K / (ms * 1e-3), "unit": "tok/s", "n_gpus": world, "steps": K,
             "warmup": W, "ms_per_step": step_ms, "higher_is_better": True, "scaling": "strong",
-            "vs_baseline": None, "dtype": "f16",
+            "vs_baseline": None,
+            "dtype": "f16" if args.weights == "fp16" else "f16 activations, fp8 e4m3 weights (per-row fp32 scales)",
             "data": "synthetic: seeded random-init fp16 weights ~N(0,0.02), uniform random prompt ids",
             "config": config_dict(args, world),
             "e2e": ({"value": B * K / (ms_e2e * 1e-3), "unit": "tok/s",
@@ -523,7 +528,8 @@ def run_b2(args, rank, world, local):
                      "api": "b2_model_decode_step (host token + position in, fp32 logits into a reused page-locked "
                             "host buffer + next id out)"}),
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
-                         "frac": achieved / peak, "traffic": ncu_traffic("gate_up") if ktimes else None,
+                         "frac": achieved / peak,
+                         "traffic": ncu_traffic("gate_up") if ktimes and args.weights == "fp16" else None,
                          "kernel": dom_name, "bytes_per_launch": dom_bytes, "launch_ms": dom_ms,
                          "peak_source": peak_src},
             "step_roofline": {"bytes_per_step": step_bytes, "achieved": step_gbs, "peak": peak, "unit": "GB/s",
@@ -539,7 +545,7 @@ def run_b2(args, rank, world, local):
             out["trace"] = trace
         if parity is not None:
             out["tp_parity"] = parity
-        if world == 1 and not args.no_cpu_baseline and args.model == "llama3-8b":
+        if world == 1 and not args.no_cpu_baseline and args.model == "llama3-8b" and args.weights == "fp16":
             try:
                 out["cpu_baseline"] = cpu_baseline_single(c, ctx_mid + 1)
             except Exception as ex:  # reported, never fatal
@@ -702,6 +708,9 @@ def main():
     ap.add_argument("--prompt", type=int, default=PROMPT, help="prompt length (512 for the metric)")
     ap.add_argument("--layers", type=int, default=0,
                     help="decoder depth override (reduced only for small profiler captures; 0 = the model's)")
+    ap.add_argument("--weights", default="fp16", choices=["fp16", "fp8"],
+                    help="decode GEMV weights: fp16 (the metric), or per-row FP8 E4M3 copies "
+                         "(b2_model_quantize_weights; batches the GEMV step takes)")
     ap.add_argument("--paged", action="store_true",
                     help="paged KV cache (16-position blocks scattered over a pool), mixed prompt lengths "
                          "prompt/2 .. 3*prompt/2, prefilled one sequence at a time")

@@ -220,6 +220,19 @@ int b2_gemv_residual(const void* W, const void* x, const void* r, void* y, int N
 int b2_gemv_batched(const void* W, const void* x, const void* extra, void* y, int B, int N, int K,
                     int epilogue, int out_f32, void* stream);
 
+/* FP8 weights (OCP E4M3) for the decode GEMVs: per row r of w [rows, K]
+ * (half), scales[r] = max|w[r,:]| / 448 (1 for an all-zero row) and
+ * q[r,k] = E4M3(w[r,k] / scales[r]), round to nearest even, saturating.
+ * q: rows * K bytes.  New API (the reference plans INT8/INT4 weights,
+ * RESULTS.md:39). */
+int b2_quantize_fp8_rows(const void* w, int64_t rows, int K, void* q, float* scales, void* stream);
+
+/* y[b,n] = scales[n] * dot(E4M3 Wq[n,:], x[b,:]), x [B,K] half, fp32
+ * accumulate, y [B,N] half (out_f32 != 0: fp32).  K % 16 == 0, 16-byte
+ * aligned Wq and x.  The decode GEMV of a quantised model.  New API. */
+int b2_gemv_fp8(const void* Wq, const float* scales, const void* x, void* y, int B, int N, int K, int out_f32,
+                void* stream);
+
 /* Copy K/V rows [num_tokens, nkv, D] into head-major caches [nkv, max_seq, D]
  * at positions start_pos..start_pos+num_tokens-1 (positions >= max_seq are
  * skipped).  Replaces engine::cuda::append_kv_cache (src/runtime/kv_cache.h:80-91). */
@@ -365,6 +378,19 @@ int b2_model_set_tensor_bf16(b2_model* m, const char* name, const uint16_t* host
  * 1 when sampling.  Synchronises.  New API (the reference samples on the
  * host, src/runtime/sampler.cu:253-339, apps/generate.cpp:884-898). */
 int b2_model_set_sampling(b2_model* m, const b2_sampler_config* cfg);
+
+/* Weight format of the decode GEMVs (batches the GEMV step takes: 1-8
+ * sequences, or fewer at widths that cap its batch tile).
+ * B2_WEIGHTS_FP8_E4M3 quantises every projection and the lm_head per output
+ * row (b2_quantize_fp8_rows) from the fp16 weights the model holds now, on
+ * the device, into copies allocated on first use, and the decode GEMVs then
+ * stream 1-byte weights -- half the bytes of a decode step.  Prefill and the
+ * batched tensor-core step keep the fp16 weights.  Call again after changing
+ * weights; B2_WEIGHTS_FP16 returns to the fp16 GEMVs (the copies are kept).
+ * Synchronises.  New API (the reference plans quantised weights as P8,
+ * RESULTS.md:39). */
+enum { B2_WEIGHTS_FP16 = 0, B2_WEIGHTS_FP8_E4M3 = 1 };
+int b2_model_quantize_weights(b2_model* m, int format);
 
 /* Clears the KV cache positions of all sequences (sets lengths to 0). */
 int b2_model_reset(b2_model* m);

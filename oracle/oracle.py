@@ -444,3 +444,79 @@ class RefModel:
             self.h = None
 
     __del__ = close
+
+
+# ---------------------------------------------------------------------------
+# FP8 E4M3 weights (the quantised decode path).  The reference has no
+# quantised path (its RESULTS.md:39-40 plans INT8/INT4 weights and FP8/INT8
+# KV); this restates the OCP 8-bit floating-point format's E4M3 encoding
+# (exponent bias 7, 3 mantissa bits, no infinities, largest finite 448) with
+# round-to-nearest-even and saturation, and the per-row scaling that
+# b2_quantize_fp8_rows documents: scale = max|w| / 448 (1 for a zero row),
+# q = E4M3(w / scale) in float32 arithmetic.
+# ---------------------------------------------------------------------------
+
+def _e4m3_positive_values() -> np.ndarray:
+    codes = np.arange(127)  # finite non-negative codes 0x00 .. 0x7e
+    e, m = codes >> 3, codes & 7
+    return np.where(e == 0, m / 8.0 * 2.0 ** -6, (1.0 + m / 8.0) * 2.0 ** (e - 7.0)).astype(np.float64)
+
+
+_E4M3 = _e4m3_positive_values()
+
+
+def e4m3_encode(x) -> np.ndarray:
+    """float32 values -> E4M3 codes (uint8): nearest, ties to the even code,
+    magnitudes above 448 saturated, the sign kept (also for zero).  Below
+    2^-6 the codes are the multiples of 2^-9; above, 3 mantissa bits per
+    binade (np.rint rounds halves to even; the scalings are exact)."""
+    x = np.asarray(x, np.float32)
+    a = np.minimum(np.abs(x), np.float32(448.0))
+    sub = a < np.float32(2.0 ** -6)
+    f, ex = np.frexp(np.where(sub, np.float32(1.0), a))      # a = f * 2^ex, f in [0.5, 1)
+    m = np.rint(f * np.float32(16.0) - np.float32(8.0))       # 3-bit mantissa, 8 = carry
+    e = ex.astype(np.int32) - 1 + (m == 8)
+    m = np.where(m == 8, 0, m).astype(np.int32)
+    code = np.where(sub, np.rint(a * np.float32(2.0 ** 9)).astype(np.int32), ((e + 7) << 3) | m)
+    code = np.minimum(code, 126)
+    return (code.astype(np.uint8) | (np.signbit(x).astype(np.uint8) << 7)).astype(np.uint8)
+
+
+def e4m3_decode(q) -> np.ndarray:
+    q = np.asarray(q, np.uint8)
+    v = _E4M3[np.minimum(q & 0x7F, 126)].astype(np.float32)
+    return np.where(q & 0x80, -v, v).astype(np.float32)
+
+
+def quantize_e4m3_rows(w):
+    """Per-row E4M3 codes and float32 scales of a [rows, K] matrix (in
+    blocks of rows, to bound the temporaries of large matrices)."""
+    w = np.asarray(w, np.float32)
+    amax = np.max(np.abs(w), axis=1)
+    scale = np.where(amax > 0, amax / np.float32(448.0), np.float32(1.0)).astype(np.float32)
+    q = np.empty(w.shape, np.uint8)
+    step = max(1, (1 << 23) // max(1, w.shape[1]))
+    for r0 in range(0, w.shape[0], step):
+        q[r0:r0 + step] = e4m3_encode((w[r0:r0 + step] / scale[r0:r0 + step, None]).astype(np.float32))
+    return q, scale
+
+
+def dequantize_e4m3_rows(q, scale) -> np.ndarray:
+    return (e4m3_decode(q) * np.asarray(scale, np.float32)[:, None]).astype(np.float32)
+
+
+def fp8_weights(w: dict) -> dict:
+    """The seeded weights with every projection and the lm_head replaced by
+    their per-row E4M3 round trip, rounded to fp16 (the oracle's weight
+    type): what a model quantised with b2_model_quantize_weights decodes
+    with, up to that fp16 rounding."""
+    out = dict(w)
+    out["layers"] = []
+    for L in w["layers"]:
+        M = dict(L)
+        for n in ("wq", "wk", "wv", "wo", "wg", "wu", "wd"):
+            M[n] = f16(dequantize_e4m3_rows(*quantize_e4m3_rows(L[n])))
+        out["layers"].append(M)
+    if "lm_head" in w:
+        out["lm_head"] = f16(dequantize_e4m3_rows(*quantize_e4m3_rows(w["lm_head"])))
+    return out

@@ -72,6 +72,8 @@ _SIGS = {
     "b2_gemv_bias": (i32, [vp, vp, vp, vp, i32, i32, vp]),
     "b2_gemv_residual": (i32, [vp, vp, vp, vp, i32, i32, vp]),
     "b2_gemv_batched": (i32, [vp, vp, vp, vp, i32, i32, i32, i32, i32, vp]),
+    "b2_quantize_fp8_rows": (i32, [vp, i64, i32, vp, vp, vp]),
+    "b2_gemv_fp8": (i32, [vp, vp, vp, vp, i32, i32, i32, i32, vp]),
     "b2_append_kv_cache": (i32, [vp, vp, vp, vp, i32, i32, i32, i32, i32, vp]),
     "b2_sampler_create": (i32, [i32, i32, C.POINTER(vp)]),
     "b2_sampler_destroy": (i32, [vp]),
@@ -94,6 +96,7 @@ _SIGS = {
     "b2_model_forward_logits": (i32, [vp, vp, i32, vp]),
     "b2_model_reset": (i32, [vp]),
     "b2_model_set_sampling": (i32, [vp, C.POINTER(SamplerConfig)]),
+    "b2_model_quantize_weights": (i32, [vp, i32]),
     "b2_model_prefill": (i32, [vp, vp, i32, i32, vp]),
     "b2_model_decode_step": (i32, [vp, vp, vp, i32, vp, vp]),
     "b2_model_decode_enqueue": (i32, [vp, vp, vp, i32, vp]),
@@ -324,6 +327,13 @@ class Model:
         (temperature 0: greedy); resets every sequence's LCG state."""
         cfg = SamplerConfig(temperature, top_k, top_p, 1.0, seed)
         call("b2_model_set_sampling", self.h, C.byref(cfg))
+
+    WEIGHTS = {"fp16": 0, "fp8": 1}
+
+    def quantize_weights(self, fmt="fp8"):
+        """Decode GEMVs on per-row FP8 (E4M3) copies of the weights ("fp8"),
+        or back on the fp16 weights ("fp16")."""
+        call("b2_model_quantize_weights", self.h, self.WEIGHTS[fmt])
 
     def prefill(self, ids, want_logits=True):
         import numpy as np

@@ -176,6 +176,28 @@ __device__ __forceinline__ uint32_t f2_to_h2(float a, float b) {
     return *reinterpret_cast<uint32_t*>(&h);
 }
 
+// acc + a * b for the low (H = 0) or high (H = 1) halves of two half2
+// words: sm_100's mixed-precision FMA (f16 operands, f32 addend and result,
+// one rounding) -- the value of fmaf(float(a), float(b), acc), since every
+// half converts to float exactly, in one instruction instead of three.
+template <int H>
+__device__ __forceinline__ float fma_f16_f32(uint32_t a, uint32_t b, float acc) {
+    const unsigned short x = (unsigned short)(H ? (a >> 16) : (a & 0xffffu));
+    const unsigned short y = (unsigned short)(H ? (b >> 16) : (b & 0xffffu));
+    asm("fma.rn.f32.f16 %0, %1, %2, %0;" : "+f"(acc) : "h"(x), "h"(y));
+    return acc;
+}
+
+// dot8 with the mixed-precision FMA: the same products in the same order,
+// so the same bits.
+__device__ __forceinline__ float dot8_mixed(const uint4& w, const uint4& x, float acc) {
+    acc = fma_f16_f32<0>(w.x, x.x, acc); acc = fma_f16_f32<1>(w.x, x.x, acc);
+    acc = fma_f16_f32<0>(w.y, x.y, acc); acc = fma_f16_f32<1>(w.y, x.y, acc);
+    acc = fma_f16_f32<0>(w.z, x.z, acc); acc = fma_f16_f32<1>(w.z, x.z, acc);
+    acc = fma_f16_f32<0>(w.w, x.w, acc); acc = fma_f16_f32<1>(w.w, x.w, acc);
+    return acc;
+}
+
 // 8-element dot product of two packed half vectors, fp32 accumulation.
 __device__ __forceinline__ float dot8(const uint4& w, const uint4& x, float acc) {
     float2 a, b;

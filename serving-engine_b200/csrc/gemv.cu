@@ -20,6 +20,8 @@
 //     before griddepcontrol.wait, overlapping the previous kernel's tail.
 // Reference kernel replaced: src/cuda/gemv.cu:28-116 (one warp per row,
 // scalar 2-byte loads, separate norm / RoPE / SwiGLU / residual kernels).
+#include <cuda_fp8.h>
+
 #include <cmath>
 #include <mutex>
 
@@ -65,27 +67,70 @@ __device__ __forceinline__ void load_rows(uint4 (&w)[R][U], const uint4* const (
     }
 }
 
-template <int R, int OM>
+// Weight row r of matrix m (0: W, 1: W2) as 16-byte chunks: 8 halves, or
+// 16 e4m3 codes when F8.
+template <bool F8>
+__device__ __forceinline__ const uint4* weight_row(const GemvParams& p, int m, int r) {
+    if constexpr (F8)
+        return reinterpret_cast<const uint4*>((m ? p.W8b : p.W8) + (size_t)r * p.K);
+    else
+        return reinterpret_cast<const uint4*>((m ? p.W2 : p.W) + (size_t)r * p.K);
+}
+
+template <int R, int OM, bool F8>
 __device__ __forceinline__ void task_rows(const GemvParams& p, int t, const uint4* (&rp)[R]) {
     if constexpr (OM == OUT_QKV) {
         const int half = p.D >> 1;
         const int h = t / half, i = t - h * half;
         const int r0 = h * p.D + i;
-        rp[0] = reinterpret_cast<const uint4*>(p.W + (size_t)r0 * p.K);
-        rp[1] = reinterpret_cast<const uint4*>(p.W + (size_t)(r0 + half) * p.K);
+        rp[0] = weight_row<F8>(p, 0, r0);
+        rp[1] = weight_row<F8>(p, 0, r0 + half);
     } else if constexpr (OM == OUT_SWIGLU) {
-        rp[0] = reinterpret_cast<const uint4*>(p.W + (size_t)t * p.K);
-        rp[1] = reinterpret_cast<const uint4*>(p.W2 + (size_t)t * p.K);
+        rp[0] = weight_row<F8>(p, 0, t);
+        rp[1] = weight_row<F8>(p, 1, t);
     } else {
-        rp[0] = reinterpret_cast<const uint4*>(p.W + (size_t)t * p.K);
+        rp[0] = weight_row<F8>(p, 0, t);
     }
+}
+
+// Per-row scales of task t's rows (FP8 weights), in task_rows' order.
+template <int R, int OM>
+__device__ __forceinline__ void task_scales(const GemvParams& p, int t, float (&sc)[R]) {
+    if constexpr (OM == OUT_QKV) {
+        const int half = p.D >> 1;
+        const int h = t / half, i = t - h * half;
+        sc[0] = p.wsc[h * p.D + i];
+        sc[1] = p.wsc[h * p.D + i + half];
+    } else if constexpr (OM == OUT_SWIGLU) {
+        sc[0] = p.wsc[t];
+        sc[1] = p.wsc2[t];
+    } else {
+        sc[0] = p.wsc[t];
+    }
+}
+
+// 16 e4m3 codes -> two chunks of 8 halves (exact: every e4m3 value is a
+// half), in element order.
+__device__ __forceinline__ void e4m3x16_to_half(const uint4& w, uint4& lo, uint4& hi) {
+    auto cvt2 = [](uint32_t bits16) -> uint32_t {
+        const __half2_raw h = __nv_cvt_fp8x2_to_halfraw2((__nv_fp8x2_storage_t)bits16, __NV_E4M3);
+        return (uint32_t)h.x | ((uint32_t)h.y << 16);
+    };
+    lo.x = cvt2(w.x & 0xffffu);
+    lo.y = cvt2(w.x >> 16);
+    lo.z = cvt2(w.y & 0xffffu);
+    lo.w = cvt2(w.y >> 16);
+    hi.x = cvt2(w.z & 0xffffu);
+    hi.y = cvt2(w.z >> 16);
+    hi.z = cvt2(w.w & 0xffffu);
+    hi.w = cvt2(w.w >> 16);
 }
 
 
 // ---------------------------------------------------------------------------
 // register-streaming form
 // ---------------------------------------------------------------------------
-template <int R, int BT, int XM, int OM, int U>
+template <int R, int BT, int XM, int OM, int U, bool F8>
 __global__ void __launch_bounds__(kGemvThreads, 2) gemv_vec_kernel(const GemvParams p) {
     extern __shared__ __align__(16) uint4 xs[];  // [BT][K8] packed half
     __shared__ float s_rs[BT];
@@ -94,8 +139,9 @@ __global__ void __launch_bounds__(kGemvThreads, 2) gemv_vec_kernel(const GemvPar
     __shared__ __align__(16) float s_push[OM == OUT_PUSH ? BT * kPushRows : 1];
 
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-    const int K8 = p.K >> 3;
-    const int NB = (K8 + 32 * U - 1) / (32 * U);
+    const int K8 = p.K >> 3;                  // 16-byte chunks of x (8 halves)
+    const int KC = F8 ? (p.K >> 4) : K8;       // 16-byte chunks of a weight row
+    const int NB = (KC + 32 * U - 1) / (32 * U);
     // Tasks are dealt round-robin over all warps of the grid, except for
     // OUT_PUSH, where each CTA owns a contiguous block of rows so that it can
     // push them to the other ranks as 16-byte stores once its stream is done.
@@ -110,8 +156,8 @@ __global__ void __launch_bounds__(kGemvThreads, 2) gemv_vec_kernel(const GemvPar
     uint4 wn[R][U];
     if (t < t_end) {
         const uint4* rp[R];
-        task_rows<R, OM>(p, t, rp);
-        load_rows<R, U>(wn, rp, 0, K8, lane);
+        task_rows<R, OM, F8>(p, t, rp);
+        load_rows<R, U>(wn, rp, 0, KC, lane);
     }
 
     // X_SUM reads the previous kernel's output only through the tagged
@@ -154,19 +200,31 @@ __global__ void __launch_bounds__(kGemvThreads, 2) gemv_vec_kernel(const GemvPar
                 if (ncb == NB) { nt = t + t_step; ncb = 0; }
                 if (nt < t_end) {
                     const uint4* rp[R];
-                    task_rows<R, OM>(p, nt, rp);
-                    load_rows<R, U>(wn, rp, ncb * 32 * U, K8, lane);
+                    task_rows<R, OM, F8>(p, nt, rp);
+                    load_rows<R, U>(wn, rp, ncb * 32 * U, KC, lane);
                 }
             }
 #pragma unroll
             for (int u = 0; u < U; ++u) {
                 const int c = cb * 32 * U + u * 32 + lane;
-                if (c < K8) {
+                if (c < KC) {
+                    if constexpr (F8) {  // 16 weights: x chunks 2c and 2c + 1
+                        uint4 lo[R], hi[R];
 #pragma unroll
-                    for (int b = 0; b < BT; ++b) {
-                        const uint4 xv = xs[b * K8 + c];
+                        for (int r = 0; r < R; ++r) e4m3x16_to_half(wc[r][u], lo[r], hi[r]);
 #pragma unroll
-                        for (int r = 0; r < R; ++r) acc[r][b] = dot8(wc[r][u], xv, acc[r][b]);
+                        for (int b = 0; b < BT; ++b) {
+                            const uint4 x0 = xs[b * K8 + 2 * c], x1 = xs[b * K8 + 2 * c + 1];
+#pragma unroll
+                            for (int r = 0; r < R; ++r) acc[r][b] = dot8_mixed(hi[r], x1, dot8_mixed(lo[r], x0, acc[r][b]));
+                        }
+                    } else {
+#pragma unroll
+                        for (int b = 0; b < BT; ++b) {
+                            const uint4 xv = xs[b * K8 + c];
+#pragma unroll
+                            for (int r = 0; r < R; ++r) acc[r][b] = dot8_mixed(wc[r][u], xv, acc[r][b]);
+                        }
                     }
                 }
             }
@@ -175,6 +233,14 @@ __global__ void __launch_bounds__(kGemvThreads, 2) gemv_vec_kernel(const GemvPar
         for (int r = 0; r < R; ++r)
 #pragma unroll
             for (int b = 0; b < BT; ++b) acc[r][b] = warp_sum(acc[r][b]);
+        if constexpr (F8) {  // the rows' scales
+            float sc[R];
+            task_scales<R, OM>(p, t, sc);
+#pragma unroll
+            for (int r = 0; r < R; ++r)
+#pragma unroll
+                for (int b = 0; b < BT; ++b) acc[r][b] *= sc[r];
+        }
         task_epilogue<R, BT, OM>(p, t, acc, lane, best, s_push, row0);
     }
 
@@ -202,9 +268,9 @@ static int xsum_cluster() {
     return cs;
 }
 
-template <int R, int BT, int XM, int OM, int U>
+template <int R, int BT, int XM, int OM, int U, bool F8>
 static int launch_vec(const GemvParams& p, cudaStream_t s, bool pdl) {
-    auto kern = gemv_vec_kernel<R, BT, XM, OM, U>;
+    auto kern = gemv_vec_kernel<R, BT, XM, OM, U, F8>;
     const int cs = XM == X_SUM ? xsum_cluster() : 1;
     // X_SUM also keeps its slice of the residual (fp32) after x
     const size_t smem = (size_t)BT * p.K * sizeof(__half) +
@@ -268,19 +334,30 @@ int gemv_batch_tile(int K) {
     return 1;
 }
 
+template <int R, int XM, int OM, int U, bool F8>
+static int dispatch_bt_w(const GemvParams& p, cudaStream_t s, bool pdl) {
+    if (p.B <= 1) return launch_vec<R, 1, XM, OM, U, F8>(p, s, pdl);
+    if (p.B <= 2) return launch_vec<R, 2, XM, OM, U, F8>(p, s, pdl);
+    if (p.B <= 4) return launch_vec<R, 4, XM, OM, U, F8>(p, s, pdl);
+    return launch_vec<R, 8, XM, OM, U, F8>(p, s, pdl);
+}
+
+// FP8 weights: 16-byte chunks of 16 codes (U chunks per lane and batch, as
+// for halves, so the same bytes are in flight with twice the weights).
 template <int R, int XM, int OM, int U>
 static int dispatch_bt(const GemvParams& p, cudaStream_t s, bool pdl) {
-    if (p.B <= 1) return launch_vec<R, 1, XM, OM, U>(p, s, pdl);
-    if (p.B <= 2) return launch_vec<R, 2, XM, OM, U>(p, s, pdl);
-    if (p.B <= 4) return launch_vec<R, 4, XM, OM, U>(p, s, pdl);
-    return launch_vec<R, 8, XM, OM, U>(p, s, pdl);
+    if (p.W8) return dispatch_bt_w<R, XM, OM, U, true>(p, s, pdl);
+    return dispatch_bt_w<R, XM, OM, U, false>(p, s, pdl);
 }
 
 int gemv_launch(const GemvParams& p, XMode xm, OutMode om, cudaStream_t s, bool pdl) {
     if (p.tasks <= 0 || p.B <= 0) return B2_OK;
-    if (p.K <= 0 || (p.K & 7) || !aligned16(p.W) || !aligned16(p.x) || (p.ldx & 7)) return B2_ERR_UNSUPPORTED;
+    if (p.K <= 0 || (p.K & 7) || !aligned16(p.x) || (p.ldx & 7)) return B2_ERR_UNSUPPORTED;
+    if (p.W8 ? ((p.K & 15) || !aligned16(p.W8) || !p.wsc || (om == OUT_SWIGLU && (!aligned16(p.W8b) || !p.wsc2)))
+             : !aligned16(p.W))
+        return B2_ERR_UNSUPPORTED;
     if (p.B > 8 || p.B > gemv_batch_tile(p.K)) return B2_ERR_UNSUPPORTED;
-    if (om == OUT_SWIGLU && !aligned16(p.W2)) return B2_ERR_UNSUPPORTED;
+    if (om == OUT_SWIGLU && !p.W8 && !aligned16(p.W2)) return B2_ERR_UNSUPPORTED;
     if ((xm == X_NORM || xm == X_SUM) && (!p.norm_w || !aligned16(p.norm_w))) return B2_ERR_UNSUPPORTED;
     if ((xm == X_SUM || om == OUT_PUSH) && (!p.tp_on || p.tpx.tp < 1 || p.tpx.tp > kMaxTp)) return B2_ERR_INVALID;
     switch (om) {

@@ -119,6 +119,15 @@ struct GemvParams {
     float* hid_out;              // X_SUM: residual stream after it
     int rows_per_cta;            // OUT_PUSH: contiguous block of rows per CTA (set at launch)
     TraceSlot trace;             // step trace (buf null: off)
+
+    // FP8 weights (a quantised model's decode GEMVs): W8 / W8b are [rows][K]
+    // e4m3 codes with one fp32 scale per row (wsc / wsc2).  When W8 is set
+    // they stand in for W / W2, and each row's dot product is multiplied by
+    // its scale before the epilogue.  K % 16 == 0.
+    const uint8_t* W8;
+    const uint8_t* W8b;
+    const float* wsc;
+    const float* wsc2;
 };
 
 constexpr int kPushRows = 128;   // OUT_PUSH rows per CTA at most
@@ -156,5 +165,8 @@ int gemv_launch(const GemvParams& p, XMode xm, OutMode om, cudaStream_t s, bool 
 
 // Maximum batch tile handled by one gemv_launch for row length K.
 int gemv_batch_tile(int K);
+
+// Per-row FP8 (E4M3) quantisation of a half matrix [rows][K] (quant.cu).
+int quantize_e4m3_rows(const __half* w, int64_t rows, int K, uint8_t* q, float* scales, cudaStream_t s);
 
 }  // namespace b2

@@ -552,9 +552,16 @@ using namespace b2;
 // ---------------------------------------------------------------------------
 // model object
 // ---------------------------------------------------------------------------
+// One quantised copy of a projection: E4M3 codes [rows][K] and a scale per row.
+struct Fp8W {
+    uint8_t* q = nullptr;
+    float* sc = nullptr;
+};
+
 struct LayerW {
     __half *wqkv = nullptr, *bqkv = nullptr, *wo = nullptr, *wg = nullptr, *wu = nullptr, *wd = nullptr;
     __half *ln1 = nullptr, *ln2 = nullptr;
+    Fp8W f8qkv, f8o, f8g, f8u, f8d;  // b2_model_quantize_weights
 };
 
 struct b2_model {
@@ -568,6 +575,8 @@ struct b2_model {
     std::vector<void*> allocs;
     __half* embed = nullptr;
     __half* lm_head = nullptr;  // local vocabulary shard
+    Fp8W f8lm;                  // its quantised copy
+    bool wfp8 = false;          // decode GEMVs read the FP8 copies
     __half* final_norm = nullptr;
     std::vector<LayerW> layers;
 
@@ -1205,6 +1214,10 @@ static int launch_qkv(b2_model* m, int l, int B, bool pdl, bool xch = false) {
     p.rope = m->rope;
     p.pos = m->positions;
     p.kv = layer_kv(m, l);
+    if (m->wfp8) {
+        p.W8 = w.f8qkv.q;
+        p.wsc = w.f8qkv.sc;
+    }
     if (xch && l > 0) {
         set_exchange(m, p, 2 * (l - 1) + 1, m->hidden2, m->hidden);
         p.x = m->hidden2;
@@ -1240,6 +1253,10 @@ static int launch_o(b2_model* m, int l, int B, bool pdl, bool xch = false) {
     GemvParams p = {};
     p.trace = next_trace(m);
     p.W = m->layers[l].wo;
+    if (m->wfp8) {
+        p.W8 = m->layers[l].f8o.q;
+        p.wsc = m->layers[l].f8o.sc;
+    }
     p.K = m->nq * c.head_dim;
     p.tasks = c.hidden_size;
     p.B = B;
@@ -1262,6 +1279,12 @@ static int launch_gateup(b2_model* m, int l, int B, bool pdl, bool xch = false) 
     p.trace = next_trace(m);
     p.W = w.wg;
     p.W2 = w.wu;
+    if (m->wfp8) {
+        p.W8 = w.f8g.q;
+        p.W8b = w.f8u.q;
+        p.wsc = w.f8g.sc;
+        p.wsc2 = w.f8u.sc;
+    }
     p.K = c.hidden_size;
     p.tasks = m->inter;
     p.B = B;
@@ -1283,6 +1306,10 @@ static int launch_down(b2_model* m, int l, int B, bool pdl, bool xch = false) {
     GemvParams p = {};
     p.trace = next_trace(m);
     p.W = m->layers[l].wd;
+    if (m->wfp8) {
+        p.W8 = m->layers[l].f8d.q;
+        p.wsc = m->layers[l].f8d.sc;
+    }
     p.K = m->inter;
     p.tasks = c.hidden_size;
     p.B = B;
@@ -1303,6 +1330,10 @@ static int launch_lm_head(b2_model* m, int B, bool pdl, bool xch = false) {
     GemvParams p = {};
     p.trace = next_trace(m);
     p.W = m->lm_head;
+    if (m->wfp8) {
+        p.W8 = m->f8lm.q;
+        p.wsc = m->f8lm.sc;
+    }
     p.K = c.hidden_size;
     p.tasks = m->vocab_l;
     p.B = B;
@@ -1527,6 +1558,40 @@ extern "C" int b2_model_set_sampling(b2_model* m, const b2_sampler_config* cfg) 
     if (on != m->sampling) {
         m->sampling = on;
         invalidate_graphs(m);  // the step gains or loses its sampling kernel
+    }
+    return B2_OK;
+}
+
+// Quantised copy of one projection (allocated on first use, kept).
+static int quantize_proj(b2_model* m, const __half* w, int64_t rows, int K, Fp8W& f) {
+    if (!f.q) {
+        M_TRY(model_alloc(m, reinterpret_cast<void**>(&f.q), (size_t)rows * K));
+        M_TRY(model_alloc(m, reinterpret_cast<void**>(&f.sc), (size_t)rows * sizeof(float)));
+    }
+    return quantize_e4m3_rows(w, rows, K, f.q, f.sc, m->stream);
+}
+
+extern "C" int b2_model_quantize_weights(b2_model* m, int format) {
+    B2_REQUIRE(m && (format == B2_WEIGHTS_FP16 || format == B2_WEIGHTS_FP8_E4M3));
+    const b2_model_config& c = m->cfg;
+    const int H = c.hidden_size, qd = m->nq * c.head_dim;
+    const bool on = format == B2_WEIGHTS_FP8_E4M3;
+    if (on) {
+        if ((H % 16) || (qd % 16) || (m->inter % 16)) return B2_ERR_UNSUPPORTED;
+        for (int l = 0; l < c.num_layers; ++l) {
+            LayerW& w = m->layers[l];
+            M_TRY(quantize_proj(m, w.wqkv, m->qkv_rows, H, w.f8qkv));
+            M_TRY(quantize_proj(m, w.wo, H, qd, w.f8o));
+            M_TRY(quantize_proj(m, w.wg, m->inter, H, w.f8g));
+            M_TRY(quantize_proj(m, w.wu, m->inter, H, w.f8u));
+            M_TRY(quantize_proj(m, w.wd, H, m->inter, w.f8d));
+        }
+        M_TRY(quantize_proj(m, m->lm_head, m->vocab_l, H, m->f8lm));
+        B2_TRY(cudaStreamSynchronize(m->stream));
+    }
+    if (on != m->wfp8) {
+        m->wfp8 = on;
+        invalidate_graphs(m);  // the step's GEMVs change form
     }
     return B2_OK;
 }
@@ -1900,9 +1965,12 @@ extern "C" double b2_model_step_bytes(const b2_model* m, int B, int ctx) {
     if (!m) return 0.0;
     const b2_model_config& c = m->cfg;
     const double H = c.hidden_size, D = c.head_dim, L = c.num_layers;
+    const double rows = L * ((double)m->qkv_rows + H + 2.0 * m->inter + H) + m->vocab_l;
     const double lin = L * ((double)m->qkv_rows * H + H * m->nq * D + 2.0 * m->inter * H + H * m->inter) +
                        (double)m->vocab_l * H;
-    double bytes = 2.0 * lin;
+    // decode GEMVs on FP8 copies: 1 byte per weight and an fp32 scale per row
+    const bool f8 = m->wfp8 && gemv_step(m, B);
+    double bytes = f8 ? lin + 4.0 * rows : 2.0 * lin;
     if (c.has_qkv_bias) bytes += 2.0 * L * m->qkv_rows;
     bytes += 2.0 * B * H;                               // embedding rows
     bytes += 2.0 * (2.0 * L + 1.0) * H;                 // norm weights
@@ -1949,13 +2017,16 @@ extern "C" double b2_model_kernel_bytes(const b2_model* m, int kind, int B, int 
     if (!m) return 0.0;
     const b2_model_config& c = m->cfg;
     const double H = c.hidden_size, D = c.head_dim;
+    // weight bytes of `rows` rows of width K: fp16, or FP8 codes + fp32 scales
+    const bool f8 = m->wfp8 && gemv_step(m, B);
+    auto wb = [&](double rows, double K) { return f8 ? rows * K + 4.0 * rows : 2.0 * rows * K; };
     switch (kind) {
-        case 0: return 2.0 * m->qkv_rows * H + 4.0 * B * H + 2.0 * H + 2.0 * B * m->qkv_rows;
+        case 0: return wb(m->qkv_rows, H) + 4.0 * B * H + 2.0 * H + 2.0 * B * m->qkv_rows;
         case 1: return 2.0 * B * m->nkv * D * 2.0 * ctx + 2.0 * 2.0 * B * m->nq * D;
-        case 2: return 2.0 * H * m->nq * D + 2.0 * B * m->nq * D + 8.0 * B * H;
-        case 3: return 2.0 * 2.0 * m->inter * H + 4.0 * B * H + 2.0 * H + 2.0 * B * m->inter;
-        case 4: return 2.0 * H * m->inter + 2.0 * B * m->inter + 8.0 * B * H;
-        default: return 2.0 * m->vocab_l * H + 4.0 * B * H + 2.0 * H + 4.0 * B * m->vocab_l;
+        case 2: return wb(H, m->nq * D) + 2.0 * B * m->nq * D + 8.0 * B * H;
+        case 3: return 2.0 * wb(m->inter, H) + 4.0 * B * H + 2.0 * H + 2.0 * B * m->inter;
+        case 4: return wb(H, m->inter) + 2.0 * B * m->inter + 8.0 * B * H;
+        default: return wb(m->vocab_l, H) + 4.0 * B * H + 2.0 * H + 4.0 * B * m->vocab_l;
     }
 }
 
