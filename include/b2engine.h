@@ -379,8 +379,8 @@ int b2_model_set_tensor_bf16(b2_model* m, const char* name, const uint16_t* host
  * host, src/runtime/sampler.cu:253-339, apps/generate.cpp:884-898). */
 int b2_model_set_sampling(b2_model* m, const b2_sampler_config* cfg);
 
-/* Weight format of the decode GEMVs (batches the GEMV step takes: 1-8
- * sequences, or fewer at widths that cap its batch tile).
+/* Weight format of the decode GEMVs at batch 1-2 (larger batches are bound
+ * by the GEMVs' arithmetic, not their bytes, and keep fp16 weights).
  * B2_WEIGHTS_FP8_E4M3 quantises every projection and the lm_head per output
  * row (b2_quantize_fp8_rows) from the fp16 weights the model holds now, on
  * the device, into copies allocated on first use, and the decode GEMVs then

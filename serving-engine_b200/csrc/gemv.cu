@@ -53,8 +53,11 @@ bool pdl_enabled() {
     return on == 1;
 }
 
-constexpr int kGemvThreads = 256;
-constexpr int kGemvWarps = kGemvThreads / 32;
+// Block size: 256 threads, two CTAs per SM, while the staged activations
+// fit twice in shared memory (kGemvSmemPair); else 512 threads and one CTA
+// per SM (batch 8 at K = 14336 stages 224 KB), the same 16 warps per SM.
+constexpr int kGemvSmemPair = 110 * 1024;
+constexpr int kGemvSmemMax = 224 * 1024;
 
 template <int R, int U>
 __device__ __forceinline__ void load_rows(uint4 (&w)[R][U], const uint4* const (&rp)[R], int cbase, int K8,
@@ -130,8 +133,9 @@ __device__ __forceinline__ void e4m3x16_to_half(const uint4& w, uint4& lo, uint4
 // ---------------------------------------------------------------------------
 // register-streaming form
 // ---------------------------------------------------------------------------
-template <int R, int BT, int XM, int OM, int U, bool F8>
-__global__ void __launch_bounds__(kGemvThreads, 2) gemv_vec_kernel(const GemvParams p) {
+template <int R, int BT, int XM, int OM, int U, bool F8, int NT>
+__global__ void __launch_bounds__(NT, NT == 256 ? 2 : 1) gemv_vec_kernel(const GemvParams p) {
+    constexpr int kGemvWarps = NT / 32;
     extern __shared__ __align__(16) uint4 xs[];  // [BT][K8] packed half
     __shared__ float s_rs[BT];
     __shared__ float s_ss[BT][kGemvWarps];
@@ -169,7 +173,7 @@ __global__ void __launch_bounds__(kGemvThreads, 2) gemv_vec_kernel(const GemvPar
     griddep_launch_dependents();
     trace_begin(p.trace);
 
-    stage_x<BT, XM, kGemvThreads>(p, xs, s_rs, s_ss, lane, warp);
+    stage_x<BT, XM, NT>(p, xs, s_rs, s_ss, lane, warp);
 
     unsigned long long best[BT];
 #pragma unroll
@@ -244,7 +248,7 @@ __global__ void __launch_bounds__(kGemvThreads, 2) gemv_vec_kernel(const GemvPar
         task_epilogue<R, BT, OM>(p, t, acc, lane, best, s_push, row0);
     }
 
-    gemv_finish<BT, OM, kGemvThreads>(p, lane, warp, best, s_best, s_push, row0, t_end, push_epoch, push_par);
+    gemv_finish<BT, OM, NT>(p, lane, warp, best, s_best, s_push, row0, t_end, push_epoch, push_par);
     __syncthreads();
     trace_end(p.trace);
     // X_SUM: no CTA leaves while a cluster peer may still read its slice of h
@@ -268,13 +272,20 @@ static int xsum_cluster() {
     return cs;
 }
 
-template <int R, int BT, int XM, int OM, int U, bool F8>
+// Dynamic shared memory of a launch: x staged as halves, and (X_SUM) this
+// CTA's slice of the fp32 residual.
+static size_t gemv_smem(int BT, int XM, int K, int cs) {
+    return (size_t)BT * K * sizeof(__half) +
+           (XM == X_SUM ? (size_t)BT * (((K >> 3) + cs - 1) / cs) * 8 * sizeof(float) : 0);
+}
+
+template <int R, int BT, int XM, int OM, int U, bool F8, int NT>
 static int launch_vec(const GemvParams& p, cudaStream_t s, bool pdl) {
-    auto kern = gemv_vec_kernel<R, BT, XM, OM, U, F8>;
+    constexpr int kGemvThreads = NT, kGemvWarps = NT / 32;
+    auto kern = gemv_vec_kernel<R, BT, XM, OM, U, F8, NT>;
     const int cs = XM == X_SUM ? xsum_cluster() : 1;
-    // X_SUM also keeps its slice of the residual (fp32) after x
-    const size_t smem = (size_t)BT * p.K * sizeof(__half) +
-                        (XM == X_SUM ? (size_t)BT * (((p.K >> 3) + cs - 1) / cs) * 8 * sizeof(float) : 0);
+    const size_t smem = gemv_smem(BT, XM, p.K, cs);
+    if (smem > (size_t)kGemvSmemMax) return B2_ERR_UNSUPPORTED;
     // per-device occupancy cache, keyed on the shared-memory footprint
     static thread_local int last_dev = -1;
     static thread_local size_t last_smem = (size_t)-1;
@@ -327,19 +338,25 @@ static int launch_vec(const GemvParams& p, cudaStream_t s, bool pdl) {
 }
 
 int gemv_batch_tile(int K) {
-    // keep two CTAs of x staging per SM within ~200 KB of shared memory
-    const long budget = 100 * 1024;
+    // x staging of one CTA (one per SM past kGemvSmemPair) within kGemvSmemMax
     for (int bt = 8; bt > 1; bt >>= 1)
-        if ((long)bt * K * 2 <= budget) return bt;
+        if ((long)bt * K * 2 <= kGemvSmemMax) return bt;
     return 1;
+}
+
+template <int R, int BT, int XM, int OM, int U, bool F8>
+static int launch_nt(const GemvParams& p, cudaStream_t s, bool pdl) {
+    const int cs = XM == X_SUM ? xsum_cluster() : 1;
+    if (gemv_smem(BT, XM, p.K, cs) <= (size_t)kGemvSmemPair) return launch_vec<R, BT, XM, OM, U, F8, 256>(p, s, pdl);
+    return launch_vec<R, BT, XM, OM, U, F8, 512>(p, s, pdl);
 }
 
 template <int R, int XM, int OM, int U, bool F8>
 static int dispatch_bt_w(const GemvParams& p, cudaStream_t s, bool pdl) {
-    if (p.B <= 1) return launch_vec<R, 1, XM, OM, U, F8>(p, s, pdl);
-    if (p.B <= 2) return launch_vec<R, 2, XM, OM, U, F8>(p, s, pdl);
-    if (p.B <= 4) return launch_vec<R, 4, XM, OM, U, F8>(p, s, pdl);
-    return launch_vec<R, 8, XM, OM, U, F8>(p, s, pdl);
+    if (p.B <= 1) return launch_nt<R, 1, XM, OM, U, F8>(p, s, pdl);
+    if (p.B <= 2) return launch_nt<R, 2, XM, OM, U, F8>(p, s, pdl);
+    if (p.B <= 4) return launch_nt<R, 4, XM, OM, U, F8>(p, s, pdl);
+    return launch_nt<R, 8, XM, OM, U, F8>(p, s, pdl);
 }
 
 // FP8 weights: 16-byte chunks of 16 codes (U chunks per lane and batch, as

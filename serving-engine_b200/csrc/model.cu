@@ -45,9 +45,17 @@ namespace cg = cooperative_groups;
 namespace b2 {
 
 // Batches up to kGemvMaxBatch decode with the fused GEMVs; larger batches
-// run the projections on the tensor cores (split-K GEMM, weights streamed
-// once per step for the whole batch).
-constexpr int kGemvMaxBatch = 8;
+// run the projections on the tensor cores (skinny weight stream, weights
+// read once per step for the whole batch).  Past 4 sequences a GEMV is
+// bound by its multiply-adds and shared-memory reads rather than HBM
+// (Llama-3-8B shape, batch 8: 1200 tok/s against 1993 on the tensor cores;
+// batch 4: 1039 against 998).
+constexpr int kGemvMaxBatch = 4;
+// FP8 weights (b2_model_quantize_weights) are read by the GEMV step up to
+// this batch; above it the E4M3 decode adds to a compute-bound kernel
+// (batch 4: 927 tok/s against 1039 with fp16 weights) and the fp16 copies
+// are streamed instead.
+constexpr int kFp8MaxBatch = 2;
 constexpr int kMaxBatch = 256;
 
 struct AttnParams;
@@ -1214,7 +1222,7 @@ static int launch_qkv(b2_model* m, int l, int B, bool pdl, bool xch = false) {
     p.rope = m->rope;
     p.pos = m->positions;
     p.kv = layer_kv(m, l);
-    if (m->wfp8) {
+    if (m->wfp8 && B <= kFp8MaxBatch) {
         p.W8 = w.f8qkv.q;
         p.wsc = w.f8qkv.sc;
     }
@@ -1253,7 +1261,7 @@ static int launch_o(b2_model* m, int l, int B, bool pdl, bool xch = false) {
     GemvParams p = {};
     p.trace = next_trace(m);
     p.W = m->layers[l].wo;
-    if (m->wfp8) {
+    if (m->wfp8 && B <= kFp8MaxBatch) {
         p.W8 = m->layers[l].f8o.q;
         p.wsc = m->layers[l].f8o.sc;
     }
@@ -1279,7 +1287,7 @@ static int launch_gateup(b2_model* m, int l, int B, bool pdl, bool xch = false) 
     p.trace = next_trace(m);
     p.W = w.wg;
     p.W2 = w.wu;
-    if (m->wfp8) {
+    if (m->wfp8 && B <= kFp8MaxBatch) {
         p.W8 = w.f8g.q;
         p.W8b = w.f8u.q;
         p.wsc = w.f8g.sc;
@@ -1306,7 +1314,7 @@ static int launch_down(b2_model* m, int l, int B, bool pdl, bool xch = false) {
     GemvParams p = {};
     p.trace = next_trace(m);
     p.W = m->layers[l].wd;
-    if (m->wfp8) {
+    if (m->wfp8 && B <= kFp8MaxBatch) {
         p.W8 = m->layers[l].f8d.q;
         p.wsc = m->layers[l].f8d.sc;
     }
@@ -1330,7 +1338,7 @@ static int launch_lm_head(b2_model* m, int B, bool pdl, bool xch = false) {
     GemvParams p = {};
     p.trace = next_trace(m);
     p.W = m->lm_head;
-    if (m->wfp8) {
+    if (m->wfp8 && B <= kFp8MaxBatch) {
         p.W8 = m->f8lm.q;
         p.wsc = m->f8lm.sc;
     }
@@ -1969,7 +1977,7 @@ extern "C" double b2_model_step_bytes(const b2_model* m, int B, int ctx) {
     const double lin = L * ((double)m->qkv_rows * H + H * m->nq * D + 2.0 * m->inter * H + H * m->inter) +
                        (double)m->vocab_l * H;
     // decode GEMVs on FP8 copies: 1 byte per weight and an fp32 scale per row
-    const bool f8 = m->wfp8 && gemv_step(m, B);
+    const bool f8 = m->wfp8 && gemv_step(m, B) && B <= kFp8MaxBatch;
     double bytes = f8 ? lin + 4.0 * rows : 2.0 * lin;
     if (c.has_qkv_bias) bytes += 2.0 * L * m->qkv_rows;
     bytes += 2.0 * B * H;                               // embedding rows
@@ -2018,7 +2026,7 @@ extern "C" double b2_model_kernel_bytes(const b2_model* m, int kind, int B, int 
     const b2_model_config& c = m->cfg;
     const double H = c.hidden_size, D = c.head_dim;
     // weight bytes of `rows` rows of width K: fp16, or FP8 codes + fp32 scales
-    const bool f8 = m->wfp8 && gemv_step(m, B);
+    const bool f8 = m->wfp8 && gemv_step(m, B) && B <= kFp8MaxBatch;
     auto wb = [&](double rows, double K) { return f8 ? rows * K + 4.0 * rows : 2.0 * rows * K; };
     switch (kind) {
         case 0: return wb(m->qkv_rows, H) + 4.0 * B * H + 2.0 * H + 2.0 * B * m->qkv_rows;
