@@ -379,14 +379,14 @@ int b2_model_set_tensor_bf16(b2_model* m, const char* name, const uint16_t* host
  * host, src/runtime/sampler.cu:253-339, apps/generate.cpp:884-898). */
 int b2_model_set_sampling(b2_model* m, const b2_sampler_config* cfg);
 
-/* Weight format of the decode GEMVs at batch 1-2 (larger batches are bound
- * by the GEMVs' arithmetic, not their bytes, and keep fp16 weights).
- * B2_WEIGHTS_FP8_E4M3 quantises every projection and the lm_head per output
- * row (b2_quantize_fp8_rows) from the fp16 weights the model holds now, on
- * the device, into copies allocated on first use, and the decode GEMVs then
- * stream 1-byte weights -- half the bytes of a decode step.  Prefill and the
- * batched tensor-core step keep the fp16 weights.  Call again after changing
- * weights; B2_WEIGHTS_FP16 returns to the fp16 GEMVs (the copies are kept).
+/* Weight format of the decode steps.  B2_WEIGHTS_FP8_E4M3 quantises every
+ * projection and the lm_head per output row (b2_quantize_fp8_rows) from the
+ * fp16 weights the model holds now, on the device, into copies allocated on
+ * first use; decode steps of 1-2 sequences (the GEMVs) and of more than 4
+ * (the tensor-core step, up to 128) then stream the 1-byte copies -- half
+ * the bytes of a step.  Batches of 3-4 (GEMVs bound by arithmetic, not
+ * bytes) and prefill keep the fp16 weights.  Call again after changing
+ * weights; B2_WEIGHTS_FP16 returns to fp16 everywhere (the copies are kept).
  * Synchronises.  New API (the reference plans quantised weights as P8,
  * RESULTS.md:39). */
 enum { B2_WEIGHTS_FP16 = 0, B2_WEIGHTS_FP8_E4M3 = 1 };

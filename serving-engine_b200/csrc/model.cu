@@ -54,7 +54,8 @@ constexpr int kGemvMaxBatch = 4;
 // FP8 weights (b2_model_quantize_weights) are read by the GEMV step up to
 // this batch; above it the E4M3 decode adds to a compute-bound kernel
 // (batch 4: 927 tok/s against 1039 with fp16 weights) and the fp16 copies
-// are streamed instead.
+// are streamed instead.  The batched tensor-core step (batch > 4) reads the
+// FP8 copies up to 128 sequences (skinny.cu: weight tiles decoded into TMEM).
 constexpr int kFp8MaxBatch = 2;
 constexpr int kMaxBatch = 256;
 
@@ -884,9 +885,9 @@ static int model_create(const b2_model_config* cfg, int tp_rank, int tp_size, co
             return B2_ERR_UNSUPPORTED;
         }
         const int qd = m->nq * D, I = m->inter;
-        auto need = [&](int N, int K) {
-            const SkinnyPlan p = skinny_plan(N, K);
-            return (size_t)p.max_slabs * B * N;
+        auto need = [&](int N, int K) {  // half (64-deep k blocks) or FP8 (128-deep) weights
+            const SkinnyPlan p = skinny_plan(N, K, 64), q = skinny_plan(N, K, 128);
+            return (size_t)std::max(p.max_slabs, q.max_slabs) * B * N;
         };
         size_t f = need(m->qkv_rows, H);
         f = std::max(f, need(H, qd));
@@ -1370,10 +1371,16 @@ static int launch_lm_head(b2_model* m, int B, bool pdl, bool xch = false) {
 // add.  Attention, step begin / end are those of the GEMV step.
 // Skinny projection X W^T of B rows into `ws`, and the slab descriptor its
 // consumer kernel reads.
+// f0 / f1: the FP8 copies of W0 / W1 (b2_model_quantize_weights), streamed
+// instead of the half weights when set.
 static int sk_proj(b2_model* m, const __half* X, int B, const __half* W0, int N0, const __half* W1, int N1, int K,
-                   float* ws, SkSlabs* out) {
+                   float* ws, SkSlabs* out, const Fp8W* f0 = nullptr, const Fp8W* f1 = nullptr) {
     SkinnyPlan pl;
-    M_TRY(gemm_skinny(X, B, W0, N0, W1, N1, K, ws, m->bws_floats, &pl, m->stream, next_trace(m)));
+    if (m->wfp8 && f0 && f0->q && B <= 128)
+        M_TRY(gemm_skinny_f8(X, B, f0->q, f0->sc, N0, f1 ? f1->q : nullptr, f1 ? f1->sc : nullptr, N1, K, ws,
+                             m->bws_floats, &pl, m->stream, next_trace(m)));
+    else
+        M_TRY(gemm_skinny(X, B, W0, N0, W1, N1, K, ws, m->bws_floats, &pl, m->stream, next_trace(m)));
     out->ws = ws;
     out->N = N0 + N1;
     out->nk = pl.nk;
@@ -1387,7 +1394,7 @@ static int sk_proj(b2_model* m, const __half* X, int B, const __half* W0, int N0
 static int lm_head_rows(b2_model* m, int B) {
     const b2_model_config& c = m->cfg;
     SkSlabs lg;
-    M_TRY(sk_proj(m, m->bxn, B, m->lm_head, m->vocab_l, nullptr, 0, c.hidden_size, m->bws_a, &lg));
+    M_TRY(sk_proj(m, m->bxn, B, m->lm_head, m->vocab_l, nullptr, 0, c.hidden_size, m->bws_a, &lg, &m->f8lm));
     const int limit = c.vocab_size > 151665 ? 151665 : c.vocab_size;
     const unsigned chunks = (unsigned)((m->vocab_l + 4095) / 4096);
     B2_TRY(launch(sk_logits_argmax_kernel, dim3(chunks, (unsigned)B), dim3(256), 0, m->stream, true, lg, B,
@@ -1437,7 +1444,7 @@ static int enqueue_step_batched(b2_model* m, int B) {
         LayerW& w = m->layers[l];
         __half* kbase = m->kv + (int64_t)l * m->kv_s_layer;
         SkSlabs qkv, o, g, u, d;
-        M_TRY(sk_proj(m, m->bxn, B, w.wqkv, R, nullptr, 0, H, m->bws_a, &qkv));
+        M_TRY(sk_proj(m, m->bxn, B, w.wqkv, R, nullptr, 0, H, m->bws_a, &qkv, &w.f8qkv));
         const unsigned qkv_threads = (unsigned)((m->nq + 2 * m->nkv) * (D / 8));
         B2_TRY(launch(sk_qkv_rope_kernel, dim3((unsigned)B, (qkv_threads + 255) / 256), dim3(256), 0, s, true,
                       qkv, B, (const __half*)w.bqkv, m->bqkv, (int64_t)R, (const float2*)m->rope, m->nq, m->nkv, D,
@@ -1456,15 +1463,15 @@ static int enqueue_step_batched(b2_model* m, int B) {
                 M_TRY(rc);
         }
         const __half* next_ln = l + 1 < c.num_layers ? m->layers[l + 1].ln1 : m->final_norm;
-        M_TRY(sk_proj(m, m->attn, B, w.wo, H, nullptr, 0, qd, m->bws_a, &o));
+        M_TRY(sk_proj(m, m->attn, B, w.wo, H, nullptr, 0, qd, m->bws_a, &o, &w.f8o));
         M_TRY(add_and_norm(m, o, B, w.ln2));
         if (fuse_gu) {
-            M_TRY(sk_proj(m, m->bxn, B, w.wg, I, w.wu, I, H, m->bws_a, &g));
+            M_TRY(sk_proj(m, m->bxn, B, w.wg, I, w.wu, I, H, m->bws_a, &g, &w.f8g, &w.f8u));
             u = g;
             u.col0 = I;
         } else {
-            M_TRY(sk_proj(m, m->bxn, B, w.wg, I, nullptr, 0, H, m->bws_a, &g));
-            M_TRY(sk_proj(m, m->bxn, B, w.wu, I, nullptr, 0, H, m->bws_b, &u));
+            M_TRY(sk_proj(m, m->bxn, B, w.wg, I, nullptr, 0, H, m->bws_a, &g, &w.f8g));
+            M_TRY(sk_proj(m, m->bxn, B, w.wu, I, nullptr, 0, H, m->bws_b, &u, &w.f8u));
         }
         {
             int64_t blocks = ((int64_t)B * I / 4 + 255) / 256;
@@ -1472,7 +1479,7 @@ static int enqueue_step_batched(b2_model* m, int B) {
             B2_TRY(launch(sk_swiglu_kernel, dim3((unsigned)blocks), dim3(256), 0, s, true, g, u, B, I, m->act,
                           next_trace(m)));
         }
-        M_TRY(sk_proj(m, m->act, B, w.wd, H, nullptr, 0, I, m->bws_a, &d));
+        M_TRY(sk_proj(m, m->act, B, w.wd, H, nullptr, 0, I, m->bws_a, &d, &w.f8d));
         M_TRY(add_and_norm(m, d, B, next_ln));
     }
     M_TRY(lm_head_rows(m, B));
@@ -1977,7 +1984,7 @@ extern "C" double b2_model_step_bytes(const b2_model* m, int B, int ctx) {
     const double lin = L * ((double)m->qkv_rows * H + H * m->nq * D + 2.0 * m->inter * H + H * m->inter) +
                        (double)m->vocab_l * H;
     // decode GEMVs on FP8 copies: 1 byte per weight and an fp32 scale per row
-    const bool f8 = m->wfp8 && gemv_step(m, B) && B <= kFp8MaxBatch;
+    const bool f8 = m->wfp8 && (gemv_step(m, B) ? B <= kFp8MaxBatch : B <= 128);
     double bytes = f8 ? lin + 4.0 * rows : 2.0 * lin;
     if (c.has_qkv_bias) bytes += 2.0 * L * m->qkv_rows;
     bytes += 2.0 * B * H;                               // embedding rows
@@ -2026,7 +2033,7 @@ extern "C" double b2_model_kernel_bytes(const b2_model* m, int kind, int B, int 
     const b2_model_config& c = m->cfg;
     const double H = c.hidden_size, D = c.head_dim;
     // weight bytes of `rows` rows of width K: fp16, or FP8 codes + fp32 scales
-    const bool f8 = m->wfp8 && gemv_step(m, B) && B <= kFp8MaxBatch;
+    const bool f8 = m->wfp8 && (gemv_step(m, B) ? B <= kFp8MaxBatch : B <= 128);
     auto wb = [&](double rows, double K) { return f8 ? rows * K + 4.0 * rows : 2.0 * rows * K; };
     switch (kind) {
         case 0: return wb(m->qkv_rows, H) + 4.0 * B * H + 2.0 * H + 2.0 * B * m->qkv_rows;

@@ -23,7 +23,8 @@ __host__ __device__ __forceinline__ int sk_nseg(int n, int nk, int per) {
     return (t * nk + nk - 1) / per - (t * nk) / per + 1;
 }
 
-SkinnyPlan skinny_plan(int N, int K);
+// kdepth: elements of K per k block (64 for half weights, 128 for FP8).
+SkinnyPlan skinny_plan(int N, int K, int kdepth = 64);
 
 // ws[slab][b][n] partials of Y[b][n] = sum_k X[b][k] W[n][k] for b < B,
 // W = W0 (rows 0..N0-1) followed by W1 (N1 rows; may be null with N1 = 0,
@@ -33,5 +34,13 @@ SkinnyPlan skinny_plan(int N, int K);
 // tr: the step trace's slot for this launch (buf null: off).
 int gemm_skinny(const __half* X, int B, const __half* W0, int N0, const __half* W1, int N1, int K, float* ws,
                 size_t ws_floats, SkinnyPlan* plan, cudaStream_t s, TraceSlot tr = TraceSlot{nullptr, 0});
+
+// As gemm_skinny with FP8 (E4M3) weights: codes W0q [N0][K], W1q [N1][K]
+// (bytes), one fp32 scale per row (sc0, sc1); ws receives the scaled
+// partials, so the consumers are those of the half form.  128-deep k blocks
+// (plan.nk = ceil(K / 128)); B <= 128, K % 16 == 0.
+int gemm_skinny_f8(const __half* X, int B, const uint8_t* W0q, const float* sc0, int N0, const uint8_t* W1q,
+                   const float* sc1, int N1, int K, float* ws, size_t ws_floats, SkinnyPlan* plan, cudaStream_t s,
+                   TraceSlot tr = TraceSlot{nullptr, 0});
 
 }  // namespace b2

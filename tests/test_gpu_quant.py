@@ -1,4 +1,4 @@
-"""FP8 (E4M3) weights for the decode GEMVs.
+"""FP8 (E4M3) weights for the decode steps.
 
 Format: per output row, scale = max|w| / 448 and q = E4M3(w / scale) with
 round-to-nearest-even and saturation (the oracle restates the OCP E4M3
@@ -11,8 +11,11 @@ Checked here:
   * a quantised model's decode (b2_model_quantize_weights) teacher-forced
     against the oracle run on the dequantised weights -- logits within
     max-abs 2e-2 and cosine 0.9999, greedy ids under the near-tie rule -- on
-    a small model and at Llama-3-8B width (2 layers); switching back to fp16
-    restores the fp16 logits bit for bit.
+    a small model and at Llama-3-8B projection widths (2 layers); switching
+    back to fp16 restores the fp16 logits bit for bit;
+  * the batched tensor-core step on the FP8 copies (E4M3 tiles by TMA,
+    decoded into TMEM, A operand from TMEM) at batch 8 and 12 and at
+    Llama-3-8B projection widths, against the same oracle.
 """
 import numpy as np
 import pytest
@@ -124,3 +127,37 @@ def test_fp8_model_decode_llama8b_width(cuda):
     cfg = O.Config(vocab=4096, hidden=4096, inter=14336, layers=2, nq=32, nkv=8, head_dim=128, theta=5e5)
     m, _ = _fp8_decode_check(cfg, 902, 8, 24)
     m.close()
+
+
+def _fp8_batched_check(cfg, seed, B, prompt_len, n_dec):
+    """B sequences decoded together on the quantised model's batched step,
+    every position teacher-forced against the oracle on the dequantised
+    weights."""
+    m = b2.Model(cfg.vocab, cfg.hidden, cfg.inter, cfg.layers, cfg.nq, cfg.nkv, cfg.head_dim, eps=cfg.eps,
+                 theta=cfg.theta, max_batch=B, max_seq=256)
+    m.init_random(seed, 0.02)
+    m.quantize_weights("fp8")
+    m.reset()
+    rng = np.random.default_rng(seed)
+    seqs = rng.integers(0, cfg.vocab, (B, prompt_len + n_dec))
+    logits = []
+    for pos in range(prompt_len + n_dec):
+        lg, _ = m.decode_step(seqs[:, pos], [pos] * B, want_logits=True, want_next=True)
+        logits.append(lg.copy())
+    W8 = O.fp8_weights(O.seeded_weights(cfg, seed))
+    for b in range(B):
+        ref = O.forward(cfg, W8, seqs[b])
+        for pos in range(prompt_len + n_dec):
+            check_logits(logits[pos][b], ref[pos], f"sequence {b} position {pos}")
+    m.close()
+
+
+@pytest.mark.parametrize("B", [8, 12])
+def test_fp8_batched_tensor_core_step(cuda, B):
+    cfg = O.Config(vocab=1000, hidden=512, inter=1024, layers=2, nq=4, nkv=2, head_dim=128, theta=5e5)
+    _fp8_batched_check(cfg, 903 + B, B, 6, 4)
+
+
+def test_fp8_batched_llama8b_width(cuda):
+    cfg = O.Config(vocab=4096, hidden=4096, inter=14336, layers=2, nq=32, nkv=8, head_dim=128, theta=5e5)
+    _fp8_batched_check(cfg, 911, 8, 3, 3)
