@@ -473,7 +473,7 @@ def run_b2(args, rank, world, local):
     ck = clocks.stop()
 
     trace = None
-    if args.trace:
+    if not args.no_trace:
         # per-launch device timestamps of a few live steps (b2_model_trace_step)
         L = c["layers"]
         layouts = [  # launch sequences of the step forms, in launch order
@@ -698,7 +698,9 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-tp-parity", action="store_true",
                     help="skip the sharded-vs-unsharded check run before the timed region at N > 1")
-    ap.add_argument("--trace", action="store_true", help="add a per-kernel device trace of a few steps")
+    ap.add_argument("--trace", action="store_true",
+                    help="(the default) add a per-kernel device trace of five steps, taken after the timed region")
+    ap.add_argument("--no-trace", action="store_true", help="leave the per-kernel trace out")
     ap.add_argument("--op", default=None, choices=["attention", "flash_prefill", "gemm"],
                     help="kernel microbenchmark instead of the decode metric (1 GPU)")
     ap.add_argument("--seq", type=int, default=0,
