@@ -133,8 +133,17 @@ __device__ __forceinline__ void e4m3x16_to_half(const uint4& w, uint4& lo, uint4
 // ---------------------------------------------------------------------------
 // register-streaming form
 // ---------------------------------------------------------------------------
+// CTAs per SM the register budget is sized for.  Three 256-thread CTAs (80
+// registers) for the batch-1 q|k|v and lm_head GEMVs: their tasks then go out
+// in one round instead of two (Llama-3-8B q|k|v: 12.2 -> 9.8 us); the o and
+// down GEMVs lose more to the tighter register budget than they gain (down
+// 19.7 -> 23.0 us), and the exchange consumers would spill.
+constexpr int gemv_min_ctas(int NT, int BT, int XM, int OM) {
+    return NT != 256 ? 1 : (BT == 1 && XM != X_SUM && (OM == OUT_QKV || OM == OUT_LOGITS)) ? 3 : 2;
+}
+
 template <int R, int BT, int XM, int OM, int U, bool F8, int NT>
-__global__ void __launch_bounds__(NT, NT == 256 ? 2 : 1) gemv_vec_kernel(const GemvParams p) {
+__global__ void __launch_bounds__(NT, gemv_min_ctas(NT, BT, XM, OM)) gemv_vec_kernel(const GemvParams p) {
     constexpr int kGemvWarps = NT / 32;
     extern __shared__ __align__(16) uint4 xs[];  // [BT][K8] packed half
     __shared__ float s_rs[BT];
