@@ -304,8 +304,14 @@ __global__ void __launch_bounds__(kClThreads) attn_cl_kernel(const __grid_consta
     __syncthreads();
     for (int idx = split * kClThreads + threadIdx.x; idx < nh * D; idx += cs * kClThreads) {
         const int g = idx / D, d = idx - (idx / D) * D;
+        // all ranks' partials requested at once, then summed in rank order
+        float part[kClMaxCluster];
+#pragma unroll
+        for (int r = 0; r < kClMaxCluster; ++r) part[r] = r < cs ? *cl.map_shared_rank(&s_pa[g][d], r) : 0.f;
         float A = 0.f;
-        for (int r = 0; r < cs; ++r) A = fmaf(*cl.map_shared_rank(&s_pa[g][d], r), s_wt[g][r], A);
+#pragma unroll
+        for (int r = 0; r < kClMaxCluster; ++r)
+            if (r < cs) A = fmaf(part[r], s_wt[g][r], A);
         p.out[(int64_t)b * p.o_sb + (int64_t)(h0 + g) * D + d] = __float2half_rn(A);
     }
     cl.sync();  // no CTA leaves while a peer still reads its partial

@@ -458,8 +458,15 @@ __global__ void __launch_bounds__(192, 1) attn_tc_kernel(const __grid_constant__
     __syncthreads();
     for (int idx = split * (int)blockDim.x + threadIdx.x; idx < nh * kAtD; idx += cs * (int)blockDim.x) {
         const int h = idx / kAtD, d = idx - (idx / kAtD) * kAtD;
+        // all ranks' partials requested at once (one distributed-shared-memory
+        // round trip), then summed in rank order
+        float part[kAtMaxCluster];
+#pragma unroll
+        for (int r = 0; r < kAtMaxCluster; ++r) part[r] = r < cs ? *cl.map_shared_rank(&s_pa[h][d], r) : 0.f;
         float A = 0.f;
-        for (int r = 0; r < cs; ++r) A = fmaf(*cl.map_shared_rank(&s_pa[h][d], r), s_wt[h][r], A);
+#pragma unroll
+        for (int r = 0; r < kAtMaxCluster; ++r)
+            if (r < cs) A = fmaf(part[r], s_wt[h][r], A);
         p.out[(int64_t)b * p.o_sb + (int64_t)(h0 + h) * kAtD + d] = __float2half_rn(A);
     }
     cl.sync();
