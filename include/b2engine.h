@@ -515,6 +515,82 @@ int b2_model_step_launches(const b2_model* m, int batch);
  * (src/model/forward_gpu.cu:542-551). */
 int b2_model_trace_step(b2_model* m, int batch, unsigned long long* host_ns, int max_slots, int* n_slots);
 
+/* ------------------------------------------------------------------------
+ * Tokenizer (host only; no CUDA call).  Byte-level BPE read from a HF
+ * tokenizer.json: the reference's Qwen2 vocabulary and, beyond it, Llama-3
+ * and GPT-2 ones.  Replaces engine::BPETokenizer (src/tokenizer/bpe.h:17-58);
+ * that class is kept over these calls in serving-engine_b200/compat
+ * (src/tokenizer/bpe.h).  A tokenizer is immutable after loading: calls on
+ * one object from several threads at once are safe.  Output buffers follow
+ * one rule: *n (ids or bytes) always receives the full length, and when it is
+ * above `cap` nothing is written and B2_ERR_WORKSPACE is returned. */
+typedef struct b2_tokenizer b2_tokenizer;
+
+/* b2_tokenizer_encode flags */
+enum {
+    B2_TOK_SPLIT_SPECIAL = 1, /* special added tokens in the text become their ids
+                                 (the reference's allowed_special); without it they
+                                 are encoded as plain text */
+    B2_TOK_ADD_SPECIAL = 2    /* apply the file's TemplateProcessing post-processor
+                                 (Llama-3: <|begin_of_text|> first) */
+};
+
+/* b2_tokenizer_info.pre_tokenizer */
+enum { B2_PRE_QWEN2 = 1, B2_PRE_LLAMA3 = 2, B2_PRE_GPT2 = 3 };
+/* b2_tokenizer_info.chat_format */
+enum { B2_CHAT_NONE = 0, B2_CHAT_CHATML = 1, B2_CHAT_LLAMA3 = 2 };
+
+typedef struct b2_tokenizer_info {
+    int64_t vocab_size;    /* distinct token strings, vocab and added (BPETokenizer::vocab_size) */
+    int64_t n_ids;         /* highest id + 1 */
+    int64_t n_merges;
+    int32_t pre_tokenizer; /* B2_PRE_* */
+    int32_t nfc;           /* 1: text is NFC-normalised before splitting */
+    int32_t ignore_merges; /* 1: a piece that is a vocab entry is one token */
+    int32_t chat_format;   /* B2_CHAT_* */
+    int32_t bos_id;        /* -1 if none */
+    int32_t eos_id;        /* end of a chat turn (<|im_end|>, <|eot_id|>); -1 if none */
+    int32_t n_stop;        /* ids that end generation, in stop_ids[0..n_stop) */
+    int32_t stop_ids[4];
+    int32_t n_added;
+} b2_tokenizer_info;
+
+/* BPETokenizer::load (src/tokenizer/bpe.cpp:87-158).  Reads and checks the
+ * whole file; B2_ERR_UNSUPPORTED (with the reason in b2_last_error()) for a
+ * normaliser, pre-tokenizer or model this tokenizer does not implement. */
+int b2_tokenizer_load(const char* tokenizer_json_path, b2_tokenizer** out);
+/* The same from the file's contents in memory. */
+int b2_tokenizer_load_json(const char* json, size_t len, b2_tokenizer** out);
+void b2_tokenizer_destroy(b2_tokenizer* t);
+
+/* BPETokenizer::encode (src/tokenizer/bpe.cpp:386-447): UTF-8 text (bytes
+ * that are not valid UTF-8 are kept as byte tokens) -> ids. */
+int b2_tokenizer_encode(const b2_tokenizer* t, const char* text, size_t len, int flags, int32_t* ids, size_t cap,
+                        size_t* n_ids);
+
+/* BPETokenizer::decode (src/tokenizer/bpe.cpp:449-483): ids -> the bytes they
+ * stand for (ids outside the vocabulary are skipped; special tokens too when
+ * skip_special != 0).  The bytes of a partial sequence may end inside a
+ * UTF-8 character. */
+int b2_tokenizer_decode(const b2_tokenizer* t, const int32_t* ids, size_t n, int skip_special, char* out, size_t cap,
+                        size_t* out_len);
+
+/* BPETokenizer::apply_chat_template (src/tokenizer/bpe.cpp:485-506): the
+ * ChatML prompt for Qwen vocabularies (the reference's format, with its
+ * default system message when the first message is not a system one), the
+ * Llama-3 header/eot format for Llama-3 vocabularies.  B2_ERR_UNSUPPORTED for
+ * a vocabulary with neither set of control tokens. */
+int b2_tokenizer_apply_chat_template(const b2_tokenizer* t, const char* const* roles, const char* const* contents,
+                                     size_t n_messages, int add_generation_prompt, char* out, size_t cap,
+                                     size_t* out_len);
+
+/* Id of an added token (by its content) or of a vocab entry (as written in
+ * tokenizer.json); B2_ERR_INVALID and *id = -1 if there is none.  Serves
+ * BPETokenizer::im_start_id / im_end_id / endoftext_id (bpe.h:33-35). */
+int b2_tokenizer_token_to_id(const b2_tokenizer* t, const char* token, size_t len, int32_t* id);
+
+int b2_tokenizer_get_info(const b2_tokenizer* t, b2_tokenizer_info* info);
+
 #ifdef __cplusplus
 }
 #endif

@@ -31,6 +31,12 @@ class KVView(C.Structure):
     _fields_ = [("data", vp), ("stride_b", i64), ("stride_h", i64), ("stride_s", i64), ("stride_d", i64)]
 
 
+class TokenizerInfo(C.Structure):
+    _fields_ = [("vocab_size", i64), ("n_ids", i64), ("n_merges", i64), ("pre_tokenizer", i32), ("nfc", i32),
+                ("ignore_merges", i32), ("chat_format", i32), ("bos_id", i32), ("eos_id", i32), ("n_stop", i32),
+                ("stop_ids", i32 * 4), ("n_added", i32)]
+
+
 class SamplerConfig(C.Structure):
     _fields_ = [("temperature", f32), ("top_k", i32), ("top_p", f32), ("repetition_penalty", f32), ("seed", u64)]
 
@@ -111,6 +117,19 @@ _SIGS = {
     "b2_model_time_kernel": (i32, [vp, i32, i32, i32, C.POINTER(f32)]),
     "b2_model_kernel_bytes": (C.c_double, [vp, i32, i32, i32]),
 }
+
+
+_SIGS.update({
+    "b2_tokenizer_load": (i32, [C.c_char_p, C.POINTER(vp)]),
+    "b2_tokenizer_load_json": (i32, [C.c_char_p, C.c_size_t, C.POINTER(vp)]),
+    "b2_tokenizer_destroy": (None, [vp]),
+    "b2_tokenizer_encode": (i32, [vp, C.c_char_p, C.c_size_t, i32, vp, C.c_size_t, C.POINTER(C.c_size_t)]),
+    "b2_tokenizer_decode": (i32, [vp, vp, C.c_size_t, i32, vp, C.c_size_t, C.POINTER(C.c_size_t)]),
+    "b2_tokenizer_apply_chat_template": (i32, [vp, vp, vp, C.c_size_t, i32, vp, C.c_size_t,
+                                               C.POINTER(C.c_size_t)]),
+    "b2_tokenizer_token_to_id": (i32, [vp, C.c_char_p, C.c_size_t, C.POINTER(i32)]),
+    "b2_tokenizer_get_info": (i32, [vp, C.POINTER(TokenizerInfo)]),
+})
 
 
 def exported_symbols():
@@ -234,6 +253,88 @@ class Sampler:
     def close(self):
         if self.h:
             lib().b2_sampler_destroy(self.h)
+            self.h = None
+
+    __del__ = close
+
+
+class Tokenizer:
+    """engine::BPETokenizer through the C-ABI (b2_tokenizer_*): a byte-level
+    BPE tokenizer read from a HF tokenizer.json (Qwen2, Llama-3 or GPT-2
+    vocabularies)."""
+
+    SPLIT_SPECIAL = 1
+    ADD_SPECIAL = 2
+
+    def __init__(self, path: str | None = None, json_text: str | bytes | None = None):
+        h = vp()
+        if path is not None:
+            call("b2_tokenizer_load", os.fsencode(path), C.byref(h))
+        else:
+            data = json_text.encode() if isinstance(json_text, str) else json_text
+            call("b2_tokenizer_load_json", data, len(data), C.byref(h))
+        self.h = h
+        info = TokenizerInfo()
+        call("b2_tokenizer_get_info", self.h, C.byref(info))
+        self.info = info
+        self.stop_ids = [info.stop_ids[i] for i in range(info.n_stop)]
+
+    def encode(self, text: str | bytes, split_special: bool = True, add_special: bool = False) -> list:
+        """ids of `text`.  split_special: special added tokens written in the
+        text become their ids (otherwise they are read as text);
+        add_special: apply the file's post-processor (Llama-3's BOS)."""
+        import numpy as np
+        data = text.encode("utf-8") if isinstance(text, str) else bytes(text)
+        flags = (self.SPLIT_SPECIAL if split_special else 0) | (self.ADD_SPECIAL if add_special else 0)
+        n = C.c_size_t(0)
+        buf = np.empty(len(data) + 8, np.int32)
+        rc = lib().b2_tokenizer_encode(self.h, data, len(data), flags, buf.ctypes.data, buf.size, C.byref(n))
+        if rc == -3:
+            buf = np.empty(n.value, np.int32)
+            rc = lib().b2_tokenizer_encode(self.h, data, len(data), flags, buf.ctypes.data, buf.size, C.byref(n))
+        if rc != 0:
+            raise B2Error("b2_tokenizer_encode", rc)
+        return buf[: n.value].tolist()
+
+    def decode_bytes(self, ids, skip_special: bool = False) -> bytes:
+        import numpy as np
+        a = np.ascontiguousarray(np.asarray(ids, dtype=np.int32).reshape(-1))
+        n = C.c_size_t(0)
+        out = C.create_string_buffer(max(16, 8 * a.size))
+        rc = lib().b2_tokenizer_decode(self.h, a.ctypes.data, a.size, int(skip_special), out, len(out), C.byref(n))
+        if rc == -3:
+            out = C.create_string_buffer(n.value)
+            rc = lib().b2_tokenizer_decode(self.h, a.ctypes.data, a.size, int(skip_special), out, len(out),
+                                           C.byref(n))
+        if rc != 0:
+            raise B2Error("b2_tokenizer_decode", rc)
+        return out.raw[: n.value]
+
+    def decode(self, ids, skip_special: bool = False) -> str:
+        """Text of `ids`; bytes that do not form UTF-8 become U+FFFD (as the
+        HF library's decode does)."""
+        return self.decode_bytes(ids, skip_special).decode("utf-8", errors="replace")
+
+    def apply_chat_template(self, messages, add_generation_prompt: bool = True) -> str:
+        """messages: (role, content) pairs or {"role", "content"} dicts."""
+        pairs = [(m["role"], m["content"]) if isinstance(m, dict) else tuple(m) for m in messages]
+        roles = (C.c_char_p * max(1, len(pairs)))(*[r.encode() for r, _ in pairs])
+        contents = (C.c_char_p * max(1, len(pairs)))(*[c.encode() for _, c in pairs])
+        n = C.c_size_t(0)
+        cap = 256 + sum(len(r.encode()) + len(c.encode()) + 64 for r, c in pairs)
+        out = C.create_string_buffer(cap)
+        call("b2_tokenizer_apply_chat_template", self.h, C.cast(roles, vp), C.cast(contents, vp), len(pairs),
+             int(add_generation_prompt), out, len(out), C.byref(n))
+        return out.raw[: n.value].decode("utf-8", errors="replace")
+
+    def token_to_id(self, token: str) -> int | None:
+        b = token.encode()
+        v = i32(-1)
+        return v.value if lib().b2_tokenizer_token_to_id(self.h, b, len(b), C.byref(v)) == 0 else None
+
+    def close(self):
+        if getattr(self, "h", None):
+            lib().b2_tokenizer_destroy(self.h)
             self.h = None
 
     __del__ = close
@@ -417,6 +518,34 @@ class Model:
             return out
         call("b2_model_generate_greedy", self.h, steps, None)
         return None
+
+    def generate_text(self, tokenizer: "Tokenizer", prompt: str | None = None, messages=None,
+                      max_new_tokens: int = 32, chunk: int = 16):
+        """Text in, text out for one sequence (the reference's generate path,
+        apps/generate.cpp:858-940, for any vocabulary the tokenizer reads):
+        the prompt -- or the chat messages through the vocabulary's chat
+        template -- is encoded (with the file's post-processor, e.g. Llama-3's
+        BOS, for a plain prompt), prefilled, and decoded greedily on the
+        device `chunk` steps at a time until a stop id of the tokenizer
+        appears or max_new_tokens are generated.  Returns (text, prompt_ids,
+        new_ids): new_ids end with the stop id when one was produced; text is
+        their decode without special tokens.  Needs max_batch >= 1 and
+        len(prompt_ids) + max_new_tokens <= max_seq."""
+        import numpy as np
+        if messages is not None:
+            ids = tokenizer.encode(tokenizer.apply_chat_template(messages, add_generation_prompt=True))
+        else:
+            ids = tokenizer.encode(prompt, add_special=True)
+        self.prefill(np.asarray(ids, np.int64)[None, :], want_logits=False)
+        stop = set(tokenizer.stop_ids)
+        new = []
+        while len(new) < max_new_tokens:
+            got = self.generate_greedy(min(chunk, max_new_tokens - len(new)))[:, 0].tolist()
+            hit = next((k for k, t in enumerate(got) if t in stop), None)
+            new += got if hit is None else got[: hit + 1]
+            if hit is not None:
+                break
+        return tokenizer.decode(new, skip_special=True), ids, new
 
     def sync(self):
         call("b2_model_sync", self.h)

@@ -696,6 +696,9 @@ static void set_last_error(const char* msg) { g_last_error = msg ? msg : ""; }
 
 extern "C" const char* b2_last_error(void) { return g_last_error.c_str(); }
 
+// the same record for the host-only parts of the library (tokenizer.cpp)
+void b2_record_error(const char* msg) { set_last_error(msg); }
+
 extern "C" int b2_nccl_unique_id(void* out128) {
     B2_REQUIRE(out128);
     ncclUniqueId id;

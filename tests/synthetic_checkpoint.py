@@ -2,8 +2,9 @@
 model loader reads (test infrastructure): config.json (Qwen2-style fields,
 src/model/config.cpp:12-35), model.safetensors (bf16 tensors under the names
 ModelWeights::load_and_validate expects, src/model/config.cpp:63-118, q/k/v
-biases included) and tokenizer.json (a byte-level vocabulary of the 256 byte
-symbols, no merges, no special tokens: every byte of a prompt is one token).
+biases included) and tokenizer.json (the Qwen2 form: NFC, the Qwen2 split,
+byte-level; a vocabulary of the 256 byte symbols, no merges, no special
+tokens: every byte of a prompt is one token).
 Weights ~N(0, std) rounded to bf16, norm weights 1.0.  No real model,
 vocabulary or text is involved."""
 from __future__ import annotations
@@ -13,6 +14,11 @@ import os
 import struct
 
 import numpy as np
+
+
+# the Qwen2 pre-tokenizer split (src/tokenizer/bpe.cpp:170)
+QWEN2_SPLIT = (r"(?i:'s|'t|'re|'ve|'m|'ll|'d)|[^\r\n\p{L}\p{N}]?\p{L}+|\p{N}| ?[^\s\p{L}\p{N}]+[\r\n]*|"
+               r"\s*[\r\n]+|\s+(?!\S)|\s+")
 
 
 def byte_symbols() -> list[str]:
@@ -89,7 +95,12 @@ def make(path: str, *, vocab=512, hidden=256, inter=512, layers=2, heads=4, kv_h
         f.write(hj)
         for a in t.values():
             f.write(np.ascontiguousarray(a).tobytes())
-    tok = {"model": {"type": "BPE", "vocab": {s: i for i, s in enumerate(byte_symbols())}, "merges": []},
+    tok = {"normalizer": {"type": "NFC"},
+           "pre_tokenizer": {"type": "Sequence", "pretokenizers": [
+               {"type": "Split", "pattern": {"Regex": QWEN2_SPLIT}, "behavior": "Isolated", "invert": False},
+               {"type": "ByteLevel", "add_prefix_space": False, "trim_offsets": False, "use_regex": False}]},
+           "decoder": {"type": "ByteLevel", "add_prefix_space": True, "trim_offsets": True, "use_regex": True},
+           "model": {"type": "BPE", "vocab": {s: i for i, s in enumerate(byte_symbols())}, "merges": []},
            "added_tokens": []}
     with open(os.path.join(path, "tokenizer.json"), "w", encoding="utf-8") as f:
         json.dump(tok, f, ensure_ascii=False)
