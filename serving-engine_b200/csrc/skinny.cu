@@ -6,7 +6,7 @@
 // zero-filled by TMA), so one tcgen05.mma (M=128, N=NB, K=16) covers the
 // whole batch and the accumulator is NB fp32 columns of TMEM.  The kernel is
 // a weight stream: one CTA per SM, a ring of 64-deep stages (16 KB of
-// weights + NB x 64 of X) as deep as shared memory allows, and the flattened
+// weights + NB x 64 of X; 5 stages at NB = 32, see SkCfg), and the flattened
 // (tile, k block) iteration space cut into equal consecutive ranges, one per
 // CTA ("stream-K"), so every SM streams the same number of weight bytes
 // whatever the tile count.  A range crossing a tile boundary produces one
@@ -35,7 +35,14 @@ struct SkCfg {
     static constexpr uint32_t W_BYTES = 128 * 64 * 2;
     static constexpr uint32_t X_BYTES = NB * 64 * 2;
     static constexpr uint32_t STAGE = W_BYTES + X_BYTES;
-    static constexpr int STAGES = (200 * 1024) / STAGE > 12 ? 12 : (200 * 1024) / STAGE;
+    // NB = 32 (decode batches up to 32): 5 stages (100 KB).  Measured in the
+    // batch-8 / 32 decode step against 10 stages (200 KB): 2083 / 7268 tok/s
+    // against 1999 / 7102 -- the projections after the attention and the
+    // slab-sum consumers start sooner beside a smaller ring, and the weight
+    // stream keeps its rate (gate|up 42.2 us either way); 4 stages began to
+    // slow the stream.
+    static constexpr uint32_t BUDGET = NB <= 32 ? 104 * 1024 : 200 * 1024;
+    static constexpr int STAGES = BUDGET / STAGE > 12 ? 12 : BUDGET / STAGE;
     static constexpr uint32_t TMEM_COLS = 2 * NB;  // two accumulators
     static constexpr size_t SMEM = (size_t)STAGES * STAGE + 256 + 1024;
 };
@@ -192,7 +199,10 @@ struct SkF8Cfg {
     static constexpr uint32_t W_BYTES = 128 * 128;
     static constexpr uint32_t X_ATOM = NB * 128;  // NB rows x 64 halves
     static constexpr uint32_t STAGE = W_BYTES + 2 * X_ATOM;
-    static constexpr int STAGES = (200 * 1024) / STAGE > 8 ? 8 : (200 * 1024) / STAGE;
+    // NB = 32: 6 stages (147 KB); measured 2299 / 8007 tok/s at batch 8 / 32
+    // against 2263 / 7807 with 8 (5 stages: 2289 / 7991)
+    static constexpr uint32_t BUDGET = NB <= 32 ? 148 * 1024 : 200 * 1024;
+    static constexpr int STAGES = BUDGET / STAGE > 8 ? 8 : BUDGET / STAGE;
     static constexpr int NA = 4;                   // TMEM staging buffers of decoded weights
     static constexpr uint32_t COL_A = 2 * NB;      // after the two accumulators, 64 columns each
     static constexpr uint32_t TMEM_COLS = 2 * NB + 64 * NA <= 256 ? 256 : 512;
