@@ -345,17 +345,27 @@ __device__ __forceinline__ float sk_sum(const SkSlabs& a, int B, int b, int n) {
 __global__ void sk_qkv_rope_kernel(SkSlabs a, int B, const __half* __restrict__ bias, __half* __restrict__ qkv,
                                    int64_t ld, const float2* __restrict__ rope, int nq, int nkv, int D,
                                    const KvLayout kv, const int* __restrict__ positions, TraceSlot tr) {
-    griddep_wait();
-    griddep_launch_dependents();
-    trace_begin(tr);
     const int b = blockIdx.x, half = D >> 1, per_head = D >> 3;
     const int t = blockIdx.y * blockDim.x + threadIdx.x;
     const int head = t / per_head, i = (t - head * per_head) * 4;
-    if (head >= nq + 2 * nkv) {
+    const bool live = head < nq + 2 * nkv;
+    const int n1 = head * D + i, n2 = n1 + half;
+    // the bias is never written by a kernel: fetch it before the wait
+    __half bv1[4] = {}, bv2[4] = {};
+    if (bias && live) {
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+            bv1[e] = bias[n1 + e];
+            bv2[e] = bias[n2 + e];
+        }
+    }
+    griddep_wait();
+    griddep_launch_dependents();
+    trace_begin(tr);
+    if (!live) {
         trace_end(tr);
         return;
     }
-    const int n1 = head * D + i, n2 = n1 + half;
     const float4 s1 = sk_sum4(a, B, b, n1), s2 = sk_sum4(a, B, b, n2);
     float x1[4] = {s1.x, s1.y, s1.z, s1.w}, x2[4] = {s2.x, s2.y, s2.z, s2.w};
     __half o1[4], o2[4];
@@ -363,8 +373,8 @@ __global__ void sk_qkv_rope_kernel(SkSlabs a, int B, const __half* __restrict__ 
 #pragma unroll
     for (int e = 0; e < 4; ++e) {
         if (bias) {
-            x1[e] += __half2float(bias[n1 + e]);
-            x2[e] += __half2float(bias[n2 + e]);
+            x1[e] += __half2float(bv1[e]);
+            x2[e] += __half2float(bv2[e]);
         }
         x1[e] = __half2float(__float2half_rn(x1[e]));
         x2[e] = __half2float(__float2half_rn(x2[e]));
@@ -396,8 +406,8 @@ __global__ void sk_qkv_rope_kernel(SkSlabs a, int B, const __half* __restrict__ 
 // hidden[b] = (add ? hidden[b] : 0) + projection; then, when norm_w is set,
 // xn[b] = half(hidden[b] * rsqrt(mean(hidden[b]^2) + eps) * norm_w).  One
 // 1024-thread CTA per row (grid B), 4 columns per thread and pass; the row's
-// sum of squares is reduced inside the CTA (warp trees, then the 32 warps in
-// order, so deterministic).  (An 8-CTA cluster per row, partials shared
+// sum of squares is reduced inside the CTA (warp trees, then a tree over the
+// 32 warp sums: a fixed order, so deterministic).  (An 8-CTA cluster per row, partials shared
 // through distributed shared memory, took 7.4 us against 5.5 at batch 8.)
 constexpr int kAddNormRowThreads = 1024;
 
@@ -408,11 +418,18 @@ __global__ void __launch_bounds__(kAddNormRowThreads) sk_add_norm_kernel(SkSlabs
                                                                             TraceSlot tr) {
     __shared__ float red[kAddNormRowThreads / 32];
     __shared__ float s_rs;
+    constexpr int kMaxV = 4;  // float4 groups per thread (H <= 16384)
+    // the norm weights are never written by a kernel: fetch them before the wait
+    uint2 wv[kMaxV];
+#pragma unroll
+    for (int k = 0; k < kMaxV; ++k) {
+        const int n = 4 * ((int)threadIdx.x + k * kAddNormRowThreads);
+        wv[k] = norm_w && n < H ? *reinterpret_cast<const uint2*>(norm_w + n) : make_uint2(0u, 0u);
+    }
     griddep_wait();
     griddep_launch_dependents();
     trace_begin(tr);
     const int b = blockIdx.x;
-    constexpr int kMaxV = 4;  // float4 groups per thread (H <= 16384)
     float4 hv[kMaxV];
     float ss = 0.f;
 #pragma unroll
@@ -434,10 +451,9 @@ __global__ void __launch_bounds__(kAddNormRowThreads) sk_add_norm_kernel(SkSlabs
         ss = warp_sum(ss);
         if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = ss;
         __syncthreads();
-        if (threadIdx.x == 0) {
-            float tot = 0.f;
-            for (int w = 0; w < kAddNormRowThreads / 32; ++w) tot += red[w];
-            s_rs = rsqrtf(tot / (float)H + eps);
+        if (threadIdx.x < 32) {  // the 32 warp sums, as a fixed shuffle tree
+            const float tot = warp_sum(red[threadIdx.x]);
+            if (threadIdx.x == 0) s_rs = rsqrtf(tot / (float)H + eps);
         }
         __syncthreads();
         const float rs = s_rs;
@@ -446,9 +462,8 @@ __global__ void __launch_bounds__(kAddNormRowThreads) sk_add_norm_kernel(SkSlabs
             const int n = 4 * ((int)threadIdx.x + k * kAddNormRowThreads);
             if (n < H) {
                 const float4 v = hv[k];
-                const uint2 wv = *reinterpret_cast<const uint2*>(norm_w + n);
-                const float2 w01 = __half22float2(*reinterpret_cast<const __half2*>(&wv.x));
-                const float2 w23 = __half22float2(*reinterpret_cast<const __half2*>(&wv.y));
+                const float2 w01 = __half22float2(*reinterpret_cast<const __half2*>(&wv[k].x));
+                const float2 w23 = __half22float2(*reinterpret_cast<const __half2*>(&wv[k].y));
                 __half2 o0 = __floats2half2_rn(v.x * rs * w01.x, v.y * rs * w01.y);
                 __half2 o1 = __floats2half2_rn(v.z * rs * w23.x, v.w * rs * w23.y);
                 uint2 ov;
