@@ -426,8 +426,10 @@ __global__ void __launch_bounds__(kAddNormRowThreads) sk_add_norm_kernel(SkSlabs
         const int n = 4 * ((int)threadIdx.x + k * kAddNormRowThreads);
         wv[k] = norm_w && n < H ? *reinterpret_cast<const uint2*>(norm_w + n) : make_uint2(0u, 0u);
     }
-    griddep_wait();
+    // The dependent is the next skinny projection, which reads only weights
+    // before its own wait: let it launch (and start its weight stream) now.
     griddep_launch_dependents();
+    griddep_wait();
     trace_begin(tr);
     const int b = blockIdx.x;
     float4 hv[kMaxV];
@@ -478,8 +480,8 @@ __global__ void __launch_bounds__(kAddNormRowThreads) sk_add_norm_kernel(SkSlabs
 
 // act[b][i] = half(silu(gate) * up), silu(x) = x / (1 + exp(-x)) in fp32
 __global__ void sk_swiglu_kernel(SkSlabs g, SkSlabs u, int B, int I, __half* __restrict__ act, TraceSlot tr) {
+    griddep_launch_dependents();  // as sk_add_norm_kernel: the down projection follows
     griddep_wait();
-    griddep_launch_dependents();
     trace_begin(tr);
     const int64_t n = (int64_t)B * I / 4;
     for (int64_t e = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; e < n; e += (int64_t)gridDim.x * blockDim.x) {
