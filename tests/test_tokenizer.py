@@ -283,3 +283,25 @@ def test_reference_app_on_this_library(golden):
         got = _stdin_tokenize(_exe("tokenize_b2"), _path(kind), [c for _, c in cases])
         want = golden["expect"][kind]["ids"]
         assert got == [want[i] for i, _ in cases], kind
+
+
+def test_reference_tokenizer_is_qwen2_only(golden, tmp_path):
+    """What the library adds over the reference's tokenizer: it reads the
+    Qwen2 split only (src/tokenizer/bpe.cpp:170-270, one digit per piece, no
+    ignore_merges) and merges written as "a b" strings only.  On the Llama-3
+    and GPT-2 vocabularies (merges rewritten as strings so that it loads) it
+    departs from the HF library on most strings -- digit runs first of all --
+    where this library matches every one (test_golden_encode)."""
+    exe = _exe("tokenize_ref")
+    cases = [(i, c) for i, c in enumerate(golden["cases"]) if c]
+    for kind in ("llama3", "gpt2"):
+        with open(_path(kind), encoding="utf-8") as f:
+            d = json.load(f)
+        d["model"]["merges"] = [" ".join(m) if isinstance(m, list) else m for m in d["model"]["merges"]]
+        p = tmp_path / f"{kind}_string_merges.json"
+        p.write_text(json.dumps(d, ensure_ascii=False), encoding="utf-8")
+        got = _stdin_tokenize(exe, str(p), [c for _, c in cases])
+        want = golden["expect"][kind]["ids"]
+        wrong = [c for (i, c), g in zip(cases, got) if g != want[i]]
+        assert len(wrong) > len(cases) // 3, (kind, len(wrong))
+        assert "1234" in wrong
