@@ -262,7 +262,10 @@ def config_dict(args, world):
             "parallelism": f"tp{world}",
             "tp_exchange": (args.exchange if world > 1 else None),
             "weights": ("fp16" if args.weights == "fp16" else
-                        "fp8 e4m3 per-row copies for the decode GEMVs (b2_model_quantize_weights)"),
+                        "fp8 e4m3 per-row copies for the decode GEMVs (b2_model_quantize_weights)"
+                        if args.weights == "fp8" else
+                        "4-bit copies, fp32 scale per 128 weights, for the batch-1/2 decode GEMVs "
+                        "(b2_model_quantize_weights)"),
             "l2": f"inputs larger than L2: every step streams the model's {weight_gb(c):.1f} GB of fp16 weights "
                   f"(half that as fp8; divided over the tensor-parallel ranks; L2 126 MB)"}
 
@@ -365,8 +368,8 @@ def run_b2(args, rank, world, local):
                  theta=c["theta"], tied=False, max_batch=B, max_seq=max_seq, tp_rank=rank, tp_size=world,
                  nccl_id=nccl_id, kv_blocks=kv_blocks, block_size=PAGE)
     m.init_random(SEED_W, 0.02)
-    if args.weights == "fp8":  # decode GEMVs on per-row FP8 copies (prefill stays fp16)
-        m.quantize_weights("fp8")
+    if args.weights != "fp16":  # decode GEMVs on quantised copies (prefill stays fp16)
+        m.quantize_weights(args.weights)
     if world > 1 and args.exchange == "p2p":
         # decode-step partial sums over NVLink peer memory (fused into the
         # GEMVs) instead of NCCL all-reduces
@@ -515,7 +518,8 @@ def run_b2(args, rank, world, local):
             "metric": METRIC, "value": B * K / (ms * 1e-3), "unit": "tok/s", "n_gpus": world, "steps": K,
             "warmup": W, "ms_per_step": step_ms, "higher_is_better": True, "scaling": "strong",
             "vs_baseline": None,
-            "dtype": "f16" if args.weights == "fp16" else "f16 activations, fp8 e4m3 weights (per-row fp32 scales)",
+            "dtype": {"fp16": "f16", "fp8": "f16 activations, fp8 e4m3 weights (per-row fp32 scales)",
+                      "int4": "f16 activations, 4-bit weights (fp32 scale per 128)"}[args.weights],
             "data": "synthetic: seeded random-init fp16 weights ~N(0,0.02), uniform random prompt ids",
             "config": config_dict(args, world),
             "e2e": ({"value": B * K / (ms_e2e * 1e-3), "unit": "tok/s",
@@ -710,9 +714,10 @@ def main():
     ap.add_argument("--prompt", type=int, default=PROMPT, help="prompt length (512 for the metric)")
     ap.add_argument("--layers", type=int, default=0,
                     help="decoder depth override (reduced only for small profiler captures; 0 = the model's)")
-    ap.add_argument("--weights", default="fp16", choices=["fp16", "fp8"],
-                    help="decode GEMV weights: fp16 (the metric), or per-row FP8 E4M3 copies "
-                         "(b2_model_quantize_weights; batches the GEMV step takes)")
+    ap.add_argument("--weights", default="fp16", choices=["fp16", "fp8", "int4"],
+                    help="decode GEMV weights: fp16 (the metric), per-row FP8 E4M3 copies "
+                         "(b2_model_quantize_weights; batches the GEMV step takes), or 4-bit copies "
+                         "with a scale per 128 weights (batch 1-2)")
     ap.add_argument("--paged", action="store_true",
                     help="paged KV cache (16-position blocks scattered over a pool), mixed prompt lengths "
                          "prompt/2 .. 3*prompt/2, prefilled one sequence at a time")

@@ -233,6 +233,22 @@ int b2_quantize_fp8_rows(const void* w, int64_t rows, int K, void* q, float* sca
 int b2_gemv_fp8(const void* Wq, const float* scales, const void* x, void* y, int B, int N, int K, int out_f32,
                 void* stream);
 
+/* 4-bit weights for the decode GEMVs: per group of 128 consecutive weights
+ * of a row of w [rows, K] (half), scales[r, g] = max|w| / 7 (fp32 division;
+ * 0 for an all-zero group) and q = rint(w / scale) in [-7, 7], stored as
+ * q + 8 in 4 bits: q [rows, K/2] bytes, each 32-bit word holding 8
+ * consecutive weights, weight j of the word at bit 16*(j & 1) + 4*(j >> 1);
+ * scales [rows, K/128] fp32.  K % 128 == 0, 16-byte aligned w and q.  New
+ * API (the reference plans INT4 weights, RESULTS.md:39). */
+int b2_quantize_int4_rows(const void* w, int64_t rows, int K, void* q, float* scales, void* stream);
+
+/* y[b,n] = sum over groups g of scales[n,g] * dot(q[n, group g], x[b, group
+ * g]), x [B,K] half, fp32 accumulate, y [B,N] half (out_f32 != 0: fp32).
+ * K % 128 == 0, 16-byte aligned Wq and x.  The batch-1/2 decode GEMV of a
+ * 4-bit model (any B: run two sequences at a time).  New API. */
+int b2_gemv_int4(const void* Wq, const float* scales, const void* x, void* y, int B, int N, int K, int out_f32,
+                 void* stream);
+
 /* Copy K/V rows [num_tokens, nkv, D] into head-major caches [nkv, max_seq, D]
  * at positions start_pos..start_pos+num_tokens-1 (positions >= max_seq are
  * skipped).  Replaces engine::cuda::append_kv_cache (src/runtime/kv_cache.h:80-91). */
@@ -387,9 +403,12 @@ int b2_model_set_sampling(b2_model* m, const b2_sampler_config* cfg);
  * the bytes of a step.  Batches of 3-4 (GEMVs bound by arithmetic, not
  * bytes) and prefill keep the fp16 weights.  Call again after changing
  * weights; B2_WEIGHTS_FP16 returns to fp16 everywhere (the copies are kept).
- * Synchronises.  New API (the reference plans quantised weights as P8,
- * RESULTS.md:39). */
-enum { B2_WEIGHTS_FP16 = 0, B2_WEIGHTS_FP8_E4M3 = 1 };
+ * B2_WEIGHTS_INT4 makes 4-bit copies (b2_quantize_int4_rows: a scale per 128
+ * weights) read by the decode GEMVs at 1-2 sequences -- about a quarter of
+ * the bytes; every other step and prefill keep the fp16 weights.  Hidden,
+ * head and FFN widths must be multiples of 128.  Synchronises.  New API
+ * (the reference plans quantised weights as P8, RESULTS.md:39). */
+enum { B2_WEIGHTS_FP16 = 0, B2_WEIGHTS_FP8_E4M3 = 1, B2_WEIGHTS_INT4 = 2 };
 int b2_model_quantize_weights(b2_model* m, int format);
 
 /* Clears the KV cache positions of all sequences (sets lengths to 0). */

@@ -505,6 +505,60 @@ def dequantize_e4m3_rows(q, scale) -> np.ndarray:
     return (e4m3_decode(q) * np.asarray(scale, np.float32)[:, None]).astype(np.float32)
 
 
+I4_GROUP = 128                                         # weights per scale
+_I4_SHIFT = np.array([16 * (j & 1) + 4 * (j >> 1) for j in range(8)], np.uint32)
+
+
+def quantize_int4_rows(w):
+    """4-bit codes of a [rows, K] matrix in the library's packed layout
+    (include/b2engine.h, b2_quantize_int4_rows) and float32 group scales
+    [rows, K/128]: scale = max|w| / 7 over each group of 128 (float32
+    division), q = rint(w / scale) in [-7, 7] (0 for an all-zero group),
+    stored as q + 8, weight j of each 8-weight word at bit
+    16*(j & 1) + 4*(j >> 1)."""
+    w = np.asarray(w, np.float32)
+    rows, K = w.shape
+    assert K % I4_GROUP == 0
+    g = w.reshape(rows, K // I4_GROUP, I4_GROUP)
+    scale = (np.max(np.abs(g), axis=2) / np.float32(7.0)).astype(np.float32)
+    safe = np.where(scale > 0, scale, np.float32(1.0)).astype(np.float32)
+    q = np.where(scale[..., None] > 0, np.rint(g / safe[..., None]), np.float32(0.0))
+    u = (np.clip(q, -7, 7).astype(np.int32) + 8).astype(np.uint32).reshape(rows, K // 8, 8)
+    words = np.bitwise_or.reduce(u << _I4_SHIFT, axis=2).astype("<u4")
+    return words.view(np.uint8).reshape(rows, K // 2), scale
+
+
+def int4_codes(packed) -> np.ndarray:
+    """Packed 4-bit weights [rows, K/2] -> the signed codes q [rows, K]."""
+    packed = np.ascontiguousarray(packed, np.uint8)
+    rows = packed.shape[0]
+    words = packed.view("<u4").reshape(rows, -1, 1)
+    u = (words >> _I4_SHIFT) & np.uint32(0xF)
+    return u.reshape(rows, -1).astype(np.int32) - 8
+
+
+def dequantize_int4_rows(packed, scale) -> np.ndarray:
+    q = int4_codes(packed).astype(np.float32)
+    rows, K = q.shape
+    s = np.repeat(np.asarray(scale, np.float32), I4_GROUP, axis=1)
+    return (q * s).astype(np.float32)
+
+
+def int4_weights(w: dict) -> dict:
+    """The seeded weights with every projection and the lm_head replaced by
+    their 4-bit round trip, rounded to fp16 (the oracle's weight type)."""
+    out = dict(w)
+    out["layers"] = []
+    for L in w["layers"]:
+        M = dict(L)
+        for n in ("wq", "wk", "wv", "wo", "wg", "wu", "wd"):
+            M[n] = f16(dequantize_int4_rows(*quantize_int4_rows(L[n])))
+        out["layers"].append(M)
+    if "lm_head" in w:
+        out["lm_head"] = f16(dequantize_int4_rows(*quantize_int4_rows(w["lm_head"])))
+    return out
+
+
 def fp8_weights(w: dict) -> dict:
     """The seeded weights with every projection and the lm_head replaced by
     their per-row E4M3 round trip, rounded to fp16 (the oracle's weight

@@ -80,6 +80,8 @@ _SIGS = {
     "b2_gemv_batched": (i32, [vp, vp, vp, vp, i32, i32, i32, i32, i32, vp]),
     "b2_quantize_fp8_rows": (i32, [vp, i64, i32, vp, vp, vp]),
     "b2_gemv_fp8": (i32, [vp, vp, vp, vp, i32, i32, i32, i32, vp]),
+    "b2_quantize_int4_rows": (i32, [vp, i64, i32, vp, vp, vp]),
+    "b2_gemv_int4": (i32, [vp, vp, vp, vp, i32, i32, i32, i32, vp]),
     "b2_append_kv_cache": (i32, [vp, vp, vp, vp, i32, i32, i32, i32, i32, vp]),
     "b2_sampler_create": (i32, [i32, i32, C.POINTER(vp)]),
     "b2_sampler_destroy": (i32, [vp]),
@@ -429,11 +431,12 @@ class Model:
         cfg = SamplerConfig(temperature, top_k, top_p, 1.0, seed)
         call("b2_model_set_sampling", self.h, C.byref(cfg))
 
-    WEIGHTS = {"fp16": 0, "fp8": 1}
+    WEIGHTS = {"fp16": 0, "fp8": 1, "int4": 2}
 
     def quantize_weights(self, fmt="fp8"):
         """Decode GEMVs on per-row FP8 (E4M3) copies of the weights ("fp8"),
-        or back on the fp16 weights ("fp16")."""
+        on 4-bit copies with a scale per 128 weights ("int4", batch 1-2), or
+        back on the fp16 weights ("fp16")."""
         call("b2_model_quantize_weights", self.h, self.WEIGHTS[fmt])
 
     def prefill(self, ids, want_logits=True):

@@ -70,30 +70,85 @@ __device__ __forceinline__ void load_rows(uint4 (&w)[R][U], const uint4* const (
     }
 }
 
-// Weight row r of matrix m (0: W, 1: W2) as 16-byte chunks: 8 halves, or
-// 16 e4m3 codes when F8.
-template <bool F8>
+// Weight formats of the register-streaming GEMV.
+enum WFormat { WF_F16 = 0, WF_E4M3 = 1, WF_I4 = 2 };
+
+// Weight row r of matrix m (0: W, 1: W2) as 16-byte chunks: 8 halves, 16
+// e4m3 codes, or 32 4-bit codes.
+template <int WF>
 __device__ __forceinline__ const uint4* weight_row(const GemvParams& p, int m, int r) {
-    if constexpr (F8)
+    if constexpr (WF == WF_E4M3)
         return reinterpret_cast<const uint4*>((m ? p.W8b : p.W8) + (size_t)r * p.K);
+    else if constexpr (WF == WF_I4)
+        return reinterpret_cast<const uint4*>((m ? p.W8b : p.W8) + (size_t)r * (p.K >> 1));
     else
         return reinterpret_cast<const uint4*>((m ? p.W2 : p.W) + (size_t)r * p.K);
 }
 
-template <int R, int OM, bool F8>
-__device__ __forceinline__ void task_rows(const GemvParams& p, int t, const uint4* (&rp)[R]) {
+// Row index and matrix of task t's rows, in the order task_rows gives them.
+template <int R, int OM>
+__device__ __forceinline__ void task_row_ids(const GemvParams& p, int t, int (&row)[R], int (&mat)[R]) {
     if constexpr (OM == OUT_QKV) {
         const int half = p.D >> 1;
         const int h = t / half, i = t - h * half;
-        const int r0 = h * p.D + i;
-        rp[0] = weight_row<F8>(p, 0, r0);
-        rp[1] = weight_row<F8>(p, 0, r0 + half);
+        row[0] = h * p.D + i;
+        row[1] = h * p.D + i + half;
+        mat[0] = mat[1] = 0;
     } else if constexpr (OM == OUT_SWIGLU) {
-        rp[0] = weight_row<F8>(p, 0, t);
-        rp[1] = weight_row<F8>(p, 1, t);
+        row[0] = row[1] = t;
+        mat[0] = 0;
+        mat[1] = 1;
     } else {
-        rp[0] = weight_row<F8>(p, 0, t);
+        row[0] = t;
+        mat[0] = 0;
     }
+}
+
+template <int R, int OM, int WF>
+__device__ __forceinline__ void task_rows(const GemvParams& p, int t, const uint4* (&rp)[R]) {
+    int row[R], mat[R];
+    task_row_ids<R, OM>(p, t, row, mat);
+#pragma unroll
+    for (int r = 0; r < R; ++r) rp[r] = weight_row<WF>(p, mat[r], row[r]);
+}
+
+// 4-bit weights: the group-scale rows of task t's rows.
+template <int R, int OM>
+__device__ __forceinline__ void task_group_scales(const GemvParams& p, int t, const float* (&sp)[R]) {
+    int row[R], mat[R];
+    task_row_ids<R, OM>(p, t, row, mat);
+    const int groups = p.K / kI4Group;
+#pragma unroll
+    for (int r = 0; r < R; ++r) sp[r] = (mat[r] ? p.wsc2 : p.wsc) + (size_t)row[r] * groups;
+}
+
+// The scales of the chunks load_rows brings (chunk c of a row lies in group
+// c / 4: 32 weights per chunk, 128 per group).
+template <int R, int U>
+__device__ __forceinline__ void load_group_scales(float (&sc)[R][U], const float* const (&sp)[R], int cbase,
+                                                  int KC, int lane) {
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+        const int c = cbase + u * 32 + lane;
+#pragma unroll
+        for (int r = 0; r < R; ++r) sc[r][u] = c < KC ? __ldg(sp[r] + (c >> 2)) : 0.f;
+    }
+}
+
+// One 32-bit word of 4-bit codes (8 weights, kI4Group's bit layout) -> 8
+// halves in weight order.  (0x6400 | u) is the half 1024 + u exactly for
+// u < 1024, so subtracting 1032 gives u - 8 = q exactly.
+__device__ __forceinline__ uint4 i4word_to_half8(uint32_t w) {
+    const __half2 bias = __halves2half2(__ushort_as_half((unsigned short)0x6408u),
+                                        __ushort_as_half((unsigned short)0x6408u));
+    uint32_t o[4];
+#pragma unroll
+    for (int pr = 0; pr < 4; ++pr) {
+        const uint32_t v = ((w >> (4 * pr)) & 0x000F000Fu) | 0x64006400u;
+        const __half2 h = __hsub2(*reinterpret_cast<const __half2*>(&v), bias);
+        o[pr] = *reinterpret_cast<const uint32_t*>(&h);
+    }
+    return make_uint4(o[0], o[1], o[2], o[3]);
 }
 
 // Per-row scales of task t's rows (FP8 weights), in task_rows' order.
@@ -138,12 +193,14 @@ __device__ __forceinline__ void e4m3x16_to_half(const uint4& w, uint4& lo, uint4
 // in one round instead of two (Llama-3-8B q|k|v: 12.2 -> 9.8 us); the o and
 // down GEMVs lose more to the tighter register budget than they gain (down
 // 19.7 -> 23.0 us), and the exchange consumers would spill.
-constexpr int gemv_min_ctas(int NT, int BT, int XM, int OM) {
-    return NT != 256 ? 1 : (BT == 1 && XM != X_SUM && (OM == OUT_QKV || OM == OUT_LOGITS)) ? 3 : 2;
+// (4-bit weights keep two: their dequantisation needs the registers, and
+// with 80 the q|k|v and lm_head forms spill.)
+constexpr int gemv_min_ctas(int NT, int BT, int XM, int OM, int WF) {
+    return NT != 256 ? 1 : (BT == 1 && XM != X_SUM && (OM == OUT_QKV || OM == OUT_LOGITS) && WF != WF_I4) ? 3 : 2;
 }
 
-template <int R, int BT, int XM, int OM, int U, bool F8, int NT>
-__global__ void __launch_bounds__(NT, gemv_min_ctas(NT, BT, XM, OM)) gemv_vec_kernel(const GemvParams p) {
+template <int R, int BT, int XM, int OM, int U, int WF, int NT>
+__global__ void __launch_bounds__(NT, gemv_min_ctas(NT, BT, XM, OM, WF)) gemv_vec_kernel(const GemvParams p) {
     constexpr int kGemvWarps = NT / 32;
     extern __shared__ __align__(16) uint4 xs[];  // [BT][K8] packed half
     __shared__ float s_rs[BT];
@@ -153,7 +210,7 @@ __global__ void __launch_bounds__(NT, gemv_min_ctas(NT, BT, XM, OM)) gemv_vec_ke
 
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const int K8 = p.K >> 3;                  // 16-byte chunks of x (8 halves)
-    const int KC = F8 ? (p.K >> 4) : K8;       // 16-byte chunks of a weight row
+    const int KC = WF == WF_E4M3 ? (p.K >> 4) : WF == WF_I4 ? (p.K >> 5) : K8;  // 16-byte chunks of a weight row
     const int NB = (KC + 32 * U - 1) / (32 * U);
     // Tasks are dealt round-robin over all warps of the grid, except for
     // OUT_PUSH, where each CTA owns a contiguous block of rows so that it can
@@ -167,10 +224,16 @@ __global__ void __launch_bounds__(NT, gemv_min_ctas(NT, BT, XM, OM)) gemv_vec_ke
 
     // Weights do not depend on the previous kernel: start streaming them now.
     uint4 wn[R][U];
+    float sn[R][U];  // 4-bit weights: the chunks' group scales
     if (t < t_end) {
         const uint4* rp[R];
-        task_rows<R, OM, F8>(p, t, rp);
+        task_rows<R, OM, WF>(p, t, rp);
         load_rows<R, U>(wn, rp, 0, KC, lane);
+        if constexpr (WF == WF_I4) {
+            const float* sp[R];
+            task_group_scales<R, OM>(p, t, sp);
+            load_group_scales<R, U>(sn, sp, 0, KC, lane);
+        }
     }
 
     // X_SUM reads the previous kernel's output only through the tagged
@@ -203,25 +266,56 @@ __global__ void __launch_bounds__(NT, gemv_min_ctas(NT, BT, XM, OM)) gemv_vec_ke
 
         for (int cb = 0; cb < NB; ++cb) {
             uint4 wc[R][U];
+            float scc[R][U];
 #pragma unroll
             for (int u = 0; u < U; ++u)
 #pragma unroll
-                for (int r = 0; r < R; ++r) wc[r][u] = wn[r][u];
+                for (int r = 0; r < R; ++r) {
+                    wc[r][u] = wn[r][u];
+                    if constexpr (WF == WF_I4) scc[r][u] = sn[r][u];
+                }
             // issue the next batch (this task's next chunk batch, or the next task's first)
             {
                 int nt = t, ncb = cb + 1;
                 if (ncb == NB) { nt = t + t_step; ncb = 0; }
                 if (nt < t_end) {
                     const uint4* rp[R];
-                    task_rows<R, OM, F8>(p, nt, rp);
+                    task_rows<R, OM, WF>(p, nt, rp);
                     load_rows<R, U>(wn, rp, ncb * 32 * U, KC, lane);
+                    if constexpr (WF == WF_I4) {
+                        const float* sp[R];
+                        task_group_scales<R, OM>(p, nt, sp);
+                        load_group_scales<R, U>(sn, sp, ncb * 32 * U, KC, lane);
+                    }
                 }
             }
 #pragma unroll
             for (int u = 0; u < U; ++u) {
                 const int c = cb * 32 * U + u * 32 + lane;
                 if (c < KC) {
-                    if constexpr (F8) {  // 16 weights: x chunks 2c and 2c + 1
+                    if constexpr (WF == WF_I4) {  // 32 weights: x chunks 4c .. 4c + 3, one group scale
+                        uint4 hw[R][4];
+#pragma unroll
+                        for (int r = 0; r < R; ++r) {
+                            hw[r][0] = i4word_to_half8(wc[r][u].x);
+                            hw[r][1] = i4word_to_half8(wc[r][u].y);
+                            hw[r][2] = i4word_to_half8(wc[r][u].z);
+                            hw[r][3] = i4word_to_half8(wc[r][u].w);
+                        }
+#pragma unroll
+                        for (int b = 0; b < BT; ++b) {
+                            const uint4* xb = xs + b * K8 + 4 * c;
+                            const uint4 x0 = xb[0], x1 = xb[1], x2 = xb[2], x3 = xb[3];
+#pragma unroll
+                            for (int r = 0; r < R; ++r) {
+                                float part = dot8_mixed(hw[r][0], x0, 0.f);
+                                part = dot8_mixed(hw[r][1], x1, part);
+                                part = dot8_mixed(hw[r][2], x2, part);
+                                part = dot8_mixed(hw[r][3], x3, part);
+                                acc[r][b] = fmaf(part, scc[r][u], acc[r][b]);
+                            }
+                        }
+                    } else if constexpr (WF == WF_E4M3) {  // 16 weights: x chunks 2c and 2c + 1
                         uint4 lo[R], hi[R];
 #pragma unroll
                         for (int r = 0; r < R; ++r) e4m3x16_to_half(wc[r][u], lo[r], hi[r]);
@@ -246,7 +340,7 @@ __global__ void __launch_bounds__(NT, gemv_min_ctas(NT, BT, XM, OM)) gemv_vec_ke
         for (int r = 0; r < R; ++r)
 #pragma unroll
             for (int b = 0; b < BT; ++b) acc[r][b] = warp_sum(acc[r][b]);
-        if constexpr (F8) {  // the rows' scales
+        if constexpr (WF == WF_E4M3) {  // the rows' scales
             float sc[R];
             task_scales<R, OM>(p, t, sc);
 #pragma unroll
@@ -288,10 +382,10 @@ static size_t gemv_smem(int BT, int XM, int K, int cs) {
            (XM == X_SUM ? (size_t)BT * (((K >> 3) + cs - 1) / cs) * 8 * sizeof(float) : 0);
 }
 
-template <int R, int BT, int XM, int OM, int U, bool F8, int NT>
+template <int R, int BT, int XM, int OM, int U, int WF, int NT>
 static int launch_vec(const GemvParams& p, cudaStream_t s, bool pdl) {
     constexpr int kGemvThreads = NT, kGemvWarps = NT / 32;
-    auto kern = gemv_vec_kernel<R, BT, XM, OM, U, F8, NT>;
+    auto kern = gemv_vec_kernel<R, BT, XM, OM, U, WF, NT>;
     const int cs = XM == X_SUM ? xsum_cluster() : 1;
     const size_t smem = gemv_smem(BT, XM, p.K, cs);
     if (smem > (size_t)kGemvSmemMax) return B2_ERR_UNSUPPORTED;
@@ -353,35 +447,43 @@ int gemv_batch_tile(int K) {
     return 1;
 }
 
-template <int R, int BT, int XM, int OM, int U, bool F8>
+template <int R, int BT, int XM, int OM, int U, int WF>
 static int launch_nt(const GemvParams& p, cudaStream_t s, bool pdl) {
     const int cs = XM == X_SUM ? xsum_cluster() : 1;
-    if (gemv_smem(BT, XM, p.K, cs) <= (size_t)kGemvSmemPair) return launch_vec<R, BT, XM, OM, U, F8, 256>(p, s, pdl);
-    return launch_vec<R, BT, XM, OM, U, F8, 512>(p, s, pdl);
+    if (gemv_smem(BT, XM, p.K, cs) <= (size_t)kGemvSmemPair) return launch_vec<R, BT, XM, OM, U, WF, 256>(p, s, pdl);
+    return launch_vec<R, BT, XM, OM, U, WF, 512>(p, s, pdl);
 }
 
-template <int R, int XM, int OM, int U, bool F8>
+template <int R, int XM, int OM, int U, int WF>
 static int dispatch_bt_w(const GemvParams& p, cudaStream_t s, bool pdl) {
-    if (p.B <= 1) return launch_nt<R, 1, XM, OM, U, F8>(p, s, pdl);
-    if (p.B <= 2) return launch_nt<R, 2, XM, OM, U, F8>(p, s, pdl);
-    if (p.B <= 4) return launch_nt<R, 4, XM, OM, U, F8>(p, s, pdl);
-    return launch_nt<R, 8, XM, OM, U, F8>(p, s, pdl);
+    if (p.B <= 1) return launch_nt<R, 1, XM, OM, U, WF>(p, s, pdl);
+    if (p.B <= 2) return launch_nt<R, 2, XM, OM, U, WF>(p, s, pdl);
+    if constexpr (WF == WF_I4) {
+        return B2_ERR_UNSUPPORTED;  // 4-bit weights: batch tiles of 1 and 2
+    } else {
+        if (p.B <= 4) return launch_nt<R, 4, XM, OM, U, WF>(p, s, pdl);
+        return launch_nt<R, 8, XM, OM, U, WF>(p, s, pdl);
+    }
 }
 
-// FP8 weights: 16-byte chunks of 16 codes (U chunks per lane and batch, as
-// for halves, so the same bytes are in flight with twice the weights).
+// FP8 weights: 16-byte chunks of 16 codes, 4-bit weights: of 32 codes (U
+// chunks per lane and batch, as for halves, so the same bytes are in flight
+// with two or four times the weights).
 template <int R, int XM, int OM, int U>
 static int dispatch_bt(const GemvParams& p, cudaStream_t s, bool pdl) {
-    if (p.W8) return dispatch_bt_w<R, XM, OM, U, true>(p, s, pdl);
-    return dispatch_bt_w<R, XM, OM, U, false>(p, s, pdl);
+    if (p.W8 && p.w4) return dispatch_bt_w<R, XM, OM, U, WF_I4>(p, s, pdl);
+    if (p.W8) return dispatch_bt_w<R, XM, OM, U, WF_E4M3>(p, s, pdl);
+    return dispatch_bt_w<R, XM, OM, U, WF_F16>(p, s, pdl);
 }
 
 int gemv_launch(const GemvParams& p, XMode xm, OutMode om, cudaStream_t s, bool pdl) {
     if (p.tasks <= 0 || p.B <= 0) return B2_OK;
     if (p.K <= 0 || (p.K & 7) || !aligned16(p.x) || (p.ldx & 7)) return B2_ERR_UNSUPPORTED;
-    if (p.W8 ? ((p.K & 15) || !aligned16(p.W8) || !p.wsc || (om == OUT_SWIGLU && (!aligned16(p.W8b) || !p.wsc2)))
+    if (p.W8 ? ((p.K & (p.w4 ? kI4Group - 1 : 15)) || !aligned16(p.W8) || !p.wsc ||
+                (om == OUT_SWIGLU && (!aligned16(p.W8b) || !p.wsc2)))
              : !aligned16(p.W))
         return B2_ERR_UNSUPPORTED;
+    if (p.W8 && p.w4 && p.B > 2) return B2_ERR_UNSUPPORTED;
     if (p.B > 8 || p.B > gemv_batch_tile(p.K)) return B2_ERR_UNSUPPORTED;
     if (om == OUT_SWIGLU && !p.W8 && !aligned16(p.W2)) return B2_ERR_UNSUPPORTED;
     if ((xm == X_NORM || xm == X_SUM) && (!p.norm_w || !aligned16(p.norm_w))) return B2_ERR_UNSUPPORTED;

@@ -128,7 +128,20 @@ struct GemvParams {
     const uint8_t* W8b;
     const float* wsc;
     const float* wsc2;
+    // w4 = 1: W8 / W8b hold 4-bit weights instead ([rows][K/2] bytes, the
+    // layout of kI4Group below) and wsc / wsc2 one fp32 scale per 128
+    // weights ([rows][K/128]), applied to each group's partial dot product.
+    // K % 128 == 0; batch tiles of 1 and 2.
+    int w4;
 };
+
+// 4-bit weights (b2_quantize_int4_rows): per group of 128 consecutive
+// weights of a row, scale = max|w| / 7 (fp32 division; 0 for an all-zero
+// group) and q = rint(w / scale) in [-7, 7], stored as q + 8.  A row is K/2
+// bytes; each 32-bit word holds 8 consecutive weights, weight j of the word
+// at bit 16*(j & 1) + 4*(j >> 1), so (word >> 4p) & 0x000F000F is the pair
+// (2p, 2p + 1) as the low bits of two halves.
+constexpr int kI4Group = 128;
 
 constexpr int kPushRows = 128;   // OUT_PUSH rows per CTA at most
 
@@ -168,5 +181,7 @@ int gemv_batch_tile(int K);
 
 // Per-row FP8 (E4M3) quantisation of a half matrix [rows][K] (quant.cu).
 int quantize_e4m3_rows(const __half* w, int64_t rows, int K, uint8_t* q, float* scales, cudaStream_t s);
+// 4-bit codes [rows][K/2] and group scales [rows][K/128] (layout: kI4Group)
+int quantize_i4_rows(const __half* w, int64_t rows, int K, uint8_t* q, float* scales, cudaStream_t s);
 
 }  // namespace b2

@@ -57,6 +57,9 @@ constexpr int kGemvMaxBatch = 4;
 // are streamed instead.  The batched tensor-core step (batch > 4) reads the
 // FP8 copies up to 128 sequences (skinny.cu: weight tiles decoded into TMEM).
 constexpr int kFp8MaxBatch = 2;
+// 4-bit weights: the GEMV step at batch 1-2 only (the batched tensor-core
+// step streams the fp16 weights).
+constexpr int kI4MaxBatch = 2;
 constexpr int kMaxBatch = 256;
 
 struct AttnParams;
@@ -578,7 +581,8 @@ using namespace b2;
 // ---------------------------------------------------------------------------
 // model object
 // ---------------------------------------------------------------------------
-// One quantised copy of a projection: E4M3 codes [rows][K] and a scale per row.
+// One quantised copy of a projection: E4M3 codes [rows][K] and a scale per
+// row, or 4-bit codes [rows][K/2] and a scale per 128 weights (kI4Group).
 struct Fp8W {
     uint8_t* q = nullptr;
     float* sc = nullptr;
@@ -588,6 +592,7 @@ struct LayerW {
     __half *wqkv = nullptr, *bqkv = nullptr, *wo = nullptr, *wg = nullptr, *wu = nullptr, *wd = nullptr;
     __half *ln1 = nullptr, *ln2 = nullptr;
     Fp8W f8qkv, f8o, f8g, f8u, f8d;  // b2_model_quantize_weights
+    Fp8W i4qkv, i4o, i4g, i4u, i4d;  // its 4-bit form
 };
 
 struct b2_model {
@@ -602,7 +607,9 @@ struct b2_model {
     __half* embed = nullptr;
     __half* lm_head = nullptr;  // local vocabulary shard
     Fp8W f8lm;                  // its quantised copy
+    Fp8W i4lm;                  // its 4-bit copy
     bool wfp8 = false;          // decode GEMVs read the FP8 copies
+    bool wint4 = false;         // decode GEMVs (batch 1-2) read the 4-bit copies
     __half* final_norm = nullptr;
     std::vector<LayerW> layers;
 
@@ -1246,6 +1253,10 @@ static int launch_qkv(b2_model* m, int l, int B, bool pdl, bool xch = false) {
     if (m->wfp8 && B <= kFp8MaxBatch) {
         p.W8 = w.f8qkv.q;
         p.wsc = w.f8qkv.sc;
+    } else if (m->wint4 && B <= kI4MaxBatch) {
+        p.W8 = w.i4qkv.q;
+        p.wsc = w.i4qkv.sc;
+        p.w4 = 1;
     }
     if (xch && l > 0) {
         set_exchange(m, p, 2 * (l - 1) + 1, m->hidden2, m->hidden);
@@ -1285,6 +1296,10 @@ static int launch_o(b2_model* m, int l, int B, bool pdl, bool xch = false) {
     if (m->wfp8 && B <= kFp8MaxBatch) {
         p.W8 = m->layers[l].f8o.q;
         p.wsc = m->layers[l].f8o.sc;
+    } else if (m->wint4 && B <= kI4MaxBatch) {
+        p.W8 = m->layers[l].i4o.q;
+        p.wsc = m->layers[l].i4o.sc;
+        p.w4 = 1;
     }
     p.K = m->nq * c.head_dim;
     p.tasks = c.hidden_size;
@@ -1313,6 +1328,12 @@ static int launch_gateup(b2_model* m, int l, int B, bool pdl, bool xch = false) 
         p.W8b = w.f8u.q;
         p.wsc = w.f8g.sc;
         p.wsc2 = w.f8u.sc;
+    } else if (m->wint4 && B <= kI4MaxBatch) {
+        p.W8 = w.i4g.q;
+        p.W8b = w.i4u.q;
+        p.wsc = w.i4g.sc;
+        p.wsc2 = w.i4u.sc;
+        p.w4 = 1;
     }
     p.K = c.hidden_size;
     p.tasks = m->inter;
@@ -1338,6 +1359,10 @@ static int launch_down(b2_model* m, int l, int B, bool pdl, bool xch = false) {
     if (m->wfp8 && B <= kFp8MaxBatch) {
         p.W8 = m->layers[l].f8d.q;
         p.wsc = m->layers[l].f8d.sc;
+    } else if (m->wint4 && B <= kI4MaxBatch) {
+        p.W8 = m->layers[l].i4d.q;
+        p.wsc = m->layers[l].i4d.sc;
+        p.w4 = 1;
     }
     p.K = m->inter;
     p.tasks = c.hidden_size;
@@ -1362,6 +1387,10 @@ static int launch_lm_head(b2_model* m, int B, bool pdl, bool xch = false) {
     if (m->wfp8 && B <= kFp8MaxBatch) {
         p.W8 = m->f8lm.q;
         p.wsc = m->f8lm.sc;
+    } else if (m->wint4 && B <= kI4MaxBatch) {
+        p.W8 = m->i4lm.q;
+        p.wsc = m->i4lm.sc;
+        p.w4 = 1;
     }
     p.K = c.hidden_size;
     p.tasks = m->vocab_l;
@@ -1606,12 +1635,20 @@ static int quantize_proj(b2_model* m, const __half* w, int64_t rows, int K, Fp8W
     return quantize_e4m3_rows(w, rows, K, f.q, f.sc, m->stream);
 }
 
+static int quantize_proj_i4(b2_model* m, const __half* w, int64_t rows, int K, Fp8W& f) {
+    if (!f.q) {
+        M_TRY(model_alloc(m, reinterpret_cast<void**>(&f.q), (size_t)rows * (K / 2)));
+        M_TRY(model_alloc(m, reinterpret_cast<void**>(&f.sc), (size_t)rows * (K / kI4Group) * sizeof(float)));
+    }
+    return quantize_i4_rows(w, rows, K, f.q, f.sc, m->stream);
+}
+
 extern "C" int b2_model_quantize_weights(b2_model* m, int format) {
-    B2_REQUIRE(m && (format == B2_WEIGHTS_FP16 || format == B2_WEIGHTS_FP8_E4M3));
+    B2_REQUIRE(m && (format == B2_WEIGHTS_FP16 || format == B2_WEIGHTS_FP8_E4M3 || format == B2_WEIGHTS_INT4));
     const b2_model_config& c = m->cfg;
     const int H = c.hidden_size, qd = m->nq * c.head_dim;
-    const bool on = format == B2_WEIGHTS_FP8_E4M3;
-    if (on) {
+    const bool f8 = format == B2_WEIGHTS_FP8_E4M3, i4 = format == B2_WEIGHTS_INT4;
+    if (f8) {
         if ((H % 16) || (qd % 16) || (m->inter % 16)) return B2_ERR_UNSUPPORTED;
         for (int l = 0; l < c.num_layers; ++l) {
             LayerW& w = m->layers[l];
@@ -1624,8 +1661,22 @@ extern "C" int b2_model_quantize_weights(b2_model* m, int format) {
         M_TRY(quantize_proj(m, m->lm_head, m->vocab_l, H, m->f8lm));
         B2_TRY(cudaStreamSynchronize(m->stream));
     }
-    if (on != m->wfp8) {
-        m->wfp8 = on;
+    if (i4) {
+        if ((H % kI4Group) || (qd % kI4Group) || (m->inter % kI4Group)) return B2_ERR_UNSUPPORTED;
+        for (int l = 0; l < c.num_layers; ++l) {
+            LayerW& w = m->layers[l];
+            M_TRY(quantize_proj_i4(m, w.wqkv, m->qkv_rows, H, w.i4qkv));
+            M_TRY(quantize_proj_i4(m, w.wo, H, qd, w.i4o));
+            M_TRY(quantize_proj_i4(m, w.wg, m->inter, H, w.i4g));
+            M_TRY(quantize_proj_i4(m, w.wu, m->inter, H, w.i4u));
+            M_TRY(quantize_proj_i4(m, w.wd, H, m->inter, w.i4d));
+        }
+        M_TRY(quantize_proj_i4(m, m->lm_head, m->vocab_l, H, m->i4lm));
+        B2_TRY(cudaStreamSynchronize(m->stream));
+    }
+    if (f8 != m->wfp8 || i4 != m->wint4) {
+        m->wfp8 = f8;
+        m->wint4 = i4;
         invalidate_graphs(m);  // the step's GEMVs change form
     }
     return B2_OK;
@@ -2003,9 +2054,11 @@ extern "C" double b2_model_step_bytes(const b2_model* m, int B, int ctx) {
     const double rows = L * ((double)m->qkv_rows + H + 2.0 * m->inter + H) + m->vocab_l;
     const double lin = L * ((double)m->qkv_rows * H + H * m->nq * D + 2.0 * m->inter * H + H * m->inter) +
                        (double)m->vocab_l * H;
-    // decode GEMVs on FP8 copies: 1 byte per weight and an fp32 scale per row
+    // decode GEMVs on FP8 copies: 1 byte per weight and an fp32 scale per row;
+    // on 4-bit copies: half a byte per weight and an fp32 scale per 128
     const bool f8 = m->wfp8 && (gemv_step(m, B) ? B <= kFp8MaxBatch : B <= 128);
-    double bytes = f8 ? lin + 4.0 * rows : 2.0 * lin;
+    const bool i4 = m->wint4 && gemv_step(m, B) && B <= kI4MaxBatch;
+    double bytes = f8 ? lin + 4.0 * rows : i4 ? 0.5 * lin + 4.0 * lin / kI4Group : 2.0 * lin;
     if (c.has_qkv_bias) bytes += 2.0 * L * m->qkv_rows;
     bytes += 2.0 * B * H;                               // embedding rows
     bytes += 2.0 * (2.0 * L + 1.0) * H;                 // norm weights
@@ -2054,7 +2107,10 @@ extern "C" double b2_model_kernel_bytes(const b2_model* m, int kind, int B, int 
     const double H = c.hidden_size, D = c.head_dim;
     // weight bytes of `rows` rows of width K: fp16, or FP8 codes + fp32 scales
     const bool f8 = m->wfp8 && (gemv_step(m, B) ? B <= kFp8MaxBatch : B <= 128);
-    auto wb = [&](double rows, double K) { return f8 ? rows * K + 4.0 * rows : 2.0 * rows * K; };
+    const bool i4 = m->wint4 && gemv_step(m, B) && B <= kI4MaxBatch;
+    auto wb = [&](double rows, double K) {
+        return f8 ? rows * K + 4.0 * rows : i4 ? 0.5 * rows * K + 4.0 * rows * K / kI4Group : 2.0 * rows * K;
+    };
     switch (kind) {
         case 0: return wb(m->qkv_rows, H) + 4.0 * B * H + 2.0 * H + 2.0 * B * m->qkv_rows;
         case 1: return 2.0 * B * m->nkv * D * 2.0 * ctx + 2.0 * 2.0 * B * m->nq * D;
