@@ -1,6 +1,9 @@
 """Tensor parallelism on 2 GPUs: the Megatron-sharded decode path (NCCL sum
 after o and down, vocabulary-sharded lm_head with a max-reduced argmax) must
-match the unsharded oracle.  Skipped where fewer than 2 GPUs are visible."""
+match the unsharded oracle -- fp16 weights at small, Llama-3-8B and 70B
+widths, and 4-bit weights at Llama-3-8B widths, each with both exchanges.
+Skipped where fewer than 2 GPUs are visible.  (tp_worker.py takes an
+optional B2_TP_CASES filter on the case names for a shorter run.)"""
 import json
 import os
 import socket
