@@ -668,6 +668,43 @@ def run_op(args):
                     "dtype": "bf16", "config": {"workload": "BASELINE causal flash prefill, batch 1",
                                                 "flop": "2*S^2*D*Hq (causal half of 4*S^2*D*Hq)"},
                     "cases": cases, "peak": peak_tf, "peak_source": "measured (MEASURED_PEAKS.json bf16_tflops)"})
+    elif args.op == "gemv":
+        # the decode GEMV's weight forms on the gate|up shape at batch 1:
+        # fp16, FP8 rows (b2_gemv_fp8), 4-bit groups of 128 (b2_gemv_int4),
+        # all quantised by the library from one seeded fp16 matrix
+        N, K = 28672, 4096
+        g = torch.Generator(device="cuda").manual_seed(7)
+        w = (torch.randn(N, K, generator=g, device="cuda") * 0.02).half()
+        x = torch.randn(1, K, generator=g, device="cuda").half()
+        y = torch.empty(1, N, dtype=torch.float16, device="cuda")
+        q8 = torch.empty(N, K, dtype=torch.uint8, device="cuda")
+        s8 = torch.empty(N, dtype=torch.float32, device="cuda")
+        q4 = torch.empty(N, K // 2, dtype=torch.uint8, device="cuda")
+        s4 = torch.empty(N, K // 128, dtype=torch.float32, device="cuda")
+        b2.call("b2_quantize_fp8_rows", w.data_ptr(), N, K, q8.data_ptr(), s8.data_ptr(), st)
+        b2.call("b2_quantize_int4_rows", w.data_ptr(), N, K, q4.data_ptr(), s4.data_ptr(), st)
+        forms = [
+            ("fp16", 2.0 * N * K, lambda: b2.call("b2_gemv", w.data_ptr(), x.data_ptr(), y.data_ptr(), N, K, st)),
+            ("fp8", 1.0 * N * K + 4.0 * N,
+             lambda: b2.call("b2_gemv_fp8", q8.data_ptr(), s8.data_ptr(), x.data_ptr(), y.data_ptr(), 1, N, K, 0, st)),
+            ("int4", 0.5 * N * K + 4.0 * N * K / 128,
+             lambda: b2.call("b2_gemv_int4", q4.data_ptr(), s4.data_ptr(), x.data_ptr(), y.data_ptr(), 1, N, K, 0,
+                             st)),
+        ]
+        cases = []
+        for name, nbytes, fn in forms:
+            for _ in range(warm):
+                fn()
+            ms = _events_time(fn, iters, flush)
+            gbs = nbytes / (ms * 1e-3) / 1e9
+            cases.append({"weights": name, "N": N, "K": K, "us": ms * 1e3, "bytes": nbytes, "GBs": gbs,
+                          "frac": gbs / peak_hbm})
+        assert b2.device_status() == 0
+        out.update({"metric": "decode GEMV achieved HBM GB/s by weight form (batch 1, N 28672, K 4096)",
+                    "value": max(c["GBs"] for c in cases), "unit": "GB/s", "higher_is_better": True,
+                    "dtype": "f16 activations", "config": {"workload": "Llama-3-8B gate|up GEMV shape, batch 1",
+                                                          "l2": "512 MB buffer written between timed calls"},
+                    "cases": cases, "peak": peak_hbm, "peak_source": hbm_src})
     elif args.op == "gemm":
         cases = []
         for (M, K, N) in [(512, 4096, 6144), (2048, 4096, 6144), (2048, 4096, 28672), (2048, 14336, 4096),
@@ -705,7 +742,7 @@ def main():
     ap.add_argument("--trace", action="store_true",
                     help="(the default) add a per-kernel device trace of five steps, taken after the timed region")
     ap.add_argument("--no-trace", action="store_true", help="leave the per-kernel trace out")
-    ap.add_argument("--op", default=None, choices=["attention", "flash_prefill", "gemm"],
+    ap.add_argument("--op", default=None, choices=["attention", "flash_prefill", "gemm", "gemv"],
                     help="kernel microbenchmark instead of the decode metric (1 GPU)")
     ap.add_argument("--seq", type=int, default=0,
                     help="--op flash_prefill: one sequence length; --op attention: one context (with --batch)")
