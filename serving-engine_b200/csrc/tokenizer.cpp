@@ -607,17 +607,26 @@ int tok_fail(int code, const std::string& msg) {
 }
 
 // Piece of normalised text -> token ids (HF BPE::tokenize with merge_all).
+struct BpeSym { int32_t id, prev, next; uint32_t len; };
+struct BpeCand { int32_t rank, pos, id; };
+
 void bpe_piece(const b2_tokenizer& t, const uint8_t* s, size_t n, std::vector<int32_t>& out) {
     if (n == 0) return;
-    if (t.ignore_merges || n == 1) {
+    if (n == 1) {  // a single byte is its byte token (or nothing)
+        if (t.byte_id[s[0]] >= 0) out.push_back(t.byte_id[s[0]]);
+        return;
+    }
+    if (t.ignore_merges) {
         auto it = t.vocab.find(std::string((const char*)s, n));
         if (it != t.vocab.end()) { out.push_back(it->second); return; }
     }
-    struct Sym { int32_t id, prev, next; uint32_t len; };
-    Sym local[64];
-    std::vector<Sym> heap_syms;
-    Sym* sy = local;
-    if (n > 64) { heap_syms.resize(n); sy = heap_syms.data(); }
+    // scratch reused across pieces on this thread (encode runs many short pieces)
+    thread_local std::vector<BpeSym> syms;
+    thread_local std::vector<BpeCand> q;
+    using Sym = BpeSym;
+    using Cand = BpeCand;
+    if (syms.size() < n) syms.resize(n);
+    Sym* sy = syms.data();
     int32_t m = 0;
     for (size_t i = 0; i < n; ++i) {
         int32_t id = t.byte_id[s[i]];
@@ -627,10 +636,8 @@ void bpe_piece(const b2_tokenizer& t, const uint8_t* s, size_t n, std::vector<in
     }
     if (m == 0) return;
     sy[m - 1].next = -1;
-    struct Cand { int32_t rank, pos, id; };
     auto worse = [](const Cand& a, const Cand& b) { return a.rank > b.rank || (a.rank == b.rank && a.pos > b.pos); };
-    std::vector<Cand> q;
-    q.reserve(2 * (size_t)m);
+    q.clear();
     auto push = [&](int32_t pos) {
         int32_t nx = sy[pos].next;
         if (nx < 0) return;
