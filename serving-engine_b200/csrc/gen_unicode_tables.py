@@ -11,6 +11,8 @@ point, rather than off Python's `unicodedata`:
 
   * \\p{L}, \\p{N}, \\s   -- a Split pre-tokenizer with the class as its
                            pattern, run over every code point;
+  * word characters      -- the code points beside which the library drops
+                           a match of a single_word added token (either side);
   * full canonical        -- NFD of each code point;
     decompositions
   * combining classes     -- the order NFD puts a mark in next to a mark of
@@ -26,7 +28,7 @@ import os
 import sys
 import unicodedata
 
-from tokenizers import Regex, normalizers, pre_tokenizers
+from tokenizers import AddedToken, Regex, Tokenizer, models, normalizers, pre_tokenizers
 
 HERE = os.path.dirname(os.path.abspath(__file__))
 SEP = "\x00"  # a starter with no decomposition that nothing composes with
@@ -58,6 +60,22 @@ def class_members(cls):
     return set(ALL) - outside
 
 
+def word_members():
+    """Code points next to which the library skips a single_word added token's
+    match (checked on both sides; they agree)."""
+    alphabet = sorted(pre_tokenizers.ByteLevel.alphabet())
+    tok = Tokenizer(models.BPE(vocab={ch: i for i, ch in enumerate(alphabet)}, merges=[]))
+    tok.pre_tokenizer = pre_tokenizers.ByteLevel(add_prefix_space=False, use_regex=False)
+    tok.add_tokens([AddedToken("qqzz", single_word=True, normalized=False, special=False)])
+    tid = tok.token_to_id("qqzz")
+    left = tok.encode_batch([chr(c) + "qqzz" for c in ALL], add_special_tokens=False)
+    right = tok.encode_batch(["qqzz" + chr(c) for c in ALL], add_special_tokens=False)
+    wl = {c for c, e in zip(ALL, left) if tid not in e.ids}
+    wr = {c for c, e in zip(ALL, right) if tid not in e.ids}
+    assert wl == wr
+    return wl
+
+
 def batch(norm, strings, chunk=100000):
     out = []
     for i in range(0, len(strings), chunk):
@@ -71,6 +89,7 @@ def batch(norm, strings, chunk=100000):
 def build_tables():
     """The text of unicode_tables.inc and a one-line summary."""
     letters, numbers, spaces = class_members(r"\p{L}"), class_members(r"\p{N}"), class_members(r"\s")
+    words = word_members()
     nfd, nfc = normalizers.NFD(), normalizers.NFC()
 
     # full canonical decompositions (Hangul syllables are algorithmic and left out)
@@ -158,6 +177,7 @@ def build_tables():
     emit_ranges("kLetterRanges", ranges(letters))
     emit_ranges("kNumberRanges", ranges(numbers))
     emit_ranges("kSpaceRanges", ranges(spaces))
+    emit_ranges("kWordRanges", ranges(words))
     out.append("static const CccRange kCccRanges[] = {\n")
     for a, b, v in ccc_ranges:
         out.append(f"    {{0x{a:X}, 0x{b:X}, {v}}},\n")
@@ -179,7 +199,7 @@ def build_tables():
         out.append(f"    {{0x{a:X}, 0x{b:X}, 0x{c:X}}},\n")
     out.append("};\n")
     summary = (f"{len(ranges(letters))} letter, {len(ranges(numbers))} number, "
-               f"{len(ranges(spaces))} space ranges; {len(ccc_ranges)} class ranges; "
+               f"{len(ranges(spaces))} space, {len(ranges(words))} word ranges; {len(ccc_ranges)} class ranges; "
                f"{len(entries)} decompositions; {len(compose)} composites")
     return "".join(out), summary
 

@@ -15,7 +15,7 @@
 //   added_tokens    split out of the text before normalisation (or after
 //                   it, for tokens marked normalized), longest match at the
 //                   leftmost position; special ones only when asked
-//                   (bpe.cpp:394-431), lstrip / rstrip honoured
+//                   (bpe.cpp:394-431), lstrip / rstrip / single_word honoured
 //   post_processor  TemplateProcessing (Llama-3's <|begin_of_text|>) applied
 //                   when the caller asks for special tokens
 //
@@ -534,8 +534,11 @@ std::string token_bytes(const std::string& tok, bool* mapped) {
 struct AddedToken {
     std::string content;
     int32_t id;
-    bool special, normalized, lstrip, rstrip;
+    bool special, normalized, lstrip, rstrip, single_word;
 };
+
+// Word characters for single_word added tokens (the library's own set).
+inline bool is_word_cp(uint32_t cp) { return cp < kRawByte && in_ranges(kWordRanges, cp); }
 
 // Trie over added-token contents for leftmost-longest matching.
 struct Trie {
@@ -692,8 +695,9 @@ inline bool is_ws_cp(uint32_t cp) { return char_class(cp) == C_SPACE; }
 // position); text between matches goes to `text(ptr, len)`, tokens to
 // `tok(index)`.  A match that `ok` refuses (a special token the caller wants
 // read as text) stays in the text and the scan resumes after it, as the HF
-// library's encode_special_tokens does.  lstrip / rstrip tokens take the
-// whitespace beside them.
+// library's encode_special_tokens does.  A single_word token's match stays
+// text too when a word character touches it on either side.  lstrip /
+// rstrip tokens take the whitespace beside them.
 template <class Ok, class Text, class Tok>
 void split_added(const b2_tokenizer& t, const Trie& trie, const uint8_t* s, size_t n, Ok ok, Text text, Tok tok) {
     if (trie.empty()) { text(s, n); return; }
@@ -705,6 +709,21 @@ void split_added(const b2_tokenizer& t, const Trie& trie, const uint8_t* s, size
         if (!ok(idx)) { i += len; continue; }
         size_t a = i, b = i + len;
         const AddedToken& at = t.added[idx];
+        if (at.single_word) {
+            bool word = false;
+            if (a > 0) {
+                size_t back = a - 1, l;
+                while (back > 0 && a - back < 4 && (s[back] & 0xC0) == 0x80) --back;
+                uint32_t cp = next_cp(s + back, n - back, &l);
+                if (back + l != a) cp = kRawByte + s[a - 1];   // a stray continuation byte
+                word = is_word_cp(cp);
+            }
+            if (!word && b < n) {
+                size_t l;
+                word = is_word_cp(next_cp(s + b, n - b, &l));
+            }
+            if (word) { i = b; continue; }
+        }
         if (at.lstrip) {
             while (a > seg) {
                 size_t back = a - 1;
@@ -890,14 +909,13 @@ int load_json(const char* text, size_t len, b2_tokenizer** out) {
             const JVal* id = a.get("id");
             if (!content || !id || id->t != JVal::NUM || content->empty())
                 return tok_fail(B2_ERR_INVALID, "tokenizer.json: bad added token");
-            if (a.is_true("single_word"))
-                return tok_fail(B2_ERR_UNSUPPORTED, "tokenizer.json: single_word added token " + *content);
             at.content = *content;
             at.id = (int32_t)id->num;
             at.special = a.is_true("special");
             at.normalized = a.is_true("normalized");
             at.lstrip = a.is_true("lstrip");
             at.rstrip = a.is_true("rstrip");
+            at.single_word = a.is_true("single_word");
             bool mapped;
             t->id_bytes[at.id] = token_bytes(at.content, &mapped);
             t->id_special[at.id] = at.special;

@@ -305,3 +305,31 @@ def test_reference_tokenizer_is_qwen2_only(golden, tmp_path):
         wrong = [c for (i, c), g in zip(cases, got) if g != want[i]]
         assert len(wrong) > len(cases) // 3, (kind, len(wrong))
         assert "1234" in wrong
+
+
+def test_single_word_added_tokens_live():
+    """single_word added tokens (a match is text when a word character --
+    the library's own set, csrc/unicode_tables.inc kWordRanges -- touches
+    it), special or not, with rstrip, against the library on seeded strings."""
+    tk = pytest.importorskip("tokenizers")
+    with open(_path("llama3"), encoding="utf-8") as f:
+        d = json.load(f)
+    nxt = max(max(d["model"]["vocab"].values()), max(t["id"] for t in d["added_tokens"])) + 1
+    for k, (content, special, rstrip) in enumerate([("qqzz", False, False), ("<sw>", True, False),
+                                                    ("zq|", False, True)]):
+        d["added_tokens"].append({"id": nxt + k, "content": content, "single_word": True, "lstrip": False,
+                                  "rstrip": rstrip, "normalized": False, "special": special})
+    text = json.dumps(d, ensure_ascii=False)
+    t = b2.Tokenizer(json_text=text)
+    hf = tk.Tokenizer.from_str(text)
+    rng = random.Random(17)
+    alpha = (["qqzz", "<sw>", "zq|", "q", "z", "<", ">", "|"] + list("ab_1 \t\n-.é中²ⅷ٣") + ["́", "ǅ", " "])
+    strs = ["".join(rng.choice(alpha) for _ in range(rng.randint(1, 10))) for _ in range(4000)]
+    strs += ["qqzz", "xqqzz", "qqzzx", "_qqzz", "qqzz_", "²qqzz", "éqqzz", "́qqzz", "a<sw>", " <sw> ",
+             "<sw><sw>", "zq|  x", "azq| x", "qqzzqqzz"]
+    want = [e.ids for e in hf.encode_batch(strs, add_special_tokens=False)]
+    for s, w in zip(strs, want):
+        assert t.encode(s) == w, s
+    hf.encode_special_tokens = True
+    for s, e in zip(strs, hf.encode_batch(strs, add_special_tokens=False)):
+        assert t.encode(s, split_special=False) == e.ids, s
