@@ -528,9 +528,10 @@ class Model:
         apps/generate.cpp:858-940, for any vocabulary the tokenizer reads):
         the prompt -- or the chat messages through the vocabulary's chat
         template -- is encoded (with the file's post-processor, e.g. Llama-3's
-        BOS, for a plain prompt), prefilled, and decoded greedily on the
-        device `chunk` steps at a time until a stop id of the tokenizer
-        appears or max_new_tokens are generated.  Returns (text, prompt_ids,
+        BOS, for a plain prompt), prefilled, and decoded on the device
+        `chunk` steps at a time (greedy, or the draw set_sampling configured)
+        until a stop id of the tokenizer appears or max_new_tokens are
+        generated.  Returns (text, prompt_ids,
         new_ids): new_ids end with the stop id when one was produced; text is
         their decode without special tokens.  Needs max_batch >= 1 and
         len(prompt_ids) + max_new_tokens <= max_seq."""
